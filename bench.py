@@ -1,0 +1,403 @@
+"""Benchmark of the NeuroDSL B200 hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one step): causal attention prefill at batch 8, 16 heads, head_dim
+64, sequence 2048, bf16 Q/K/V ~ N(0,1), fp32 accumulation — one call of the
+library's prefill kernel over all 128 (batch, head) pairs.  Metric: attention
+TFLOP/s with the algorithmic causal count 4·B·H·D·S(S+1)/2 per step.  The same
+JSON line carries the KV-cache decode workload (batch 64, 12 heads, head_dim
+64, cache 1024 -> 1152 over 128 appending steps) as tokens/s, each with its
+roofline against the measured B200 peaks.
+
+Multi-GPU: one process per GPU (torchrun); every rank runs its own full
+workload (independent batches, no collective on the data path) and the job
+value is the sum over ranks divided by the slowest rank's time (weak scaling).
+
+--impl reference times the reference's CPU path restated by the oracle
+(the Julia reference cannot run on this machine) on all host threads, on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, H, S, D = 8, 16, 2048, 64
+FLOPS_PER_STEP = 4 * B * H * D * S * (S + 1) // 2          # 68,753,031,168
+DEC_B, DEC_H, DEC_L0, DEC_T = 64, 12, 1024, 128
+METRIC = "Attn prefill TFLOP/s + KV-decode tokens/s (dim 1024), % of B200 roofline"
+N_SETS = 3  # rotating input sets: 3 x 134 MB > 126 MB L2
+
+
+def dec_bytes(L):
+    """Algorithmic HBM bytes of one decode step over L keys: K and V read,
+    q read, new K/V written, output written (bf16)."""
+    return 2 * DEC_B * DEC_H * L * D * 2 + DEC_B * DEC_H * D * 2 * 4
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"],
+                "bf16_tflops_sustained": j.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic(name):
+    """Per-launch DRAM bytes from a committed ncu summary (profiles/<name>.md,
+    line 'dram_bytes_per_launch = <int>'), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch"):
+            try:
+                return int(float(line.split("=")[1].strip().split()[0]))
+            except (IndexError, ValueError):
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self._t.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() in ("active", "1"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# --------------------------------------------------------------- CPU arm ---
+
+def cpu_prefill_sample(min_seconds=10.0, nthreads=0):
+    """Time the oracle's restatement of the reference CPU attention on a bounded
+    sample of (batch, head) pairs of the prefill workload; returns
+    (TFLOP/s with the algorithmic causal count, threads, sample description)."""
+    import numpy as np
+
+    import oracle
+    rng = np.random.default_rng(0)
+    nh = 8
+    Q = oracle.bf16_round(rng.standard_normal((1, nh, S, D), dtype=np.float32))
+    K = oracle.bf16_round(rng.standard_normal((1, nh, S, D), dtype=np.float32))
+    V = oracle.bf16_round(rng.standard_normal((1, nh, S, D), dtype=np.float32))
+    threads = nthreads or os.cpu_count() or 1
+    oracle.attn_bhsd(Q[:, :1], K[:, :1], V[:, :1], causal=True, nthreads=threads)  # warm
+    reps = 0
+    t0 = time.perf_counter()
+    while True:
+        oracle.attn_bhsd(Q, K, V, causal=True, nthreads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= 64:
+            break
+    flops = reps * nh * 4 * D * S * (S + 1) // 2
+    return flops / el / 1e12, threads, f"{reps}x{nh} heads of S={S}, D={D} (causal), {el:.1f}s"
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    vals = []
+    desc = ""
+    for i in range(args.warmup + args.steps):
+        v, threads, desc = cpu_prefill_sample(min_seconds=args.ref_seconds, nthreads=threads)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": FLOPS_PER_STEP / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), bf16-rounded)",
+        "config": {"workload": f"causal attention prefill B={B} H={H} S={S} D={D}",
+                   "path": "oracle restatement of flash_attn_fwd_cpu_simple! "
+                           "(src/flash_attention.jl:49-69); Julia reference not runnable here"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- GPU arm ---
+
+def run_ours(args):
+    import torch
+
+    from neurodsl_b200 import ops
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        pg = dist
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def max_over_ranks(x):
+        if pg is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    sets = []
+    for _ in range(N_SETS):
+        q = torch.randn(B, H, S, D, device=dev, generator=gen).bfloat16()
+        k = torch.randn(B, H, S, D, device=dev, generator=gen).bfloat16()
+        v = torch.randn(B, H, S, D, device=dev, generator=gen).bfloat16()
+        o = torch.empty(B, H, S, D, device=dev, dtype=torch.bfloat16)
+        lse = torch.empty(B, H, S, device=dev)
+        m = torch.empty(B, H, S, device=dev)
+        sets.append((q, k, v, o, lse, m))
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        q, k, v, o, lse, m = sets[i % N_SETS]
+        ops.flash_attn_fwd(q, k, v, causal=True, out=o, lse=lse, row_max=m)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    # soak so the clock record covers steady-state load around the timed region
+    t_end = time.time() + args.soak
+    i = 0
+    while time.time() < t_end:
+        step(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms_local)
+    value = world * FLOPS_PER_STEP / (ms * 1e-3) / 1e12
+    kernel_tflops = FLOPS_PER_STEP / (ms_local * 1e-3) / 1e12
+
+    # ---- decode workload (128 appending steps per "step" of the decode line)
+    L_max = DEC_L0 + DEC_T
+    kc = torch.randn(DEC_B, DEC_H, L_max, D, device=dev, generator=gen).bfloat16()
+    vc = torch.randn(DEC_B, DEC_H, L_max, D, device=dev, generator=gen).bfloat16()
+    qs = torch.randn(DEC_T, DEC_B, DEC_H, D, device=dev, generator=gen).bfloat16()
+    kns = torch.randn(DEC_T, DEC_B, DEC_H, D, device=dev, generator=gen).bfloat16()
+    vns = torch.randn(DEC_T, DEC_B, DEC_H, D, device=dev, generator=gen).bfloat16()
+    dout = torch.empty(DEC_B, DEC_H, D, device=dev, dtype=torch.bfloat16)
+    dlse = torch.empty(DEC_B, DEC_H, device=dev)
+
+    def decode_pass():
+        for t in range(1, DEC_T + 1):
+            ops.kv_decode_attn(qs[t - 1], kc, vc, DEC_L0 + t, k_new=kns[t - 1], v_new=vns[t - 1],
+                               out=dout, lse=dlse)
+
+    for _ in range(max(1, args.warmup)):
+        decode_pass()
+    torch.cuda.synchronize()
+    barrier()
+    d0 = torch.cuda.Event(enable_timing=True)
+    d1 = torch.cuda.Event(enable_timing=True)
+    dec_reps = max(1, args.decode_reps)
+    d0.record(stream)
+    for _ in range(dec_reps):
+        decode_pass()
+    d1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    dec_ms_local = d0.elapsed_time(d1) / dec_reps
+    dec_ms = max_over_ranks(dec_ms_local)
+    clocks = sampler.stop()
+    dec_bytes_total = sum(dec_bytes(DEC_L0 + t) for t in range(1, DEC_T + 1))
+    dec_tokens = world * DEC_B * DEC_T / (dec_ms * 1e-3)
+    dec_gbs = dec_bytes_total / (dec_ms_local * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers (pinned)
+    hq = torch.randn(B, H, S, D, generator=torch.Generator().manual_seed(7)).bfloat16().pin_memory()
+    hk = torch.randn(B, H, S, D, generator=torch.Generator().manual_seed(8)).bfloat16().pin_memory()
+    hv = torch.randn(B, H, S, D, generator=torch.Generator().manual_seed(9)).bfloat16().pin_memory()
+    ho = torch.empty(B, H, S, D, dtype=torch.bfloat16).pin_memory()
+    dq, dk, dv, do, dl, dm = sets[0]
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ops.flash_attn_fwd(dq, dk, dv, causal=True, out=do, lse=dl, row_max=dm)
+        ho.copy_(do, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    x0 = torch.cuda.Event(enable_timing=True)
+    x1 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 20))
+    x0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    x1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(x0.elapsed_time(x1) / e2e_steps)
+    e2e_value = world * FLOPS_PER_STEP / (e2e_ms * 1e-3) / 1e12
+    h2d = 3 * B * H * S * D * 2
+    d2h = B * H * S * D * 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, thr, desc = cpu_prefill_sample(min_seconds=args.cpu_seconds)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port", "sample": desc}
+
+    peaks = load_peaks()
+    traffic = load_traffic("flash_fwd_causal_b8_h16_s2048_d64")
+    dec_traffic = load_traffic("kv_decode_b64_h12_l1024_d64")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": f"causal attention prefill B={B} H={H} S={S} D={D} per GPU",
+                       "flops_per_step": FLOPS_PER_STEP,
+                       "l2": f"{N_SETS} rotating input sets of 134 MB (> 126 MB L2)",
+                       "parallelism": f"dp{world} over independent batches"},
+            "roofline": {"bound": "tensor", "achieved": kernel_tflops,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": kernel_tflops / peaks["bf16_tflops"],
+                         "traffic": traffic, "peak_source": peaks["source"] + " burst bf16"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "decode": {
+                "workload": f"KV decode B={DEC_B} H={DEC_H} D={D} cache {DEC_L0}->{DEC_L0 + DEC_T}, "
+                            f"{DEC_T} appending steps",
+                "value": dec_tokens, "unit": "tokens/s", "ms_per_pass": dec_ms,
+                "us_per_token_step": dec_ms * 1e3 / DEC_T,
+                "gpu_launches": dec_reps * DEC_T,
+                "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peaks["hbm_gbs"],
+                             "unit": "GB/s", "frac": dec_gbs / peaks["hbm_gbs"],
+                             "traffic": dec_traffic,
+                             "bytes_per_pass": dec_bytes_total},
+            },
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--soak", type=float, default=2.0, help="seconds of load before timing")
+    ap.add_argument("--decode-reps", type=int, default=5)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

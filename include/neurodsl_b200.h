@@ -1,0 +1,151 @@
+/*
+ * neurodsl_b200.h — C ABI of libneurodsl_b200.so, the B200 (sm_100a) kernels
+ * behind NeuroDSL's transformer-inference operators.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * handle passed as void* (cudaStream_t; NULL = legacy default stream), is
+ * asynchronous on that stream, and returns an int status (ND_OK = 0).  On a
+ * non-zero status nd_last_error_string() describes the failure (thread-local).
+ * Nothing here synchronises the device.
+ *
+ * Tensor layouts are C row-major.  Head-major attention tensors are
+ * [B][H][S][D] (a Julia array of size (D, S, H, B) has the same bytes).  A
+ * Julia column-major (rows, cols) Float32 matrix is converted to/from this
+ * layout by nd_convert_2d.
+ *
+ * Reference interfaces replaced (paths inside the NeuroDSL project):
+ *   nd_flash_attn_fwd   flash_attn_fwd!(::CUDADevice, out, Q, K, V, d_head; causal)
+ *                       src/flash_attention.jl:116-134, reached from the
+ *                       :flash_attn custom op _dispatch_flash_attn!
+ *                       src/flash_attention.jl:175-200 (register_op! :203-208)
+ *   nd_kv_decode_attn   no reference counterpart (KV-cache decode is absent);
+ *                       defined as flash_attn_fwd_cpu_simple!
+ *                       (src/flash_attention.jl:49-69) with one query row
+ *   nd_kv_append        no reference counterpart (cache append for decode)
+ *   nd_gemm_bias_act    :linear src/dispatch.jl:363-384, :fused_matmul_add
+ *                       :281-296, :matmul trans_b :213-243, residual :add
+ *                       :386-417, fused_linear_gelu notebook/compiler.ipynb
+ *                       cell 15 (rule name src/compiler_config.jl:154-158)
+ *   nd_layernorm        the :layernorm rule symbol src/compiler_config.jl:168-172
+ *                       (the reference ships only RMSNorm, rmsnorm_fwd!
+ *                       src/kernels.jl:48-64,104-131, used by :rmsnorm
+ *                       src/dispatch.jl:426-438)
+ *   nd_convert_2d       Backend.to_device / Array() copies, src/backend.jl:20-26
+ */
+#ifndef NEURODSL_B200_H
+#define NEURODSL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ----------------------------------------------------- */
+#define ND_OK 0
+#define ND_ERR_INVALID_ARG 1   /* null pointer where one is required, negative size */
+#define ND_ERR_SHAPE 2         /* inconsistent or unsupported shape */
+#define ND_ERR_ALIGNMENT 3     /* pointer not 16-byte aligned */
+#define ND_ERR_UNSUPPORTED 4   /* dtype / head_dim / flag not supported */
+#define ND_ERR_CUDA 5          /* CUDA runtime error (message has details) */
+#define ND_ERR_DEVICE 6        /* current device is not an sm_100 GPU */
+#define ND_ERR_WORKSPACE 7     /* workspace missing or too small */
+#define ND_ERR_TIMEOUT 8       /* a kernel's bounded wait expired (nd_device_error) */
+
+/* ---- element types ---------------------------------------------------- */
+#define ND_F32 0
+#define ND_BF16 1
+
+/* ---- GEMM epilogue activation ------------------------------------------ */
+#define ND_ACT_NONE 0
+#define ND_ACT_GELU_SIGMOID 1  /* z * sigmoid(1.702 z): the reference's fused_linear_gelu */
+#define ND_ACT_GELU_TANH 2     /* 0.5 z (1 + tanh(sqrt(2/pi) (z + 0.044715 z^3))) */
+#define ND_ACT_GELU_ERF 3      /* 0.5 z (1 + erf(z / sqrt(2))) */
+
+/* Library version (major*100 + minor). */
+int nd_version(void);
+
+/* Description of the last failure on the calling thread ("" if none). */
+const char *nd_last_error_string(void);
+
+/* 0 if `device` is an sm_100 GPU usable by this library, else ND_ERR_DEVICE. */
+int nd_device_check(int device);
+
+/* Read and clear the device-side error word (set when a kernel's bounded
+ * wait expired; 0 = none).  Synchronises the current device. */
+int nd_device_error(int *code);
+
+/*
+ * Attention prefill (flash attention forward).
+ *   Q [B][H][Sq][D], K/V [B][H][Sk][D] bf16, 16-byte aligned; D must be 64.
+ *   O [B][H][Sq][D] in o_dtype (ND_BF16 or ND_F32).
+ *   lse, row_max: [B][H][Sq] fp32 or NULL — the reference's aux_data
+ *   :flash_l (log-sum-exp) and :flash_m (row max of the scaled scores).
+ *   scale: multiplies Q·Kᵀ (the reference uses 1/sqrt(d_head)).
+ *   causal: key j is masked for query i when j > i; requires Sq == Sk.
+ */
+int nd_flash_attn_fwd(void *stream, const void *Q, const void *K, const void *V, void *O,
+                      int o_dtype, float *lse, float *row_max, int B, int H, int Sq, int Sk,
+                      int D, float scale, int causal);
+
+/*
+ * Scratch bytes needed by nd_kv_decode_attn for (B, H, L).  0 means the call
+ * needs none.  A caller-provided workspace must be zero-filled once before
+ * its first use; every call leaves it ready for the next.
+ */
+int nd_kv_decode_workspace_size(int B, int H, int L, int D, size_t *bytes);
+
+/*
+ * KV-cache single-token decode attention.
+ *   q [B][H][D] bf16; k_cache, v_cache [B][H][L_max][D] bf16; attends over
+ *   keys [0, L).  D must be 64.  If k_new and v_new (both [B][H][D] bf16) are
+ *   given, they are the token at position L-1: they are written into the
+ *   caches and used for that key (append fused into the attention pass).
+ *   out [B][H][D] in o_dtype; lse [B][H] fp32 or NULL.
+ *   workspace: nd_kv_decode_workspace_size bytes (zero-filled before first
+ *   use), or NULL to use a buffer owned by the library for this device.
+ */
+int nd_kv_decode_attn(void *stream, const void *q, const void *k_new, const void *v_new,
+                      void *k_cache, void *v_cache, void *out, int o_dtype, float *lse, int B,
+                      int H, int L, int L_max, int D, float scale, void *workspace,
+                      size_t workspace_bytes);
+
+/* Write one token's K/V rows ([B][H][D] bf16) at position `pos` of the caches. */
+int nd_kv_append(void *stream, const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+                 int B, int H, int pos, int L_max, int D);
+
+/*
+ * Fused linear layer: Y[M][N] = act(A[M][K] · W[N][K]ᵀ + bias[N]) + residual[M][N]
+ *   A, W bf16 (K % 8 == 0, 16-byte aligned); bias fp32 [N] or NULL;
+ *   residual [M][N] in residual_dtype or NULL; Y in y_dtype; act = ND_ACT_*.
+ *   W is laid out like a Linear weight (out_features, in_features), i.e. the
+ *   reference's :matmul with trans_b = true.
+ */
+int nd_gemm_bias_act(void *stream, const void *A, const void *W, const float *bias,
+                     const void *residual, int residual_dtype, void *Y, int y_dtype, int M, int N,
+                     int K, int act);
+
+/*
+ * LayerNorm over the last dimension of x [rows][d]:
+ *   y = (x - mean) / sqrt(var + eps) * gamma + beta
+ *   x in x_dtype, y in y_dtype; gamma, beta fp32 [d] or NULL (1 / 0);
+ *   mean, rstd fp32 [rows] or NULL.
+ */
+int nd_layernorm(void *stream, const void *x, int x_dtype, const float *gamma, const float *beta,
+                 void *y, int y_dtype, float *mean, float *rstd, int rows, int d, float eps);
+
+/*
+ * Layout/dtype conversion of a 2-D matrix between a host-language array and
+ * the row-major device layout used by this library.
+ *   src_col_major = 1: src is column-major (rows, cols) (a Julia Matrix);
+ *   dst is row-major [rows][cols].  src_col_major = 0: plain copy/convert.
+ */
+int nd_convert_2d(void *stream, const void *src, int src_dtype, int src_col_major, void *dst,
+                  int dst_dtype, int rows, int cols);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NEURODSL_B200_H */

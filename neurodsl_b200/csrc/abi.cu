@@ -1,0 +1,381 @@
+// abi.cu — extern "C" entry points of libneurodsl_b200.so.
+//
+// Validates every argument on the host before any launch (shape, alignment,
+// dtype, device), converts failures to ND_ERR_* status codes with a message
+// in nd_last_error_string(), and forwards to the kernel launchers.  The
+// reference reports failures with error("❌ ...") (e.g. src/dispatch.jl:8,583);
+// the host wrappers turn a non-zero status back into an exception.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/neurodsl_b200.h"
+#include "flash_fwd.h"
+#include "gemm.h"
+#include "kv_decode.h"
+#include "layernorm.h"
+
+namespace {
+// Device error word: one int per device (a __device__ variable exists once
+// per device that loads the library).
+__device__ int g_device_error = 0;
+}  // namespace
+
+namespace nd {
+int* device_error_word() {
+  static int* cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cached[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int*>(p);
+  }
+  return cached[dev];
+}
+}  // namespace nd
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = '\0';
+  return ND_OK;
+}
+
+int cuda_fail(cudaError_t e, const char* where, const char* extra = nullptr) {
+  return fail(ND_ERR_CUDA, "%s: %s%s%s", where, cudaGetErrorString(e), extra ? " — " : "",
+              extra ? extra : "");
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+constexpr int kMaxDevices = 64;
+int g_cc_major[kMaxDevices];  // 0 = unknown
+
+// Checks that the current device is sm_100; caches the answer per device.
+int check_current_device(int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(ND_ERR_DEVICE, "device index %d out of range", dev);
+  int major = __atomic_load_n(&g_cc_major[dev], __ATOMIC_ACQUIRE);
+  if (major == 0) {
+    int minor = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (major != 10 || minor != 0)
+      return fail(ND_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                  major, minor);
+    __atomic_store_n(&g_cc_major[dev], major, __ATOMIC_RELEASE);
+  }
+  if (dev_out) *dev_out = dev;
+  return ND_OK;
+}
+
+// Library-owned decode scratch, one buffer per device, grown on demand and
+// zero-filled when (re)allocated.  Growth synchronises the device, so a
+// caller that captures decode into a CUDA graph makes one uncaptured call of
+// the largest size first.
+struct OwnedWorkspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+OwnedWorkspace g_ws[kMaxDevices];
+std::mutex g_ws_mu;
+
+int owned_workspace(int dev, size_t need, void** out) {
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  OwnedWorkspace& w = g_ws[dev];
+  if (w.bytes < need) {
+    if (w.ptr) {
+      cudaError_t e = cudaFree(w.ptr);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFree (decode workspace)");
+      w.ptr = nullptr;
+      w.bytes = 0;
+    }
+    size_t sz = need < (1u << 20) ? (1u << 20) : need;
+    cudaError_t e = cudaMalloc(&w.ptr, sz);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (decode workspace)");
+    e = cudaMemset(w.ptr, 0, sz);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset (decode workspace)");
+    w.bytes = sz;
+  }
+  *out = w.ptr;
+  return ND_OK;
+}
+
+// ---- 2-D layout conversion kernel (32x32 tiles through shared memory) ------
+template <typename TS, typename TD>
+__device__ __forceinline__ TD cvt(TS v);
+template <> __device__ __forceinline__ float cvt<float, float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt<float, __nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ float cvt<__nv_bfloat16, float>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16, __nv_bfloat16>(__nv_bfloat16 v) { return v; }
+
+template <typename TS, typename TD, bool kColMajor>
+__global__ void convert_kernel(const TS* __restrict__ src, TD* __restrict__ dst, int rows,
+                               int cols) {
+  __shared__ TS tile[32][33];
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  if (kColMajor) {
+    // read coalesced along rows of the column-major source
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const int c = c0 + i, r = r0 + threadIdx.x;
+      if (r < rows && c < cols) tile[threadIdx.x][i] = src[static_cast<size_t>(c) * rows + r];
+    }
+  } else {
+    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+      const int r = r0 + i, c = c0 + threadIdx.x;
+      if (r < rows && c < cols) tile[i][threadIdx.x] = src[static_cast<size_t>(r) * cols + c];
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) dst[static_cast<size_t>(r) * cols + c] = cvt<TS, TD>(tile[i][threadIdx.x]);
+  }
+}
+
+template <typename TS, typename TD>
+cudaError_t launch_convert(cudaStream_t st, const void* src, void* dst, int rows, int cols,
+                           bool col_major) {
+  dim3 block(32, 8), grid((cols + 31) / 32, (rows + 31) / 32);
+  if (col_major)
+    convert_kernel<TS, TD, true><<<grid, block, 0, st>>>(static_cast<const TS*>(src), static_cast<TD*>(dst), rows, cols);
+  else
+    convert_kernel<TS, TD, false><<<grid, block, 0, st>>>(static_cast<const TS*>(src), static_cast<TD*>(dst), rows, cols);
+  return cudaGetLastError();
+}
+
+bool valid_dtype(int t) { return t == ND_F32 || t == ND_BF16; }
+
+}  // namespace
+
+extern "C" {
+
+__attribute__((visibility("default"))) int nd_version(void) { return 100; }
+
+__attribute__((visibility("default"))) const char* nd_last_error_string(void) { return g_err; }
+
+__attribute__((visibility("default"))) int nd_device_check(int device) {
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device != prev) {
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  }
+  int rc = check_current_device(nullptr);
+  if (device != prev) cudaSetDevice(prev);
+  return rc == ND_OK ? ok() : rc;
+}
+
+__attribute__((visibility("default"))) int nd_device_error(int* code) {
+  if (code == nullptr) return fail(ND_ERR_INVALID_ARG, "nd_device_error: code is NULL");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int zero = 0;
+  e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "device error word");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_flash_attn_fwd(void* stream, const void* Q,
+                                                             const void* K, const void* V, void* O,
+                                                             int o_dtype, float* lse,
+                                                             float* row_max, int B, int H, int Sq,
+                                                             int Sk, int D, float scale,
+                                                             int causal) {
+  if (B < 0 || H < 0 || Sq < 0 || Sk < 0)
+    return fail(ND_ERR_INVALID_ARG, "nd_flash_attn_fwd: negative size (B=%d H=%d Sq=%d Sk=%d)", B, H, Sq, Sk);
+  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "nd_flash_attn_fwd: head_dim %d not supported (64 only)", D);
+  if (!valid_dtype(o_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_flash_attn_fwd: bad o_dtype %d", o_dtype);
+  if (causal && Sq != Sk)
+    return fail(ND_ERR_SHAPE, "nd_flash_attn_fwd: causal attention needs Sq == Sk (got %d, %d)", Sq, Sk);
+  if (!causal && Sk == 0 && Sq > 0)
+    return fail(ND_ERR_SHAPE, "nd_flash_attn_fwd: no keys (Sk = 0) for %d queries", Sq);
+  if (static_cast<long long>(B) * H * ((Sq + 127) / 128) > 0x7fffffffLL)
+    return fail(ND_ERR_SHAPE, "nd_flash_attn_fwd: grid too large");
+  if (B == 0 || H == 0 || Sq == 0) return ok();
+  if (!Q || !K || !V || !O) return fail(ND_ERR_INVALID_ARG, "nd_flash_attn_fwd: null tensor pointer");
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
+    return fail(ND_ERR_ALIGNMENT, "nd_flash_attn_fwd: Q/K/V/O must be 16-byte aligned");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  const char* msg = nullptr;
+  cudaError_t e = nd::launch_flash_fwd(static_cast<cudaStream_t>(stream),
+                                       static_cast<const __nv_bfloat16*>(Q),
+                                       static_cast<const __nv_bfloat16*>(K),
+                                       static_cast<const __nv_bfloat16*>(V), O, o_dtype == ND_F32,
+                                       lse, row_max, B, H, Sq, Sk, scale, causal != 0, &msg);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_flash_attn_fwd", msg);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_kv_decode_workspace_size(int B, int H, int L, int D,
+                                                                       size_t* bytes) {
+  if (!bytes) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_workspace_size: bytes is NULL");
+  if (B < 0 || H < 0 || L < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_workspace_size: negative size");
+  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_workspace_size: head_dim %d not supported", D);
+  *bytes = nd::kv_decode_workspace_bytes(B, H, L);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_kv_decode_attn(
+    void* stream, const void* q, const void* k_new, const void* v_new, void* k_cache,
+    void* v_cache, void* out, int o_dtype, float* lse, int B, int H, int L, int L_max, int D,
+    float scale, void* workspace, size_t workspace_bytes) {
+  if (B < 0 || H < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn: negative size");
+  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn: head_dim %d not supported (64 only)", D);
+  if (L < 1 || L > L_max)
+    return fail(ND_ERR_SHAPE, "nd_kv_decode_attn: need 1 <= L <= L_max (L=%d, L_max=%d)", L, L_max);
+  if (!valid_dtype(o_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn: bad o_dtype %d", o_dtype);
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn: k_new and v_new must both be given or both NULL");
+  if (static_cast<long long>(B) * H > 65535)
+    return fail(ND_ERR_SHAPE, "nd_kv_decode_attn: B*H = %lld exceeds 65535", static_cast<long long>(B) * H);
+  if (B == 0 || H == 0) return ok();
+  if (!q || !k_cache || !v_cache || !out) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn: null tensor pointer");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) ||
+      (k_new && (!aligned16(k_new) || !aligned16(v_new))))
+    return fail(ND_ERR_ALIGNMENT, "nd_kv_decode_attn: tensors must be 16-byte aligned");
+  int dev = 0;
+  int rc = check_current_device(&dev);
+  if (rc) return rc;
+  const size_t need = nd::kv_decode_workspace_bytes(B, H, L);
+  void* ws = workspace;
+  if (need > 0) {
+    if (ws == nullptr) {
+      rc = owned_workspace(dev, need, &ws);
+      if (rc) return rc;
+    } else if (workspace_bytes < need) {
+      return fail(ND_ERR_WORKSPACE, "nd_kv_decode_attn: workspace %zu bytes < %zu needed", workspace_bytes, need);
+    } else if (!aligned16(ws)) {
+      return fail(ND_ERR_ALIGNMENT, "nd_kv_decode_attn: workspace must be 16-byte aligned");
+    }
+  }
+  cudaError_t e = nd::launch_kv_decode(
+      static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(q),
+      static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new),
+      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), out,
+      o_dtype == ND_F32, lse, B, H, L, L_max, scale, ws);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_kv_decode_attn");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_kv_append(void* stream, const void* k_new,
+                                                        const void* v_new, void* k_cache,
+                                                        void* v_cache, int B, int H, int pos,
+                                                        int L_max, int D) {
+  if (B < 0 || H < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_append: negative size");
+  if (D <= 0 || D % 8) return fail(ND_ERR_UNSUPPORTED, "nd_kv_append: head_dim %d must be a positive multiple of 8", D);
+  if (pos < 0 || pos >= L_max) return fail(ND_ERR_SHAPE, "nd_kv_append: pos %d outside [0, %d)", pos, L_max);
+  if (B == 0 || H == 0) return ok();
+  if (!k_new || !v_new || !k_cache || !v_cache) return fail(ND_ERR_INVALID_ARG, "nd_kv_append: null tensor pointer");
+  if (!aligned16(k_new) || !aligned16(v_new) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ND_ERR_ALIGNMENT, "nd_kv_append: tensors must be 16-byte aligned");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_kv_append(static_cast<cudaStream_t>(stream),
+                                       static_cast<const __nv_bfloat16*>(k_new),
+                                       static_cast<const __nv_bfloat16*>(v_new),
+                                       static_cast<__nv_bfloat16*>(k_cache),
+                                       static_cast<__nv_bfloat16*>(v_cache), B, H, pos, L_max, D);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_kv_append");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_gemm_bias_act(void* stream, const void* A,
+                                                            const void* W, const float* bias,
+                                                            const void* residual,
+                                                            int residual_dtype, void* Y,
+                                                            int y_dtype, int M, int N, int K,
+                                                            int act) {
+  if (M < 0 || N < 0 || K < 0) return fail(ND_ERR_INVALID_ARG, "nd_gemm_bias_act: negative size");
+  if (act < ND_ACT_NONE || act > ND_ACT_GELU_ERF) return fail(ND_ERR_UNSUPPORTED, "nd_gemm_bias_act: bad act %d", act);
+  if (!valid_dtype(y_dtype) || (residual && !valid_dtype(residual_dtype)))
+    return fail(ND_ERR_UNSUPPORTED, "nd_gemm_bias_act: bad dtype");
+  if (M == 0 || N == 0) return ok();
+  if (K == 0) return fail(ND_ERR_SHAPE, "nd_gemm_bias_act: K = 0");
+  if (K % 8) return fail(ND_ERR_SHAPE, "nd_gemm_bias_act: K = %d must be a multiple of 8", K);
+  if (!A || !W || !Y) return fail(ND_ERR_INVALID_ARG, "nd_gemm_bias_act: null tensor pointer");
+  if (!aligned16(A) || !aligned16(W) || !aligned16(Y))
+    return fail(ND_ERR_ALIGNMENT, "nd_gemm_bias_act: A/W/Y must be 16-byte aligned");
+  if ((M + 127) / 128 > 65535) return fail(ND_ERR_SHAPE, "nd_gemm_bias_act: M too large");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  const char* msg = nullptr;
+  cudaError_t e = nd::launch_gemm(static_cast<cudaStream_t>(stream),
+                                  static_cast<const __nv_bfloat16*>(A),
+                                  static_cast<const __nv_bfloat16*>(W), bias, residual,
+                                  residual_dtype == ND_F32, Y, y_dtype == ND_F32, M, N, K, act, &msg);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_gemm_bias_act", msg);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_layernorm(void* stream, const void* x, int x_dtype,
+                                                        const float* gamma, const float* beta,
+                                                        void* y, int y_dtype, float* mean,
+                                                        float* rstd, int rows, int d, float eps) {
+  if (rows < 0 || d < 0) return fail(ND_ERR_INVALID_ARG, "nd_layernorm: negative size");
+  if (!valid_dtype(x_dtype) || !valid_dtype(y_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_layernorm: bad dtype");
+  if (rows == 0) return ok();
+  if (d == 0) return fail(ND_ERR_SHAPE, "nd_layernorm: d = 0");
+  if (!x || !y) return fail(ND_ERR_INVALID_ARG, "nd_layernorm: null tensor pointer");
+  if (static_cast<size_t>(d) * sizeof(float) > 200 * 1024)
+    return fail(ND_ERR_SHAPE, "nd_layernorm: d = %d too large", d);
+  if (rows > 0x7fffffff / 8) return fail(ND_ERR_SHAPE, "nd_layernorm: too many rows");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  const bool vec_ok = (d % 8 == 0) && aligned16(x) && aligned16(y) &&
+                      (!gamma || aligned16(gamma)) && (!beta || aligned16(beta));
+  cudaError_t e = nd::launch_layernorm(static_cast<cudaStream_t>(stream), x, x_dtype == ND_BF16,
+                                       gamma, beta, y, y_dtype == ND_BF16, mean, rstd, rows, d, eps,
+                                       vec_ok);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_layernorm");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_convert_2d(void* stream, const void* src,
+                                                         int src_dtype, int src_col_major,
+                                                         void* dst, int dst_dtype, int rows,
+                                                         int cols) {
+  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_convert_2d: negative size");
+  if (!valid_dtype(src_dtype) || !valid_dtype(dst_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_convert_2d: bad dtype");
+  if (rows == 0 || cols == 0) return ok();
+  if (!src || !dst) return fail(ND_ERR_INVALID_ARG, "nd_convert_2d: null pointer");
+  if ((rows + 31) / 32 > 65535) return fail(ND_ERR_SHAPE, "nd_convert_2d: too many rows");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool cm = src_col_major != 0;
+  cudaError_t e;
+  if (src_dtype == ND_F32 && dst_dtype == ND_F32) e = launch_convert<float, float>(st, src, dst, rows, cols, cm);
+  else if (src_dtype == ND_F32) e = launch_convert<float, __nv_bfloat16>(st, src, dst, rows, cols, cm);
+  else if (dst_dtype == ND_F32) e = launch_convert<__nv_bfloat16, float>(st, src, dst, rows, cols, cm);
+  else e = launch_convert<__nv_bfloat16, __nv_bfloat16>(st, src, dst, rows, cols, cm);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_convert_2d");
+  return ok();
+}
+
+}  // extern "C"

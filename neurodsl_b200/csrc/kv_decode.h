@@ -1,0 +1,28 @@
+// kv_decode.h — launchers for the decode-attention and KV-append kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace nd {
+
+// Most (batch, head) pairs one decode call may cover (grid.y limit).
+constexpr int kDecodeMaxHeads = 65535;
+
+// Scratch bytes for one decode call: a fixed ticket region of kDecodeMaxHeads
+// words followed by the per-chunk partials.  The ticket region must be zero
+// before the first call; every call leaves it at zero.
+size_t kv_decode_workspace_bytes(int B, int H, int L);
+size_t kv_decode_partials_offset();
+
+cudaError_t launch_kv_decode(cudaStream_t stream, const __nv_bfloat16* q,
+                             const __nv_bfloat16* k_new, const __nv_bfloat16* v_new,
+                             __nv_bfloat16* k_cache, __nv_bfloat16* v_cache, void* out,
+                             bool out_f32, float* lse, int B, int H, int L, int L_max, float scale,
+                             void* workspace);
+
+cudaError_t launch_kv_append(cudaStream_t stream, const __nv_bfloat16* k_new,
+                             const __nv_bfloat16* v_new, __nv_bfloat16* k_cache,
+                             __nv_bfloat16* v_cache, int B, int H, int pos, int L_max, int D);
+
+}  // namespace nd

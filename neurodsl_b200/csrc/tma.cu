@@ -1,0 +1,58 @@
+// tma.cu — tensor-map encoding through cuTensorMapEncodeTiled.
+#include "tma.h"
+
+#include <mutex>
+
+namespace nd {
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_status = cudaSuccess;
+
+void load_encode() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  g_encode_status =
+      cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+  if (g_encode_status == cudaSuccess && q != cudaDriverEntryPointSuccess)
+    g_encode_status = cudaErrorSymbolNotFound;
+  if (g_encode_status == cudaSuccess) g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+}
+}  // namespace
+
+cudaError_t make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank,
+                                 const uint64_t* dims, const uint64_t* strides_bytes,
+                                 const uint32_t* box, const char** err_msg) {
+  std::call_once(g_encode_once, load_encode);
+  if (g_encode == nullptr) {
+    if (err_msg) *err_msg = "cuTensorMapEncodeTiled entry point unavailable";
+    return g_encode_status != cudaSuccess ? g_encode_status : cudaErrorSymbolNotFound;
+  }
+  cuuint64_t gdim[5];
+  cuuint64_t gstride[4];
+  cuuint32_t bdim[5];
+  cuuint32_t estride[5];
+  for (int i = 0; i < rank; ++i) {
+    gdim[i] = dims[i];
+    bdim[i] = box[i];
+    estride[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) gstride[i] = strides_bytes[i];
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
+                        const_cast<void*>(base), gdim, gstride, bdim, estride,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err_msg) *err_msg = "cuTensorMapEncodeTiled rejected the tensor geometry";
+    return cudaErrorInvalidValue;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace nd

@@ -1,0 +1,546 @@
+"""NeuroDSL's operator API (GraphRule / register_op! / demand!) over the B200 library.
+
+A Python mirror of the reference's graph executor for the hot path, so that a
+graph written against NeuroDSL's operator API runs on libneurodsl_b200.so with
+the same op symbols, attrs, output-buffer ownership and CtxStore contents:
+
+  reference (Julia)                         here
+  ---------------------------------------   ------------------------------------
+  NeuroGraph / GraphNode / GraphRule        NeuroGraph / GraphNode / GraphRule
+    src/types.jl:12-69
+  set!(g, sym, value; is_param)             set_(g, sym, value, is_param=...)
+    src/graph_api.jl:12-35
+  addrule!(g, rule)  src/graph_api.jl:152   addrule(g, rule)
+  topo_order!        src/graph_api.jl:163   topo_order(g)
+  demand!(g, sym; ctx_store)                demand(g, sym, ctx_store=...)
+    src/dispatch.jl:592-615
+  execute_rule!      src/dispatch.jl:106    execute_rule(g, rule, ...)
+  _infer_output_shape  src/dispatch.jl:36   _infer_output_shape(op, inputs, attrs)
+  _dispatch_op       src/dispatch.jl:212    _dispatch_op(dev, out, op, inputs, ...)
+  register_op! / CUSTOM_OPS  :587-588       register_op / CUSTOM_OPS
+  @defop  src/dsl_macros.jl:9-26            @defop-style: register_op(name, fn)
+
+Op symbols are strings ("flash_attn" for :flash_attn).  Node values are torch
+CUDA tensors on the graph's B200Device: float32 (the reference's Float32
+typing) or bfloat16 (device storage for tensor-core operands).  Every op
+writes in place into the output buffer that execute_rule allocated, as the
+reference's ops do, and stores the same CtxStore keys.  There is no CPU
+device and no fallback: an op whose kernel is missing raises.
+"""
+from __future__ import annotations
+
+import math
+import warnings
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Any, Callable, Dict, List, Optional
+
+import torch
+
+from . import ops
+from ._lib import NeuroDSLError
+
+CtxStore = dict  # src/types.jl:3
+
+
+class NeurAtom:
+    pass
+
+
+class Datom(NeurAtom):
+    pass
+
+
+class Quantom(NeurAtom):
+    pass
+
+
+@dataclass
+class B200Device:
+    """The device tag of a graph whose ops run on libneurodsl_b200.so
+    (the counterpart of Backend.CUDADevice, src/backend.jl:6-9)."""
+    index: int = 0
+
+    @property
+    def torch_device(self):
+        return torch.device("cuda", self.index)
+
+
+def zeros32(dev: B200Device, *shape):
+    """Backend.zeros32 (src/backend.jl:11-12) on the B200 device."""
+    return torch.zeros(*shape, dtype=torch.float32, device=dev.torch_device)
+
+
+def to_device(dev: B200Device, x):
+    """Backend.to_device (src/backend.jl:20-26)."""
+    if isinstance(x, torch.Tensor):
+        return x.to(dev.torch_device)
+    import numpy as np
+    if isinstance(x, np.ndarray):
+        return torch.from_numpy(np.ascontiguousarray(x)).to(dev.torch_device)
+    return x
+
+
+@dataclass
+class GraphNode:
+    """src/types.jl:12-31."""
+    name: str
+    value: Optional[torch.Tensor]
+    gradient: Optional[torch.Tensor] = None
+    valid: bool = True
+    backwarded: bool = False
+    atom_type: type = Quantom
+    is_param: bool = False
+    namespace: str = "default"
+    aux_data: Dict[str, Any] = field(default_factory=dict)
+    watchers: List[str] = field(default_factory=list)
+    on_change: Optional[Callable] = None
+
+
+@dataclass
+class GraphRule:
+    """GraphRule(output, inputs, op; attrs, namespace, atom_type), src/types.jl:37-46."""
+    output: str
+    inputs: List[str]
+    op: str
+    attrs: Dict[str, Any] = field(default_factory=dict)
+    namespace: str = "default"
+    atom_type: type = Quantom
+
+
+class NeuroGraph:
+    """src/types.jl:51-69 — nodes and rules per namespace, cached topo order."""
+
+    def __init__(self, namespace: str = "default", device: Optional[B200Device] = None):
+        self.nodes: Dict[str, Dict[str, GraphNode]] = {}
+        self.rules: Dict[str, Dict[str, GraphRule]] = {}
+        self.grad_registry: Dict[str, Callable] = {}
+        self._topo_cache: Dict[str, Optional[List[str]]] = {}
+        self.active_ns = namespace
+        self.device = device if device is not None else B200Device(0)
+        self._ensure_namespace(namespace)
+
+    def _ensure_namespace(self, ns):
+        self.nodes.setdefault(ns, {})
+        self.rules.setdefault(ns, {})
+        self._topo_cache.setdefault(ns, None)
+
+
+def _consumers(g, ns):
+    cons: Dict[str, List[str]] = {}
+    for out, r in g.rules[ns].items():
+        for s in r.inputs:
+            cons.setdefault(s, []).append(out)
+    return cons
+
+
+def _invalidate_downstream(g, sym, ns):
+    """BFS invalidation of every node computed from `sym` (src/graph_api.jl:37-71)."""
+    cons = _consumers(g, ns)
+    q = deque(cons.get(sym, []))
+    seen = set()
+    while q:
+        s = q.popleft()
+        if s in seen:
+            continue
+        seen.add(s)
+        nd = g.nodes[ns].get(s)
+        if nd is not None:
+            nd.valid = False
+            if nd.on_change is not None:
+                nd.on_change(s)
+        q.extend(cons.get(s, []))
+
+
+def set_(g: NeuroGraph, name: str, value, is_param: bool = False, namespace: Optional[str] = None,
+         atom_type=Quantom):
+    """set!(g, name, value; is_param, namespace) — src/graph_api.jl:12-35."""
+    ns = namespace or g.active_ns
+    g._ensure_namespace(ns)
+    v = to_device(g.device, value)
+    nd = g.nodes[ns].get(name)
+    if nd is None:
+        g.nodes[ns][name] = GraphNode(name, v, is_param=is_param, namespace=ns, atom_type=atom_type)
+        g._topo_cache[ns] = None
+    else:
+        nd.value = v
+        nd.valid = True
+        nd.is_param = nd.is_param or is_param
+    _invalidate_downstream(g, name, ns)
+    return g.nodes[ns][name]
+
+
+def addrule(g: NeuroGraph, rule: GraphRule):
+    """addrule!(g, rule) — src/graph_api.jl:152-160."""
+    ns = rule.namespace
+    g._ensure_namespace(ns)
+    g.rules[ns][rule.output] = rule
+    if rule.output not in g.nodes[ns]:
+        g.nodes[ns][rule.output] = GraphNode(rule.output, None, valid=False, namespace=ns,
+                                             atom_type=rule.atom_type)
+    else:
+        g.nodes[ns][rule.output].valid = False
+    g._topo_cache[ns] = None
+    return rule
+
+
+def topo_order(g: NeuroGraph, namespace: Optional[str] = None) -> List[str]:
+    """topo_order! — iterative DFS, cached per namespace (src/graph_api.jl:163-209)."""
+    ns = namespace or g.active_ns
+    cached = g._topo_cache.get(ns)
+    if cached is not None:
+        return cached
+    order: List[str] = []
+    state: Dict[str, int] = {}
+    for root in list(g.nodes[ns].keys()):
+        if state.get(root):
+            continue
+        stack = [(root, False)]
+        while stack:
+            s, done = stack.pop()
+            if done:
+                state[s] = 2
+                order.append(s)
+                continue
+            st = state.get(s, 0)
+            if st == 2:
+                continue
+            if st == 1:
+                raise NeuroDSLError(2, f"cycle detected at :{s}")
+            state[s] = 1
+            stack.append((s, True))
+            r = g.rules[ns].get(s)
+            if r is not None:
+                for inp in reversed(r.inputs):
+                    if state.get(inp, 0) == 0:
+                        stack.append((inp, False))
+                    elif state.get(inp) == 1:
+                        raise NeuroDSLError(2, f"cycle detected at :{inp}")
+    g._topo_cache[ns] = order
+    return order
+
+
+def _store_ctx(ctx_store, sym, d):
+    """_store_ctx! (src/dispatch.jl:29-33)."""
+    if ctx_store is not None:
+        ctx_store[sym] = d
+
+
+# ----------------------------------------------------------------- shapes ---
+
+def _infer_output_shape(op: str, inputs, attrs):
+    """_infer_output_shape (src/dispatch.jl:36-97) with entries for the new ops."""
+    if op in ("matmul", "fused_matmul_add", "fused_linear_gelu", "fused_matmul_relu"):
+        A, B = inputs[0], inputs[1]
+        tb = attrs.get("trans_b", False)
+        return (A.shape[0], B.shape[0] if tb else B.shape[1])
+    if op in ("linear", "fused_linear_residual", "fused_layernorm_linear"):
+        X, W = inputs[0], inputs[1]
+        return (X.shape[0], W.shape[0])
+    if op == "hcat_heads":
+        return (inputs[0].shape[0], sum(x.shape[1] for x in inputs))
+    if op == "slice_cols":
+        return (inputs[0].shape[0], attrs["end_col"] - attrs["start_col"] + 1)
+    if op in ("add", "identity", "flash_attn", "flash_attention", "layernorm", "gelu"):
+        return tuple(inputs[0].shape)
+    if op == "kv_decode_attn":
+        return tuple(inputs[0].shape)
+    # the reference warns and falls back to the first input's shape (:93-96)
+    warnings.warn(f"Shape inference non implémentée pour :{op}, utilisation de la forme du "
+                  "premier argument")
+    return tuple(inputs[0].shape)
+
+
+# ------------------------------------------------------------------- exec ---
+
+def execute_rule(g: NeuroGraph, rule: GraphRule, ctx_store=None, namespace=None):
+    """execute_rule! (src/dispatch.jl:106-152): gather inputs, (re)allocate the
+    output buffer when its shape changed, run the op in place, mark valid."""
+    dev = g.device
+    ns = rule.namespace
+    out_node = g.nodes[ns][rule.output]
+    inputs = []
+    for s in rule.inputs:
+        v = g.nodes[ns][s].value
+        if not isinstance(v, torch.Tensor):
+            raise NeuroDSLError(1, f":{s} has no value (input of :{rule.output})")
+        inputs.append(v)
+    shape = _infer_output_shape(rule.op, inputs, rule.attrs)
+    out_dtype = rule.attrs.get("out_dtype", torch.float32)
+    if (out_node.value is None or tuple(out_node.value.shape) != tuple(shape)
+            or out_node.value.dtype != out_dtype):
+        out_node.value = torch.zeros(shape, dtype=out_dtype, device=dev.torch_device)
+    _dispatch_op(dev, out_node.value, rule.op, inputs, rule.attrs, rule.output, out_node, ctx_store)
+    out_node.valid = True
+    return out_node.value
+
+
+def demand(g: NeuroGraph, name: str, ctx_store=None, namespace=None):
+    """demand!(g, name; ctx_store) — src/dispatch.jl:592-615."""
+    ns = namespace or g.active_ns
+    if ns not in g.nodes or name not in g.nodes[ns]:
+        raise NeuroDSLError(1, f":{name} introuvable dans :{ns}")
+    nd = g.nodes[ns][name]
+    if nd.valid and nd.value is not None:
+        return nd.value
+    for sym in topo_order(g, ns):
+        ndi = g.nodes[ns][sym]
+        if ndi.valid and ndi.value is not None:
+            continue
+        if sym not in g.rules[ns]:
+            continue
+        execute_rule(g, g.rules[ns][sym], ctx_store=ctx_store, namespace=ns)
+        if sym == name:
+            break
+    return g.nodes[ns][name].value
+
+
+CUSTOM_OPS: Dict[str, Callable] = {}
+
+
+def register_op(name: str, fn: Callable):
+    """register_op!(name, fn) — src/dispatch.jl:587-588."""
+    CUSTOM_OPS[name] = fn
+    return fn
+
+
+# ----------------------------------------------------------- op helpers ---
+
+def _bf16_rows(x):
+    """A 2-D operand as contiguous bf16 (converted on the device by the library)."""
+    if x.dtype == torch.bfloat16 and x.is_contiguous():
+        return x
+    rows, cols = x.shape
+    return ops.convert_2d(x.contiguous(), rows, cols, False, torch.bfloat16)
+
+
+def _weight_nk(W, trans_b):
+    """The weight as [N][K] bf16: trans_b=true weights already are; a (K, N)
+    row-major matrix is the column-major (N, K) one and is converted."""
+    if trans_b:
+        return _bf16_rows(W)
+    K, N = W.shape
+    return ops.convert_2d(W.contiguous(), N, K, True, torch.bfloat16)
+
+
+def _bias_vec(b):
+    if b is None:
+        return None
+    return b.reshape(-1).to(torch.float32).contiguous()
+
+
+def _gemm_into(out, X, Wnk, bias=None, residual=None, act="none"):
+    if out.dtype not in (torch.float32, torch.bfloat16) or not out.is_contiguous():
+        raise NeuroDSLError(4, "output buffer must be contiguous fp32 or bf16")
+    ops.linear(_bf16_rows(X), Wnk, _bias_vec(bias), residual=residual, act=act, out=out)
+
+
+def _alias_safe(out, out_node, inputs):
+    """Output buffer aliasing an input is redirected through aux_data[:_alias_buf]
+    (src/dispatch.jl:220-231, :366-376)."""
+    if any(out.data_ptr() == x.data_ptr() for x in inputs):
+        buf = out_node.aux_data.get("_alias_buf")
+        if buf is None or buf.shape != out.shape or buf.dtype != out.dtype:
+            buf = torch.empty_like(out)
+            out_node.aux_data["_alias_buf"] = buf
+        return buf, True
+    return out, False
+
+
+# ------------------------------------------------------------- dispatch ---
+
+def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, ctx_store):
+    """_dispatch_op (src/dispatch.jl:212-585) for the ops on the inference hot
+    path; custom ops (CUSTOM_OPS) are looked up after the built-ins, like the
+    reference's fall-through at :571-573."""
+    if op == "matmul":
+        A, B = inputs[0], inputs[1]
+        tb = attrs.get("trans_b", False)
+        kA = A.shape[1]
+        kB = B.shape[1] if tb else B.shape[0]
+        if kA != kB:
+            raise NeuroDSLError(2, f"[{out_sym}] matmul incompatible A={tuple(A.shape)} "
+                                   f"B={tuple(B.shape)} trans_b={tb}")
+        buf, aliased = _alias_safe(output_buffer, out_node, inputs)
+        _gemm_into(buf, A, _weight_nk(B, tb))
+        if aliased:
+            output_buffer.copy_(buf)
+        _store_ctx(ctx_store, out_sym, {"trans_b": tb, "A": A.clone() if ctx_store is not None else A,
+                                        "B": B})
+        return output_buffer
+    if op == "fused_matmul_add":
+        A, B, bias = inputs[0], inputs[1], inputs[2]
+        tb = attrs.get("trans_b", False)
+        _gemm_into(output_buffer, A, _weight_nk(B, tb), bias=bias)
+        _store_ctx(ctx_store, out_sym, {"trans_b": tb, "A": A, "B": B})
+        return output_buffer
+    if op == "linear":
+        X, W = inputs[0], inputs[1]
+        bias = inputs[2] if len(inputs) == 3 else None
+        buf, aliased = _alias_safe(output_buffer, out_node, inputs)
+        _gemm_into(buf, X, _bf16_rows(W), bias=bias)
+        if aliased:
+            output_buffer.copy_(buf)
+        _store_ctx(ctx_store, out_sym, {"X": X, "W": W, "n_inputs": len(inputs)})
+        return output_buffer
+    if op in CUSTOM_OPS:
+        CUSTOM_OPS[op](dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store)
+        return output_buffer
+    if op == "identity":
+        output_buffer.copy_(inputs[0])
+        return output_buffer
+    raise NeuroDSLError(4, f"Opérateur inconnu : :{op}. Utilisez register_op! pour enregistrer "
+                           "un op custom.")
+
+
+# ------------------------------------------------ B200 custom operators ---
+
+def _dispatch_flash_attn(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:flash_attn on one head, Q/K/V (N, D) — _dispatch_flash_attn!
+    (src/flash_attention.jl:175-200): aux_data[:flash_l] = log-sum-exp,
+    aux_data[:flash_m] = row max, ctx {Q,K,V,out,l,m,d_head,causal}."""
+    Q, K, V = inputs[0], inputs[1], inputs[2]
+    d_head = attrs.get("d_head", Q.shape[1])
+    causal = attrs.get("causal", True)
+    N, D = Q.shape
+    Nk = K.shape[0]
+    l_buf = out_node.aux_data.get("flash_l")
+    if l_buf is None or l_buf.numel() != N:
+        l_buf = torch.zeros(N, dtype=torch.float32, device=dev.torch_device)
+        m_buf = torch.full((N,), -math.inf, dtype=torch.float32, device=dev.torch_device)
+        out_node.aux_data["flash_l"] = l_buf
+        out_node.aux_data["flash_m"] = m_buf
+    m_buf = out_node.aux_data["flash_m"]
+    q4 = _bf16_rows(Q).view(1, 1, N, D)
+    k4 = _bf16_rows(K).view(1, 1, Nk, D)
+    v4 = _bf16_rows(V).view(1, 1, Nk, D)
+    ops.flash_attn_fwd(q4, k4, v4, causal=causal, scale=1.0 / math.sqrt(d_head),
+                       out=output_buffer.view(1, 1, N, D), lse=l_buf.view(1, 1, N),
+                       row_max=m_buf.view(1, 1, N))
+    _store_ctx(ctx_store, out_sym, {"Q": Q, "K": K, "V": V, "out": output_buffer, "l": l_buf,
+                                    "m": m_buf, "d_head": d_head, "causal": causal})
+    return output_buffer
+
+
+def _heads_major(x, S, H, D):
+    """(S, H·D) row-major -> [1][H][S][D] bf16 (the per-head :slice_cols of
+    src/flash_attention.jl:241-246 done as one device transpose)."""
+    return _bf16_rows(x).view(S, H, D).permute(1, 0, 2).contiguous().view(1, H, S, D)
+
+
+def _dispatch_flash_attention(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:flash_attention — all heads of q_full/k_full/v_full (S, H·D) in one
+    launch; replaces H × (3 :slice_cols + :flash_attn) and :hcat_heads
+    (src/flash_attention.jl:232-256)."""
+    q, k, v = inputs[0], inputs[1], inputs[2]
+    S, d = q.shape
+    H = attrs["n_heads"]
+    D = attrs.get("d_head", d // H)
+    causal = attrs.get("causal", True)
+    if H * D != d:
+        raise NeuroDSLError(2, f"n_heads {H} x d_head {D} != dim {d}")
+    Sk = k.shape[0]
+    q4 = _heads_major(q, S, H, D)
+    k4 = _heads_major(k, Sk, H, D)
+    v4 = _heads_major(v, Sk, H, D)
+    o4, lse, m = ops.flash_attn_fwd(q4, k4, v4, causal=causal, scale=1.0 / math.sqrt(D),
+                                    out_dtype=output_buffer.dtype)
+    output_buffer.copy_(o4.view(H, S, D).permute(1, 0, 2).reshape(S, d))
+    out_node.aux_data["flash_l"] = lse.view(H, S)
+    out_node.aux_data["flash_m"] = m.view(H, S)
+    _store_ctx(ctx_store, out_sym, {"Q": q, "K": k, "V": v, "out": output_buffer,
+                                    "l": out_node.aux_data["flash_l"],
+                                    "m": out_node.aux_data["flash_m"], "d_head": D,
+                                    "causal": causal, "n_heads": H})
+    return output_buffer
+
+
+def _dispatch_kv_decode_attn(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:kv_decode_attn — inputs [q (B, H·D), k_cache, v_cache ([B][H][L_max][D])]
+    (+ optional [k_new, v_new] (B, H·D) appended at cache_len-1), attrs
+    :n_heads, :d_head, :cache_len.  Output (B, H·D)."""
+    q, kc, vc = inputs[0], inputs[1], inputs[2]
+    B, d = q.shape
+    H = attrs["n_heads"]
+    D = attrs.get("d_head", d // H)
+    L = attrs["cache_len"]
+    kn = vn = None
+    if len(inputs) == 5:
+        kn = _bf16_rows(inputs[3]).view(B, H, D)
+        vn = _bf16_rows(inputs[4]).view(B, H, D)
+    out, lse = ops.kv_decode_attn(_bf16_rows(q).view(B, H, D), kc, vc, L, k_new=kn, v_new=vn,
+                                  scale=1.0 / math.sqrt(D), out_dtype=output_buffer.dtype,
+                                  out=output_buffer.view(B, H, D))
+    out_node.aux_data["decode_lse"] = lse
+    _store_ctx(ctx_store, out_sym, {"q": q, "cache_len": L, "l": lse, "n_heads": H, "d_head": D})
+    return output_buffer
+
+
+_GELU_APPROX = {"sigmoid": "sigmoid", "tanh": "tanh", "erf": "erf"}
+
+
+def _dispatch_fused_linear_gelu(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:fused_linear_gelu — inputs [A, W(, b)], attrs :trans_b, :approx.
+    The reference's notebook @defop (notebook/compiler.ipynb cell 15) is
+    z·σ(1.702 z) of A·B(ᵀ) with no bias; the default approx is that one."""
+    A, W = inputs[0], inputs[1]
+    b = inputs[2] if len(inputs) > 2 else None
+    tb = attrs.get("trans_b", False)
+    approx = _GELU_APPROX[str(attrs.get("approx", "sigmoid")).lstrip(":")]
+    _gemm_into(output_buffer, A, _weight_nk(W, tb), bias=b, act=approx)
+    _store_ctx(ctx_store, out_sym, {"trans_b": tb, "A": A, "B": W, "output": output_buffer})
+    return output_buffer
+
+
+def _dispatch_fused_linear_residual(dev, output_buffer, inputs, attrs, out_sym, out_node,
+                                    ctx_store):
+    """:fused_linear_residual — X·Wᵀ + b + R: the :linear rule followed by the
+    residual :add (src/dispatch.jl:363-417) in one GEMM epilogue."""
+    X, W, b, R = inputs[0], inputs[1], inputs[2], inputs[3]
+    res = R if R.is_contiguous() else R.contiguous()
+    _gemm_into(output_buffer, X, _bf16_rows(W), bias=b, residual=res)
+    _store_ctx(ctx_store, out_sym, {"X": X, "W": W, "n_inputs": 4})
+    return output_buffer
+
+
+def _dispatch_layernorm(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:layernorm — inputs [x, gamma(, beta)], attr :eps (default 1e-5).
+    aux_data[:ln_mean], [:ln_rstd] and ctx {x, gamma, beta, mean, rstd}
+    mirror :rmsnorm's aux_data[:rms_inv] (src/dispatch.jl:426-438)."""
+    x = inputs[0]
+    gamma = inputs[1] if len(inputs) > 1 else None
+    beta = inputs[2] if len(inputs) > 2 else None
+    eps = float(attrs.get("eps", 1e-5))
+    rows = x.shape[0]
+    mean = out_node.aux_data.get("ln_mean")
+    if mean is None or mean.numel() != rows:
+        mean = torch.zeros(rows, dtype=torch.float32, device=dev.torch_device)
+        out_node.aux_data["ln_mean"] = mean
+        out_node.aux_data["ln_rstd"] = torch.zeros_like(mean)
+    rstd = out_node.aux_data["ln_rstd"]
+    g = None if gamma is None else gamma.reshape(-1).float().contiguous()
+    bt = None if beta is None else beta.reshape(-1).float().contiguous()
+    ops.layernorm(x.contiguous(), g, bt, eps=eps, out=output_buffer, mean=mean, rstd=rstd)
+    _store_ctx(ctx_store, out_sym, {"x": x, "gamma": gamma, "beta": beta, "mean": mean,
+                                    "rstd": rstd})
+    return output_buffer
+
+
+def _dispatch_add(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:add residual (src/dispatch.jl:386-417) as a graph-glue device op."""
+    torch.add(inputs[0], inputs[1], out=output_buffer)
+    return output_buffer
+
+
+def register_b200_ops():
+    """Register the B200 operators (the @defop / register_op! plugin form)."""
+    register_op("flash_attn", _dispatch_flash_attn)
+    register_op("flash_attention", _dispatch_flash_attention)
+    register_op("kv_decode_attn", _dispatch_kv_decode_attn)
+    register_op("fused_linear_gelu", _dispatch_fused_linear_gelu)
+    register_op("fused_linear_residual", _dispatch_fused_linear_residual)
+    register_op("layernorm", _dispatch_layernorm)
+    register_op("add", _dispatch_add)
+
+
+register_b200_ops()

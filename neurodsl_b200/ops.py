@@ -1,0 +1,189 @@
+"""Torch-tensor front end of the C ABI: one function per hot-path kernel.
+
+Tensors are CUDA tensors (torch is used only to own device memory and to
+name the current stream); each call validates dtype/shape/contiguity here
+and then calls the corresponding nd_* entry point, which validates again.
+Outputs are allocated here when the caller passes none.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+
+from . import _lib
+from ._lib import check
+
+_DT = {torch.float32: _lib.ND_F32, torch.bfloat16: _lib.ND_BF16}
+ACT = {"none": _lib.ND_ACT_NONE, "sigmoid": _lib.ND_ACT_GELU_SIGMOID,
+       "tanh": _lib.ND_ACT_GELU_TANH, "erf": _lib.ND_ACT_GELU_ERF}
+
+
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _need(t, name, dtype=None, dims=None):
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if dims is not None and t.dim() != dims:
+        raise ValueError(f"{name} must have {dims} dims, got shape {tuple(t.shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def flash_attn_fwd(Q, K, V, causal=True, scale=None, out=None, out_dtype=torch.bfloat16,
+                   lse=None, row_max=None, stream=None):
+    """O = softmax(Q·Kᵀ·scale [causal]) · V for [B][H][S][64] bf16 tensors.
+
+    Mirrors flash_attn_fwd!(dev, out, Q, K, V, d_head; causal)
+    (src/flash_attention.jl:113-134); returns (O, lse, row_max) like the
+    reference's (out, l, m).
+    """
+    for n, t in (("Q", Q), ("K", K), ("V", V)):
+        _need(t, n, torch.bfloat16, 4)
+    B, H, Sq, D = Q.shape
+    Sk = K.shape[2]
+    if K.shape != (B, H, Sk, D) or V.shape != K.shape:
+        raise ValueError(f"shape mismatch Q{tuple(Q.shape)} K{tuple(K.shape)} V{tuple(V.shape)}")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, H, Sq, D), dtype=out_dtype, device=Q.device)
+    _need(out, "out", None, 4)
+    if lse is None:
+        lse = torch.empty((B, H, Sq), dtype=torch.float32, device=Q.device)
+    if row_max is None:
+        row_max = torch.empty((B, H, Sq), dtype=torch.float32, device=Q.device)
+    check(_lib.load().nd_flash_attn_fwd(_stream(stream), _ptr(Q), _ptr(K), _ptr(V), _ptr(out),
+                                        _DT[out.dtype], _ptr(lse), _ptr(row_max), B, H, Sq, Sk,
+                                        D, float(scale), int(bool(causal))))
+    return out, lse, row_max
+
+
+def kv_decode_workspace_size(B, H, L, D=64):
+    n = ctypes.c_size_t(0)
+    check(_lib.load().nd_kv_decode_workspace_size(B, H, L, D, ctypes.byref(n)))
+    return n.value
+
+
+def kv_decode_attn(q, k_cache, v_cache, L, k_new=None, v_new=None, scale=None, out=None,
+                   out_dtype=torch.bfloat16, lse=None, workspace=None, stream=None):
+    """Single-token decode over keys [0, L) of [B][H][L_max][64] bf16 caches.
+
+    With k_new/v_new the token at L-1 is appended to the caches in the same
+    pass.  Returns (out [B][H][64], lse [B][H]).
+    """
+    _need(q, "q", torch.bfloat16, 3)
+    _need(k_cache, "k_cache", torch.bfloat16, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, 4)
+    B, H, D = q.shape
+    L_max = k_cache.shape[2]
+    if k_cache.shape != (B, H, L_max, D) or v_cache.shape != k_cache.shape:
+        raise ValueError("cache shape mismatch")
+    if (k_new is None) != (v_new is None):
+        raise ValueError("k_new and v_new go together")
+    if k_new is not None:
+        _need(k_new, "k_new", torch.bfloat16, 3)
+        _need(v_new, "v_new", torch.bfloat16, 3)
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=out_dtype, device=q.device)
+    if lse is None:
+        lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(_lib.load().nd_kv_decode_attn(_stream(stream), _ptr(q), _ptr(k_new), _ptr(v_new),
+                                        _ptr(k_cache), _ptr(v_cache), _ptr(out), _DT[out.dtype],
+                                        _ptr(lse), B, H, int(L), L_max, D, float(scale),
+                                        _ptr(workspace), ws_bytes))
+    return out, lse
+
+
+def kv_append(k_new, v_new, k_cache, v_cache, pos, stream=None):
+    _need(k_new, "k_new", torch.bfloat16, 3)
+    _need(v_new, "v_new", torch.bfloat16, 3)
+    B, H, D = k_new.shape
+    L_max = k_cache.shape[2]
+    check(_lib.load().nd_kv_append(_stream(stream), _ptr(k_new), _ptr(v_new), _ptr(k_cache),
+                                   _ptr(v_cache), B, H, int(pos), L_max, D))
+
+
+def linear(A, W, bias=None, residual=None, act="none", out=None, out_dtype=torch.bfloat16,
+           stream=None):
+    """Y = act(A·Wᵀ + bias) + residual with A [M][K], W [N][K] bf16.
+
+    :linear (src/dispatch.jl:363-384) / fused_linear_gelu
+    (notebook/compiler.ipynb cell 15) with the GELU variant `act`.
+    """
+    _need(A, "A", torch.bfloat16, 2)
+    _need(W, "W", torch.bfloat16, 2)
+    M, K = A.shape
+    N = W.shape[0]
+    if W.shape[1] != K:
+        raise ValueError(f"A{tuple(A.shape)} and W{tuple(W.shape)} disagree on K")
+    if bias is not None:
+        _need(bias, "bias", torch.float32)
+        if bias.numel() != N:
+            raise ValueError("bias length != N")
+    rdt = _lib.ND_F32
+    if residual is not None:
+        _need(residual, "residual", None, 2)
+        if tuple(residual.shape) != (M, N):
+            raise ValueError("residual shape != (M, N)")
+        rdt = _DT[residual.dtype]
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=A.device)
+    _need(out, "out", None, 2)
+    check(_lib.load().nd_gemm_bias_act(_stream(stream), _ptr(A), _ptr(W), _ptr(bias),
+                                       _ptr(residual), rdt, _ptr(out), _DT[out.dtype], M, N, K,
+                                       ACT[act] if isinstance(act, str) else int(act)))
+    return out
+
+
+def layernorm(x, gamma=None, beta=None, eps=1e-5, out=None, out_dtype=None, mean=None,
+              rstd=None, stream=None):
+    """Row LayerNorm of x [rows][d]; returns (y, mean, rstd)."""
+    _need(x, "x", None, 2)
+    rows, d = x.shape
+    if out is None:
+        out = torch.empty((rows, d), dtype=out_dtype or x.dtype, device=x.device)
+    if mean is None:
+        mean = torch.empty(rows, dtype=torch.float32, device=x.device)
+    if rstd is None:
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    for n, t in (("gamma", gamma), ("beta", beta)):
+        if t is not None:
+            _need(t, n, torch.float32)
+    check(_lib.load().nd_layernorm(_stream(stream), _ptr(x), _DT[x.dtype], _ptr(gamma),
+                                   _ptr(beta), _ptr(out), _DT[out.dtype], _ptr(mean), _ptr(rstd),
+                                   rows, d, float(eps)))
+    return out, mean, rstd
+
+
+def convert_2d(src, rows, cols, src_col_major, dst_dtype, out=None, stream=None):
+    """Column-major (Julia) or row-major 2-D matrix -> row-major [rows][cols]."""
+    _need(src, "src")
+    if src.numel() != rows * cols:
+        raise ValueError("src size != rows*cols")
+    if out is None:
+        out = torch.empty((rows, cols), dtype=dst_dtype, device=src.device)
+    check(_lib.load().nd_convert_2d(_stream(stream), _ptr(src), _DT[src.dtype],
+                                    int(bool(src_col_major)), _ptr(out), _DT[out.dtype], rows,
+                                    cols))
+    return out
+
+
+def device_error():
+    """Read and clear the device error word (non-zero after a timed-out wait)."""
+    c = ctypes.c_int(0)
+    check(_lib.load().nd_device_error(ctypes.byref(c)))
+    return c.value

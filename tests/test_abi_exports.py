@@ -1,0 +1,79 @@
+"""CPU checks of the C ABI library: it loads without a GPU and exports every
+function that include/neurodsl_b200.h declares (no compute call is made)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "neurodsl_b200.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\**\s*(nd_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for required in ("nd_flash_attn_fwd", "nd_kv_decode_attn", "nd_gemm_bias_act",
+                     "nd_layernorm", "nd_last_error_string"):
+        assert required in names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    from neurodsl_b200 import _lib
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = set(re.findall(r"\bT (nd_\w+)", out))
+    assert set(declared_functions()) <= exported
+    # no stray exports beyond the header
+    assert exported <= set(declared_functions()), exported - set(declared_functions())
+
+
+def test_version_and_error_string_without_gpu():
+    from neurodsl_b200 import _lib
+    lib = _lib.load()
+    assert lib.nd_version() >= 100
+    assert isinstance(lib.nd_last_error_string(), bytes)
+
+
+def test_argument_validation_runs_before_any_device_work():
+    """Shape/dtype errors are reported on the host, even with no GPU present."""
+    from neurodsl_b200 import _lib
+    lib = _lib.load()
+    rc = lib.nd_flash_attn_fwd(None, None, None, None, None, 0, None, None, 1, 1, 16, 16, 32,
+                               0.125, 1)
+    assert rc == _lib.ND_ERR_UNSUPPORTED
+    assert b"head_dim" in lib.nd_last_error_string()
+    rc = lib.nd_flash_attn_fwd(None, None, None, None, None, 0, None, None, 1, 1, 16, 20, 64,
+                               0.125, 1)
+    assert rc == _lib.ND_ERR_SHAPE
+    rc = lib.nd_kv_decode_attn(None, None, None, None, None, None, None, 0, None, 1, 1, 9, 8, 64,
+                               0.125, None, 0)
+    assert rc == _lib.ND_ERR_SHAPE
+    rc = lib.nd_gemm_bias_act(None, None, None, None, None, 0, None, 0, 4, 8, 12, 0)
+    assert rc == _lib.ND_ERR_SHAPE
+    rc = lib.nd_layernorm(None, None, 0, None, None, None, 0, None, None, 4, 0, 1e-5)
+    assert rc == _lib.ND_ERR_SHAPE
+    n = ctypes.c_size_t(0)
+    assert lib.nd_kv_decode_workspace_size(64, 12, 1152, 64, ctypes.byref(n)) == 0
+    assert n.value > 64 * 12 * 9 * 256
+
+
+def test_missing_library_raises(tmp_path):
+    from neurodsl_b200 import _lib
+    with pytest.raises(ImportError):
+        old = _lib._lib
+        _lib._lib = None
+        try:
+            _lib.load(str(tmp_path / "nope.so"))
+        finally:
+            _lib._lib = old

@@ -1,0 +1,82 @@
+"""GPU parity of nd_gemm_bias_act (the :linear / fused_linear_gelu rules)
+against the oracle and a torch fp32 reference, through the C ABI."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import oracle  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+REL_L2 = 1e-2
+
+
+def _ops():
+    from neurodsl_b200 import ops
+    return ops
+
+
+def _t(a, dtype=torch.bfloat16):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda().to(dtype)
+
+
+def check(y, ref):
+    y = np.asarray(y, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = float(np.abs(y - ref).max())
+    rel = float(np.linalg.norm(y - ref) / max(np.linalg.norm(ref), 1e-30))
+    assert err <= MAX_ABS and rel <= REL_L2, (err, rel)
+
+
+def test_golden_fixture(golden):
+    g = golden("linear_gelu")
+    ops = _ops()
+    A, W, b = _t(g["A"]), _t(g["W"]), _t(g["bias"], torch.float32)
+    for act in ("sigmoid", "tanh", "erf"):
+        y = ops.linear(A, W, b, act=act, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        check(y.cpu().numpy(), g["Y_" + act])
+    y = ops.linear(A, W, b, residual=_t(g["residual"], torch.float32), out_dtype=torch.float32)
+    check(y.cpu().numpy(), g["Y_residual"])
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 4096, 1024), (128, 1024, 4096), (200, 300, 136),
+                                   (1, 64, 64), (513, 768, 768), (4096, 4096, 1024)])
+@pytest.mark.parametrize("act", ["none", "sigmoid"])
+def test_shapes_vs_torch(M, N, K, act):
+    ops = _ops()
+    gen = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.randn(M, K, device="cuda", generator=gen).bfloat16()
+    W = (0.02 * torch.randn(N, K, device="cuda", generator=gen)).bfloat16()
+    b = torch.randn(N, device="cuda", generator=gen) * 0.1
+    y = ops.linear(A, W, b, act=act, out_dtype=torch.float32)
+    z = A.float() @ W.float().T + b
+    if act == "sigmoid":
+        z = z * torch.sigmoid(1.702 * z)
+    torch.cuda.synchronize()
+    check(y.cpu().numpy(), z.cpu().numpy())
+
+
+def test_residual_bf16_and_bf16_out():
+    ops = _ops()
+    rng = np.random.default_rng(4)
+    M, N, K = 130, 256, 192
+    A = oracle.bf16_round(rng.standard_normal((M, K), dtype=np.float32))
+    W = oracle.bf16_round((0.05 * rng.standard_normal((N, K))).astype(np.float32))
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    R = oracle.bf16_round(rng.standard_normal((M, N), dtype=np.float32))
+    y = ops.linear(_t(A), _t(W), _t(b, torch.float32), residual=_t(R), act="tanh")
+    torch.cuda.synchronize()
+    ref = oracle.linear(A, W, b, residual=R, act="tanh")
+    check(y.float().cpu().numpy(), ref)
+
+
+def test_rejects_bad_arguments():
+    ops = _ops()
+    from neurodsl_b200._lib import NeuroDSLError
+    A = torch.zeros(4, 12, device="cuda", dtype=torch.bfloat16)  # K % 8 != 0
+    W = torch.zeros(8, 12, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(NeuroDSLError):
+        ops.linear(A, W)

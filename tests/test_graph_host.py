@@ -1,0 +1,123 @@
+"""CPU tests of the operator-API mirror (no GPU): topo order, invalidation,
+demand! semantics, register_op! fall-through, shape inference and error
+behaviour, modelled on the reference's test/test_graph_api.jl:4-36.  The
+executor is exercised with ops registered by the test on a host device tag,
+so no kernel is called."""
+import pytest
+import torch
+
+from neurodsl_b200 import graph as G
+from neurodsl_b200._lib import NeuroDSLError
+
+
+class HostDevice:
+    torch_device = torch.device("cpu")
+
+
+def host_graph():
+    return G.NeuroGraph(device=HostDevice())
+
+
+@pytest.fixture(autouse=True)
+def _restore_custom_ops():
+    saved = dict(G.CUSTOM_OPS)
+    yield
+    G.CUSTOM_OPS.clear()
+    G.CUSTOM_OPS.update(saved)
+
+
+def test_set_and_demand_with_custom_op():
+    calls = []
+
+    def double(dev, out, inputs, attrs, out_sym, nd, ctx):
+        calls.append(out_sym)
+        out.copy_(inputs[0] * attrs.get("factor", 2.0))
+        if ctx is not None:
+            ctx[out_sym] = {"x": inputs[0]}
+
+    G.register_op("twice", double)
+    g = host_graph()
+    G.set_(g, "x", torch.ones(2, 3))
+    G.addrule(g, G.GraphRule("y", ["x"], "twice", {"factor": 3.0}))
+    G.addrule(g, G.GraphRule("z", ["y"], "twice"))
+    ctx = G.CtxStore()
+    z = G.demand(g, "z", ctx_store=ctx)
+    assert torch.equal(z, torch.full((2, 3), 6.0))
+    assert calls == ["y", "z"] and set(ctx) == {"y", "z"}
+    # valid nodes are not recomputed
+    G.demand(g, "z")
+    assert calls == ["y", "z"]
+    # set! invalidates downstream only
+    G.set_(g, "x", torch.full((2, 3), 2.0))
+    assert not g.nodes["default"]["y"].valid and not g.nodes["default"]["z"].valid
+    assert torch.equal(G.demand(g, "z"), torch.full((2, 3), 12.0))
+    assert calls == ["y", "z", "y", "z"]
+
+
+def test_output_buffer_is_reused_in_place():
+    def fill(dev, out, inputs, attrs, out_sym, nd, ctx):
+        out.copy_(inputs[0] + 1)
+
+    G.register_op("inc", fill)
+    g = host_graph()
+    G.set_(g, "x", torch.zeros(4))
+    G.addrule(g, G.GraphRule("y", ["x"], "identity"))
+    G.addrule(g, G.GraphRule("w", ["x"], "inc"))
+    y1 = G.demand(g, "w")
+    ptr = y1.data_ptr()
+    G.set_(g, "x", torch.ones(4))
+    y2 = G.demand(g, "w")
+    assert y2.data_ptr() == ptr and torch.equal(y2, torch.full((4,), 2.0))
+
+
+def test_topo_order_and_namespaces():
+    g = host_graph()
+    G.set_(g, "a", torch.zeros(1))
+    G.addrule(g, G.GraphRule("b", ["a"], "identity"))
+    G.addrule(g, G.GraphRule("c", ["b", "a"], "add"))
+    order = G.topo_order(g)
+    assert order.index("a") < order.index("b") < order.index("c")
+    G.set_(g, "a", torch.zeros(1), namespace="other")
+    assert "b" not in g.nodes["other"]
+
+
+def test_cycle_detected():
+    g = host_graph()
+    G.addrule(g, G.GraphRule("p", ["q"], "identity"))
+    G.addrule(g, G.GraphRule("q", ["p"], "identity"))
+    with pytest.raises(NeuroDSLError):
+        G.topo_order(g)
+
+
+def test_unknown_op_raises_like_reference():
+    g = host_graph()
+    G.set_(g, "x", torch.zeros(2, 2))
+    G.addrule(g, G.GraphRule("y", ["x"], "gelu_unknown"))
+    with pytest.raises(NeuroDSLError, match="register_op"):
+        G.demand(g, "y")
+
+
+def test_missing_node_raises():
+    g = host_graph()
+    with pytest.raises(NeuroDSLError):
+        G.demand(g, "nope")
+
+
+def test_shape_inference_for_b200_ops():
+    X = torch.zeros(128, 1024)
+    W = torch.zeros(4096, 1024)
+    assert G._infer_output_shape("fused_linear_gelu", [X, W], {"trans_b": True}) == (128, 4096)
+    assert G._infer_output_shape("fused_linear_gelu", [X, W.T], {}) == (128, 4096)
+    assert G._infer_output_shape("linear", [X, W], {}) == (128, 4096)
+    assert G._infer_output_shape("fused_linear_residual", [X, W], {}) == (128, 4096)
+    assert G._infer_output_shape("flash_attention", [X, X, X], {"n_heads": 16}) == (128, 1024)
+    assert G._infer_output_shape("layernorm", [X], {}) == (128, 1024)
+    assert G._infer_output_shape("hcat_heads", [torch.zeros(5, 64)] * 3, {}) == (5, 192)
+    with pytest.warns(UserWarning):
+        assert G._infer_output_shape("no_such_op", [X], {}) == (128, 1024)
+
+
+def test_b200_ops_registered():
+    for op in ("flash_attn", "flash_attention", "kv_decode_attn", "fused_linear_gelu",
+               "fused_linear_residual", "layernorm"):
+        assert op in G.CUSTOM_OPS
