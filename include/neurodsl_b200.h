@@ -111,6 +111,33 @@ int nd_kv_decode_attn(void *stream, const void *q, const void *k_new, const void
                       int H, int L, int L_max, int D, float scale, void *workspace,
                       size_t workspace_bytes);
 
+/*
+ * Allocation-free KV-cache decode attention.  No counterpart in the
+ * reference: it exists for callers that may not allocate device memory while
+ * they run decode — a host runtime whose device memory all comes from its
+ * own pool (a foreign cudaMalloc would escape the pool's accounting and its
+ * limit), or a serving process that reserves its HBM at start-up and forbids
+ * allocation and the device-wide synchronisation of cudaMalloc/cudaFree on
+ * the token loop.  nd_kv_decode_attn either takes a caller workspace (which
+ * someone must allocate) or grows a library-owned one with cudaMalloc; this
+ * entry point does neither.
+ *
+ * Arguments and results are those of nd_kv_decode_attn without the
+ * workspace.  Its scratch is a fixed 8 MiB block inside the library image
+ * (held by every GPU that loads the library until the process exits);
+ * shapes whose scratch exceeds it (256 KiB of tickets plus
+ * B*H*ceil(L/128)*272 bytes of partials) are rejected with ND_ERR_WORKSPACE.
+ * The first call on a device does a one-time set-up on `stream` (resolves the
+ * block's device address, zero-fills its ticket words); make that first call
+ * before any stream capture.  Every call shares the block and leaves the
+ * tickets at zero for the next: calls that overlap on the GPU (concurrent
+ * streams, or several host threads) race on it and must be serialised by the
+ * caller.  It never calls cudaMalloc, cudaFree or an allocating routine.
+ */
+int nd_kv_decode_attn_noalloc(void *stream, const void *q, const void *k_new, const void *v_new,
+                              void *k_cache, void *v_cache, void *out, int o_dtype, float *lse,
+                              int B, int H, int L, int L_max, int D, float scale);
+
 /* Write one token's K/V rows ([B][H][D] bf16) at position `pos` of the caches. */
 int nd_kv_append(void *stream, const void *k_new, const void *v_new, void *k_cache, void *v_cache,
                  int B, int H, int pos, int L_max, int D);

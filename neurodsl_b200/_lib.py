@@ -45,6 +45,8 @@ SIGNATURES = {
     "nd_kv_decode_workspace_size": (_i, [_i, _i, _i, _i, ctypes.POINTER(_sz)]),
     "nd_kv_decode_attn": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _f,
                                _vp, _sz]),
+    "nd_kv_decode_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i,
+                                       _i, _i, _f]),
     "nd_kv_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
     "nd_layernorm": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _f]),

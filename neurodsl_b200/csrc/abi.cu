@@ -283,6 +283,57 @@ __attribute__((visibility("default"))) int nd_kv_decode_attn(
   return ok();
 }
 
+// Allocation-free variant of nd_kv_decode_attn for callers that may not call
+// cudaMalloc: its scratch is the library's fixed 8 MiB per-GPU block
+// (kv_decode_static_scratch), never a fresh allocation.  Same arguments and
+// results as nd_kv_decode_attn minus the workspace.
+__attribute__((visibility("default"))) int nd_kv_decode_attn_noalloc(
+    void* stream, const void* q, const void* k_new, const void* v_new, void* k_cache,
+    void* v_cache, void* out, int o_dtype, float* lse, int B, int H, int L, int L_max, int D,
+    float scale) {
+  if (B < 0 || H < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn_noalloc: negative size");
+  if (D != 64)
+    return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn_noalloc: head_dim %d not supported (64 only)", D);
+  if (L < 1 || L > L_max)
+    return fail(ND_ERR_SHAPE, "nd_kv_decode_attn_noalloc: need 1 <= L <= L_max (L=%d, L_max=%d)", L, L_max);
+  if (!valid_dtype(o_dtype))
+    return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn_noalloc: bad o_dtype %d", o_dtype);
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return fail(ND_ERR_INVALID_ARG,
+                "nd_kv_decode_attn_noalloc: k_new and v_new must both be given or both NULL");
+  if (static_cast<long long>(B) * H > 65535)
+    return fail(ND_ERR_SHAPE, "nd_kv_decode_attn_noalloc: B*H = %lld exceeds 65535",
+                static_cast<long long>(B) * H);
+  if (B == 0 || H == 0) return ok();
+  if (!q || !k_cache || !v_cache || !out)
+    return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn_noalloc: null tensor pointer");
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) ||
+      (k_new && (!aligned16(k_new) || !aligned16(v_new))))
+    return fail(ND_ERR_ALIGNMENT, "nd_kv_decode_attn_noalloc: tensors must be 16-byte aligned");
+  const size_t need = nd::kv_decode_workspace_bytes(B, H, L);
+  if (need > nd::kDecodeStaticScratchBytes)
+    return fail(ND_ERR_WORKSPACE,
+                "nd_kv_decode_attn_noalloc: B=%d H=%d L=%d needs %zu bytes of scratch, more than "
+                "the %zu-byte fixed block of the allocation-free entry point; use "
+                "nd_kv_decode_attn with a workspace",
+                B, H, L, need, nd::kDecodeStaticScratchBytes);
+  int dev = 0;
+  int rc = check_current_device(&dev);
+  if (rc) return rc;
+  void* ws = nullptr;
+  if (need > 0) {
+    cudaError_t e = nd::kv_decode_static_scratch(dev, static_cast<cudaStream_t>(stream), &ws);
+    if (e != cudaSuccess) return cuda_fail(e, "nd_kv_decode_attn_noalloc (scratch set-up)");
+  }
+  cudaError_t e = nd::launch_kv_decode(
+      static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(q),
+      static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new),
+      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), out,
+      o_dtype == ND_F32, lse, B, H, L, L_max, scale, ws);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_kv_decode_attn_noalloc");
+  return ok();
+}
+
 __attribute__((visibility("default"))) int nd_kv_append(void* stream, const void* k_new,
                                                         const void* v_new, void* k_cache,
                                                         void* v_cache, int B, int H, int pos,

@@ -16,6 +16,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "kv_decode.h"
 
 namespace nd {
@@ -250,6 +252,42 @@ size_t kv_decode_workspace_bytes(int B, int H, int L) {
 size_t kv_decode_partials_offset() {
   const size_t tick = static_cast<size_t>(kDecodeMaxHeads) * sizeof(unsigned int);
   return (tick + 255) & ~static_cast<size_t>(255);
+}
+
+// ---- scratch for the allocation-free decode entry point --------------------
+// A fixed block of device memory, part of the library image: every GPU that
+// loads the library holds these kDecodeStaticScratchBytes until the process
+// exits, and no call ever allocates.  It has the same layout as a
+// caller-provided workspace (ticket region, then per-chunk partials).  In host
+// code the name g_decode_static_scratch is only a host-side stand-in, not a
+// device address: kv_decode_static_scratch() obtains the real address of this
+// device's copy with cudaGetSymbolAddress, once per device.
+static __device__ __align__(256) unsigned char g_decode_static_scratch[kDecodeStaticScratchBytes];
+
+namespace {
+constexpr int kScratchMaxDevices = 64;
+void* g_static_scratch_addr[kScratchMaxDevices] = {};
+std::mutex g_static_scratch_mu;
+}  // namespace
+
+cudaError_t kv_decode_static_scratch(int device, cudaStream_t stream, void** ptr) {
+  if (device < 0 || device >= kScratchMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+  if (g_static_scratch_addr[device] == nullptr) {
+    // Set-up, once per device, with `device` current (the caller's current
+    // device): resolve this device's copy of the array and clear its ticket
+    // region, which must start at zero (every call then returns the tickets it
+    // used to zero).  The clear is ordered on the caller's stream before the
+    // first kernel that reads the tickets.
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_decode_static_scratch);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(p, 0, kv_decode_partials_offset(), stream);
+    if (e != cudaSuccess) return e;
+    g_static_scratch_addr[device] = p;
+  }
+  *ptr = g_static_scratch_addr[device];
+  return cudaSuccess;
 }
 
 cudaError_t launch_kv_decode(cudaStream_t stream, const __nv_bfloat16* q,

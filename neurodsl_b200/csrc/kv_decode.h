@@ -15,6 +15,15 @@ constexpr int kDecodeMaxHeads = 65535;
 size_t kv_decode_workspace_bytes(int B, int H, int L);
 size_t kv_decode_partials_offset();
 
+// Size of the library's fixed decode scratch used by the allocation-free
+// entry point: 8 MiB per GPU (256 KiB of tickets, the rest for partials).
+constexpr size_t kDecodeStaticScratchBytes = static_cast<size_t>(8) << 20;
+
+// Device address of that scratch on `device` (which must be current).  The
+// first call on a device does the set-up: it resolves the address and clears
+// the ticket region with cudaMemsetAsync on `stream`.  Allocates nothing.
+cudaError_t kv_decode_static_scratch(int device, cudaStream_t stream, void** ptr);
+
 cudaError_t launch_kv_decode(cudaStream_t stream, const __nv_bfloat16* q,
                              const __nv_bfloat16* k_new, const __nv_bfloat16* v_new,
                              __nv_bfloat16* k_cache, __nv_bfloat16* v_cache, void* out,
