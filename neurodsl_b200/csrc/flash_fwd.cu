@@ -6,17 +6,28 @@
 // (src/flash_attention.jl:49-69, :113-134) evaluated blockwise with an online
 // softmax (the reference's tiled form, :9-46), never materialising S.
 //
-// Per CTA: 256 query rows of one head as two 128-row tiles that share one
-// stream of K/V tiles (128 keys each).  Warp roles (320 threads):
-//   warps 0..3   softmax of query tile 0 (thread t owns row t = TMEM lane t)
+// Persistent CTAs (one per SM) loop over work items of 256 query rows of one
+// head, taken heaviest first in alternating-direction rounds.  An item is two
+// 128-row query tiles sharing one stream of K/V tiles (128 keys each); Q is
+// double-buffered and the K/V ring runs on across items, so the next item's
+// loads overlap the current item's tail.  Warp roles (kHalves = 1, 384
+// threads):
+//   warps 0..3   softmax of query tile 0 (thread = row = TMEM lane)
 //   warps 4..7   softmax of query tile 1
-//   warp 8       TMA producer: Q0/Q1 once, then K/V tiles (kStages-deep ring)
+//   warp 8       TMA producer: Q0/Q1 per item, then K/V tiles (kStages ring)
 //   warp 9       TMEM allocator + single-thread UMMA issuer
-// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,320), O1 [320,384).
-// Softmax i reads S_i, writes P_i as packed bf16 over S_i's first 64
-// columns, and O_i += P_i·V_j reads P_i straight from tensor memory (A
-// operand in TMEM, V as an MN-major shared-memory operand).  While one
-// tile's softmax runs, the tensor core works on the other tile.
+//   warps 10, 11 idle (they complete the control warpgroup)
+// With kHalves = 2 every score row is split over two warpgroups that combine
+// their row maxima through shared memory (more warps to hide latency); on
+// B200 that loses to one warpgroup per tile because the exponential unit,
+// not latency, bounds the softmax, so kHalves = 1 is the configuration built.
+// TMEM (512 columns), per tile i at base 256·i: S_i [0,128) fp32 scores,
+// P_i [128,192) packed bf16 probabilities, O_i [192,256) fp32 accumulator.
+// Because P has its own columns, S_i(j+1) = Q_i·K_{j+1}ᵀ is issued as soon as
+// softmax i has read S_i(j) (barrier s_free), so the tensor core computes the
+// next scores while the softmax computes exponentials.  O_i += P_i·V_j reads
+// P_i straight from tensor memory (A operand in TMEM, V an MN-major
+// shared-memory operand).
 // The running max is raised only when a row's max grows by more than 8
 // (log2 units); O and l share the stale offset, so the final O/l is exact.
 #include <cuda.h>
@@ -36,42 +47,189 @@ constexpr int kRowsPerCta = kBM * kTiles;
 constexpr int kBN = 128;               // keys per K/V tile
 constexpr int kD = 64;
 constexpr int kStages = 3;
-constexpr int kSoftmaxThreads = 128 * kTiles;
-constexpr int kThreads = kSoftmaxThreads + 64;   // + producer warp + MMA warp
+constexpr int kHalves = 1;             // warpgroups sharing one score row (1 or 2)
+constexpr int kHalfCols = kBN / kHalves;   // score columns per softmax thread
+constexpr int kOutCols = kD / kHalves;     // output columns per softmax thread
+constexpr int kSoftmaxThreads = 128 * kTiles * kHalves;
+constexpr int kThreadsPerTile = 128 * kHalves;   // arrivals per softmax barrier
+constexpr int kThreads = kSoftmaxThreads + 128;  // + one control warpgroup
 constexpr int kWarpProducer = kSoftmaxThreads / 32;
 constexpr int kWarpMma = kWarpProducer + 1;
+// Register split.  One half (384 threads): launch gives 168 per thread
+// (64512 total), control 72 + softmax 216: 128 x 72 + 256 x 216 = 64512.
+// Two halves (640 threads): 96 per thread (61440), 128 x 32 + 512 x 112.
+constexpr uint32_t kLaunchRegs = (65536 / kThreads) & ~7u;
+constexpr uint32_t kRegsControl = kHalves == 1 ? 72 : 32;
+constexpr uint32_t kRegsSoftmax = kHalves == 1 ? 216 : 112;
+static_assert(128 * kRegsControl + kSoftmaxThreads * kRegsSoftmax <= kThreads * kLaunchRegs,
+              "register split exceeds the launch budget");
 constexpr uint32_t kTileBytes = kBM * kD * 2;    // 16 KB (one Q, K or V tile)
 constexpr uint32_t kTmemCols = 512;
-// TMEM columns: S_i at i*128, O_i at 256 + i*64
-__host__ __device__ constexpr uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 128u; }
-__host__ __device__ constexpr uint32_t col_o(int i) { return 256u + static_cast<uint32_t>(i) * 64u; }
+// TMEM columns of tile i
+__host__ __device__ constexpr uint32_t col_s(int i) { return static_cast<uint32_t>(i) * 256u; }
+__host__ __device__ constexpr uint32_t col_p(int i) { return col_s(i) + 128u; }
+__host__ __device__ constexpr uint32_t col_o(int i) { return col_s(i) + 192u; }
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;
 
 // shared-memory map (offsets from a 1024-aligned base)
-constexpr uint32_t kOffQ = 0;                                   // 2 x 16 KB
-constexpr uint32_t kOffK = kOffQ + kTiles * kTileBytes;
+constexpr uint32_t kOffQ = 0;                                   // 2 buffers x 2 x 16 KB
+constexpr uint32_t kOffK = kOffQ + 2 * kTiles * kTileBytes;
 constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
 constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;           // + alignment slack
+constexpr uint32_t kOffX = kOffBar + 256;                       // row-max / row-sum exchange
+constexpr uint32_t kSmemBytes = kOffX + 8192 + 1024;            // + alignment slack
+
+// Partner exchange between the two column halves of a score row: partial
+// maxima (double-buffered by iteration parity) and the final row sums.
+struct Exchange {
+  float max_part[2][kTiles][kHalves][kBM];
+  float sum_part[kTiles][kHalves][kBM];
+};
+static_assert(sizeof(Exchange) <= 8192, "exchange area");
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, false, false);
 constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, false, true);
 
 struct Bars {
-  uint64_t q_full;
+  uint64_t q_full[2];        // Q tiles of item n land in buffer n & 1
+  uint64_t q_empty[2];       // every S of that item has read the buffer
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[kTiles];
-  uint64_t p_full[kTiles];
-  uint64_t o_done[kTiles];
+  uint64_t s_full[kTiles];   // S_i(j) written (UMMA commit)
+  uint64_t s_free[kTiles];   // S_i(j) read into registers (256 softmax threads)
+  uint64_t p_full[kTiles];   // P_i(j) written and O_i rescaled (256 softmax threads)
+  uint64_t o_done[kTiles];   // O_i += P_i(j)·V_j complete (UMMA commit)
   uint64_t drained;
   uint32_t tmem_base;
   int abort_flag;
 };
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+// ---- packed fp32 helpers (two lanes per instruction) -----------------------
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// bf16x2 pack of two non-negative finite floats on the integer pipe: round to
+// nearest (halfway cases up) by adding half an output ulp to the fp32 bits,
+// then keep the high halves.  The conversion instruction would run on the
+// same pipe as the exponentials; these three integer ops do not.
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  return __byte_perm(a, b, 0x7632);
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// ---- exp2 on the FMA pipe ----------------------------------------------------
+// 2^x for x in [-126, 8] by Cody-Waite range reduction and a polynomial:
+// x = n + f with n = round(x) (the 1.5·2^23 magic-add rounding, exact for
+// |x| < 2^22) and f in [-0.5, 0.5]; 2^f from a degree-3 minimax polynomial
+// (coefficients computed for this kernel with the Remez exchange algorithm,
+// minimising relative error on [-0.5, 0.5]: max 7.5e-5, far below the 2^-9
+// rounding of the bf16 probabilities); 2^n is added into the exponent field.
+constexpr float kExpC0 = 0.99992806f;
+constexpr float kExpC1 = 0.69326097f;
+constexpr float kExpC2 = 0.24261113f;
+constexpr float kExpC3 = 0.05517167f;
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+// Pairs out of every 8 whose exponentials use the polynomial.  Measured on
+// B200 at head_dim 64 the softmax is bound by instruction issue and latency,
+// not by the exponential unit (which sustains 16/clk/SM), so moving work to
+// the FMA pipe only adds instructions: 0 is the fastest setting.
+constexpr int kPolyPairsPer8 = 0;
+
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// Probabilities for 2·kHalfCols/2 scores: p = 2^(s·scale - m) packed to bf16
+// in pk, row-sum partials accumulated in acc (four f32x2 chains).
+template <int kPoly>
+__device__ __forceinline__ void exp2_pairs(const float* sv, uint64_t scale2, uint64_t negm2,
+                                           uint32_t* pk, uint64_t* acc) {
+  const uint64_t magic2 = f2_pack(kRoundMagic, kRoundMagic);
+  const uint64_t c0 = f2_pack(kExpC0, kExpC0), c1 = f2_pack(kExpC1, kExpC1);
+  const uint64_t c2 = f2_pack(kExpC2, kExpC2), c3 = f2_pack(kExpC3, kExpC3);
+#pragma unroll
+  for (int c = 0; c < kHalfCols; c += 2) {
+    const int q = c >> 1;
+    float x0, x1, p0, p1;
+    f2_unpack(f2_fma(f2_pack(sv[c], sv[c + 1]), scale2, negm2), x0, x1);
+    if ((q & 7) < kPoly) {
+      const uint64_t x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+      const uint64_t t2 = f2_add(x2, magic2);         // magic + round(x)
+      const uint64_t f2 = f2_add(x2, f2_sub(magic2, t2));  // x - round(x)
+      uint64_t pp = f2_fma(f2, c3, c2);
+      pp = f2_fma(pp, f2, c1);
+      pp = f2_fma(pp, f2, c0);
+      float t0, t1;
+      f2_unpack(t2, t0, t1);
+      f2_unpack(pp, p0, p1);
+      // low bits of t hold round(x); shifting by 23 drops the magic's bits
+      p0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+      p1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+    } else {
+      p0 = fast_exp2(x0);
+      p1 = fast_exp2(x1);
+    }
+    acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
+    pk[q] = pack_bf16x2_int(p0, p1);
+  }
+}
+
+// One unit of work: 256 query rows (two tiles) of one (batch, head).
+struct WorkItem {
+  int blk;        // which 256-row block of the sequence
+  int bh;         // batch * H + head
+  int n_kv[kTiles];
+  int n_total;    // K/V tiles streamed for the item (the last tile needs the most)
+};
+
+template <bool kCausal>
+__device__ __forceinline__ WorkItem decode_item(int k, int BH, int n_blk, int n_k) {
+  WorkItem w;
+  // Heavy items first: with a causal mask the last query rows see the most keys.
+  w.blk = kCausal ? (n_blk - 1 - k / BH) : k / BH;
+  w.bh = k % BH;
+#pragma unroll
+  for (int i = 0; i < kTiles; ++i) {
+    const int qt = w.blk * kTiles + i;
+    w.n_kv[i] = kCausal ? min(qt + 1, n_k) : n_k;
+  }
+  w.n_total = w.n_kv[kTiles - 1];
+  return w;
+}
+
+// The n-th item of CTA `cta` out of `grid` persistent CTAs: items are visited
+// in rounds of `grid`, alternating direction so each CTA's heavy and light
+// items pair up (the cost list is sorted heaviest first).
+__device__ __forceinline__ int item_of(int n, int cta, int grid) {
+  return n * grid + ((n & 1) ? (grid - 1 - cta) : cta);
+}
 
 template <bool kCausal, bool kOutF32>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -88,31 +246,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // Heavy blocks first: with a causal mask the last query rows see the most keys.
   const int n_blk = ceil_div(Sq, kRowsPerCta);
-  const int blk = kCausal ? (n_blk - 1 - static_cast<int>(blockIdx.x) / BH)
-                          : static_cast<int>(blockIdx.x) / BH;
-  const int bh = static_cast<int>(blockIdx.x) % BH;
   const int n_k = ceil_div(Sk, kBN);
-  // K/V tiles needed by query tile i (its index among 128-row tiles is 2*blk+i)
-  int n_kv[kTiles];
-#pragma unroll
-  for (int i = 0; i < kTiles; ++i) {
-    const int qt = blk * kTiles + i;
-    n_kv[i] = kCausal ? min(qt + 1, n_k) : n_k;
-  }
-  const int n_total = n_kv[kTiles - 1];  // the last tile needs the most
+  const int n_items = n_blk * BH;
+  const int cta = static_cast<int>(blockIdx.x);
+  const int grid = static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(&bars->q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->q_full[b], 1);
+      mbar_init(&bars->q_empty[b], 1);
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->kv_full[s], 1);
       mbar_init(&bars->kv_empty[s], 1);
     }
     for (int i = 0; i < kTiles; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->p_full[i], kBM);
+      mbar_init(&bars->s_free[i], kThreadsPerTile);
+      mbar_init(&bars->p_full[i], kThreadsPerTile);
       mbar_init(&bars->o_done[i], 1);
     }
     mbar_init(&bars->drained, 1);
@@ -130,158 +282,219 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpProducer) {
     // ------------------------------------------------------------ producer
+    regs_decrease<kRegsControl>();
     if (elect_one()) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(&bars->q_full, kTiles * kTileBytes);
-      for (int i = 0; i < kTiles; ++i)
-        tma_load_3d(&tm_q, &bars->q_full, smem + kOffQ + i * kTileBytes, 0,
-                    blk * kRowsPerCta + i * kBM, bh);
-      int issued = 0;
-      for (int j = 0; j < n_total; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages) {
-          if (!mbar_wait(&bars->kv_empty[s], ((j / kStages) - 1) & 1, abort_flag)) {
-            raise_abort(abort_flag, err_word, kDevErrTimeoutProducer);
+      int kv_it = 0;  // K/V tiles loaded so far (ring position)
+      int n = 0;
+      bool ok = true;
+      for (int k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
+        const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
+        const int qb = n & 1;
+        if (n >= 2 && !mbar_wait(&bars->q_empty[qb], ((n >> 1) - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&bars->q_full[qb], kTiles * kTileBytes);
+        for (int i = 0; i < kTiles; ++i)
+          tma_load_3d(&tm_q, &bars->q_full[qb], smem + kOffQ + (qb * kTiles + i) * kTileBytes, 0,
+                      w.blk * kRowsPerCta + i * kBM, w.bh);
+        for (int j = 0; j < w.n_total; ++j, ++kv_it) {
+          const int s = kv_it % kStages;
+          if (kv_it >= kStages &&
+              !mbar_wait(&bars->kv_empty[s], ((kv_it / kStages) - 1) & 1, abort_flag)) {
+            ok = false;
             break;
           }
+          mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
+          tma_load_3d(&tm_k, &bars->kv_full[s], smem + kOffK + s * kTileBytes, 0, j * kBN, w.bh);
+          tma_load_3d(&tm_v, &bars->kv_full[s], smem + kOffV + s * kTileBytes, 0, j * kBN, w.bh);
         }
-        mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
-        tma_load_3d(&tm_k, &bars->kv_full[s], smem + kOffK + s * kTileBytes, 0, j * kBN, bh);
-        tma_load_3d(&tm_v, &bars->kv_full[s], smem + kOffV + s * kTileBytes, 0, j * kBN, bh);
-        ++issued;
       }
+      if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutProducer);
       // Drain: every issued copy lands before the CTA may exit.
-      (void)mbar_wait(&bars->q_full, 0, abort_flag);
-      for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
+      for (int m = (n > 2 ? n - 2 : 0); m < n; ++m)
+        (void)mbar_wait(&bars->q_full[m & 1], (m >> 1) & 1, abort_flag);
+      for (int j = (kv_it > kStages ? kv_it - kStages : 0); j < kv_it; ++j)
         (void)mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1, abort_flag);
     }
   } else if (warp == kWarpMma) {
     // ---------------------------------------------------------- UMMA issuer
+    regs_decrease<kRegsControl>();
     if (elect_one()) {
       const uint32_t sQ = smem_u32(smem + kOffQ);
       const uint32_t sK = smem_u32(smem + kOffK);
       const uint32_t sV = smem_u32(smem + kOffV);
-      bool ok = mbar_wait(&bars->q_full, 0, abort_flag);
-      int kv_ready = -1;  // highest K/V tile whose kv_full has been observed
-      auto wait_kv = [&](int j) -> bool {
-        if (j <= kv_ready) return true;
-        if (!mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1, abort_flag)) return false;
-        kv_ready = j;
+      bool ok = true;
+      int kv_base = 0;            // ring position of the item's first K/V tile
+      int kv_ready = -1;          // highest ring position whose kv_full was observed
+      int s_cnt[kTiles] = {0, 0};   // S_i products issued so far
+      int pv_cnt[kTiles] = {0, 0};  // O_i products issued so far
+      auto wait_kv = [&](int it) -> bool {
+        if (it <= kv_ready) return true;
+        if (!mbar_wait(&bars->kv_full[it % kStages], (it / kStages) & 1, abort_flag)) return false;
+        kv_ready = it;
         return true;
       };
-      auto issue_s = [&](int i, int j) {
-        const int s = j % kStages;
-        const uint32_t d = tmem + col_s(i);
+      // S_i = Q_i·K^T into TMEM once softmax i has read the previous S_i.
+      auto issue_s = [&](int i, int qb, int it) -> bool {
+        if (s_cnt[i] > 0 && !mbar_wait(&bars->s_free[i], (s_cnt[i] - 1) & 1, abort_flag))
+          return false;
+        if (!wait_kv(it)) return false;
+        tc_fence_after();
+        const int s = it % kStages;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint64_t a = sdesc_sw128(sQ + i * kTileBytes + kk * 32, 16, 1024);
+          const uint64_t a = sdesc_sw128(sQ + (qb * kTiles + i) * kTileBytes + kk * 32, 16, 1024);
           const uint64_t b = sdesc_sw128(sK + s * kTileBytes + kk * 32, 16, 1024);
-          umma_ss(d, a, b, kIdescS, kk > 0 ? 1u : 0u);
+          umma_ss(tmem + col_s(i), a, b, kIdescS, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bars->s_full[i]);
+        ++s_cnt[i];
+        return true;
       };
-      auto issue_pv = [&](int i, int j) {
-        const int s = j % kStages;
+      // O_i (+)= P_i·V once softmax i has written P_i.
+      auto issue_pv = [&](int i, int it, bool first) -> bool {
+        if (!mbar_wait(&bars->p_full[i], pv_cnt[i] & 1, abort_flag)) return false;
+        tc_fence_after();
+        const int s = it % kStages;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint64_t b = sdesc_sw128(sV + s * kTileBytes + kk * 2048, 8192, 1024);
           // P_i: 128 lanes x 64 columns of packed bf16 pairs; 16 keys = 8 columns
-          umma_ts(tmem + col_o(i), tmem + col_s(i) + kk * 8, b, kIdescO,
-                  (j > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, b, kIdescO,
+                  (!first || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bars->o_done[i]);
+        ++pv_cnt[i];
+        return true;
       };
-      if (ok && (ok = wait_kv(0))) {
-        tc_fence_after();
-        for (int i = 0; i < kTiles; ++i) issue_s(i, 0);
-      }
-      for (int j = 0; ok && j < n_total; ++j) {
-        for (int i = 0; i < kTiles; ++i) {
-          if (j >= n_kv[i]) continue;
-          if (!mbar_wait(&bars->p_full[i], j & 1, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(i, j);
-          if (i == kTiles - 1) umma_commit(&bars->kv_empty[j % kStages]);
-          if (j + 1 < n_kv[i]) {
-            if (!wait_kv(j + 1)) { ok = false; break; }
-            tc_fence_after();
-            issue_s(i, j + 1);
-          }
+      for (int n = 0, k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
+        const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
+        const int qb = n & 1;
+        if (!mbar_wait(&bars->q_full[qb], (n >> 1) & 1, abort_flag)) { ok = false; break; }
+        for (int i = 0; ok && i < kTiles; ++i) ok = issue_s(i, qb, kv_base);
+        for (int j = 0; ok && j < w.n_total; ++j) {
+          // next scores as soon as each softmax has read the current ones
+          for (int i = 0; ok && i < kTiles; ++i)
+            if (j + 1 < w.n_kv[i]) ok = issue_s(i, qb, kv_base + j + 1);
+          // then O_i += P_i·V_j as each P_i arrives
+          for (int i = 0; ok && i < kTiles; ++i)
+            if (j < w.n_kv[i]) ok = issue_pv(i, kv_base + j, j == 0);
+          if (ok) umma_commit(&bars->kv_empty[(kv_base + j) % kStages]);
         }
+        if (ok) umma_commit(&bars->q_empty[qb]);  // every S of this item has read Q
+        kv_base += w.n_total;
       }
       if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutMma);
       // Every issued UMMA completes before teardown.
       umma_commit(&bars->drained);
       (void)mbar_wait(&bars->drained, 0, abort_flag);
     }
+  } else if (warp > kWarpMma) {
+    regs_decrease<kRegsControl>();  // idle warps of the control warpgroup
   } else {
     // -------------------------------------------------------------- softmax
-    const int tile = warp >> 2;                     // 0 or 1
+    // warp -> (tile, column half, TMEM lane quarter); thread = one score row,
+    // half of its columns.  The two halves of a row meet through shared memory
+    // at a 64-thread named barrier (ids 1..8, one per tile and lane quarter).
+    regs_increase<kRegsSoftmax>();
+    Exchange* xch = reinterpret_cast<Exchange*>(smem + kOffX);
+    const int tile = warp / (4 * kHalves);
+    const int half = (warp / 4) % kHalves;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;            // TMEM lane = row within the tile
-    const int q_idx = blk * kRowsPerCta + tile * kBM + row;
+    const uint32_t pair_bar = 1 + tile * 4 + quarter;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + col_s(tile);
-    const uint32_t o_addr = tmem + lane_base + col_o(tile);
-    const int nkv = n_kv[tile];
-    float m_used = -INFINITY;  // offset used for exponentials (log2 units)
-    float m_true = -INFINITY;  // true running row max (log2 units)
-    float l = 0.f;
+    const uint32_t s_addr = tmem + lane_base + col_s(tile) + half * kHalfCols;
+    const uint32_t p_addr = tmem + lane_base + col_p(tile) + half * (kHalfCols / 2);
+    const uint32_t o_addr = tmem + lane_base + col_o(tile) + half * kOutCols;
+    const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    int it = 0;  // S_i tiles processed so far, across items
     bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      if (!warp_wait(&bars->s_full[tile], j & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sr[kBN];
-#pragma unroll
-      for (int c = 0; c < kBN / 32; ++c)
-        tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
-      tmem_ld_wait();
-      float* sv = reinterpret_cast<float*>(sr);
-      if (j == nkv - 1) {
-        const int k0 = j * kBN;
-#pragma unroll
-        for (int c = 0; c < kBN; ++c) {
-          const int k_idx = k0 + c;
-          if ((k_idx >= Sk) || (kCausal && k_idx > q_idx)) sv[c] = -INFINITY;
-        }
-      }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < kBN; ++c) mx = fmaxf(mx, sv[c]);
-      const float t_max = mx * scale_log2;
-      m_true = fmaxf(m_true, t_max);
-      float m_new = m_used;
-      float alpha = 1.f;
-      if (t_max > m_used + kRescaleThreshold) {
-        m_new = t_max;
-        alpha = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
-      }
-      const float neg_m = -m_new;
-      float rs = 0.f;
-      uint32_t pk[kBN / 2];
-#pragma unroll
-      for (int c = 0; c < kBN; c += 2) {
-        const float p0 = fast_exp2(fmaf(sv[c], scale_log2, neg_m));
-        const float p1 = fast_exp2(fmaf(sv[c + 1], scale_log2, neg_m));
-        rs += p0 + p1;
-        pk[c >> 1] = pack_bf16x2(p0, p1);
-      }
-      l = l * alpha + rs;
-      // P_i over the first 64 columns of S_i.  S_i(j) has been read in full,
-      // and its commit followed P_i(j-1)·V in issue order, so that product has
-      // finished reading the previous P_i and O_i is stable.
-      tmem_st32(s_addr, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(s_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
-      if (j > 0) {
-        // already complete (see above); the wait is a cheap check
-        if (!warp_wait(&bars->o_done[tile], (j - 1) & 1, abort_flag)) { ok = false; break; }
+    for (int n = 0, k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
+      const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
+      const int q_idx = w.blk * kRowsPerCta + tile * kBM + row;
+      const int nkv = w.n_kv[tile];
+      float m_used = -INFINITY;  // offset used for exponentials (log2 units)
+      float m_true = -INFINITY;  // true running row max (log2 units)
+      float l = 0.f;             // this half's share of the row sum
+      for (int j = 0; j < nkv; ++j, ++it) {
+        if (!warp_wait(&bars->s_full[tile], it & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-          uint32_t orr[32];
+        uint32_t sr[kHalfCols];
 #pragma unroll
-          for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < kHalfCols / 32; ++c)
+          tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
+        tmem_ld_wait();
+        // S_i now lives in registers: let the tensor core write the next one.
+        tc_fence_before();
+        mbar_arrive(&bars->s_free[tile]);
+        float* sv = reinterpret_cast<float*>(sr);
+        if (j == nkv - 1) {
+          const int k0 = j * kBN + half * kHalfCols;
+#pragma unroll
+          for (int c = 0; c < kHalfCols; ++c) {
+            const int k_idx = k0 + c;
+            if ((k_idx >= Sk) || (kCausal && k_idx > q_idx)) sv[c] = -INFINITY;
+          }
+        }
+        // partial row max over this half: 4 independent chains of 3-input max
+        float mx0 = fmaxf(sv[0], sv[1]), mx1 = fmaxf(sv[2], sv[3]);
+        float mx2 = fmaxf(sv[4], sv[5]), mx3 = fmaxf(sv[6], sv[7]);
+        static_assert(kHalfCols % 8 == 0, "the max chains consume 8 scores per step");
+#pragma unroll
+        for (int c = 8; c < kHalfCols; c += 8) {
+          mx0 = fmax3(mx0, sv[c], sv[c + 1]);
+          mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
+          mx2 = fmax3(mx2, sv[c + 4], sv[c + 5]);
+          mx3 = fmax3(mx3, sv[c + 6], sv[c + 7]);
+        }
+        float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+        if constexpr (kHalves > 1) {
+          xch->max_part[it & 1][tile][half][row] = mx;
+          named_bar_sync(pair_bar, 64);
+          mx = fmaxf(mx, xch->max_part[it & 1][tile][half ^ 1][row]);
+        }
+        const float t_max = mx * scale_log2;
+        m_true = fmaxf(m_true, t_max);
+        float m_new = m_used;
+        float alpha = 1.f;
+        if (t_max > m_used + kRescaleThreshold) {
+          m_new = t_max;
+          alpha = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
+        }
+        // p = 2^(s·scale_log2 - m_new), two at a time, four partial sums.  The
+        // masked last tile uses the exponential unit for every element (masked
+        // keys give exactly 0); other tiles send part of the pairs through the
+        // FMA-pipe polynomial, which relieves the exponential unit.
+        const uint64_t negm2 = f2_pack(-m_new, -m_new);
+        uint64_t acc[4] = {0, 0, 0, 0};
+        uint32_t pk[kHalfCols / 2];
+        if (j == nkv - 1)
+          exp2_pairs<0>(sv, scale2, negm2, pk, acc);
+        else
+          exp2_pairs<kPolyPairsPer8>(sv, scale2, negm2, pk, acc);
+        float a0, a1;
+        f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), a0, a1);
+        l = l * alpha + (a0 + a1);
+        // P_i may be overwritten once the previous O_i += P_i·V has completed
+        // (for j == 0 the previous item's epilogue already waited for it).
+        if (j > 0) {
+          if (!warp_wait(&bars->o_done[tile], (it - 1) & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int c = 0; c < kHalfCols / 64; ++c)
+          tmem_st32(p_addr + c * 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
+        // O_i is stable here; rescale this thread's output columns if the warp
+        // has a row whose running max moved.
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < kOutCols / 32; ++c) {
+            uint32_t orr[32];
             tmem_ld32(o_addr + c * 32, orr);
             tmem_ld_wait();
 #pragma unroll
@@ -289,49 +502,59 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_st32(o_addr + c * 32, orr);
           }
         }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&bars->p_full[tile]);
+        m_used = m_new;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&bars->p_full[tile]);
-      m_used = m_new;
-    }
-    // ------------------------------------------------------------ epilogue
-    if (ok && nkv > 0) {
-      if (!warp_wait(&bars->o_done[tile], (nkv - 1) & 1, abort_flag)) ok = false;
-    }
-    if (!ok) {
-      raise_abort(abort_flag, err_word, kDevErrTimeoutSoftmax);
-    } else {
+      if (!ok) break;
+      // ---------------------------------------------------------- epilogue
+      if (!warp_wait(&bars->o_done[tile], (it - 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      uint32_t orr[kD];
-      tmem_ld32(o_addr, *reinterpret_cast<uint32_t(*)[32]>(&orr[0]));
-      tmem_ld32(o_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&orr[32]));
-      tmem_ld_wait();
-      if (q_idx < Sq) {
-        const float inv_l = 1.f / l;
-        const size_t row_off = static_cast<size_t>(bh) * Sq + q_idx;
-        if constexpr (kOutF32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + row_off * kD);
+      uint32_t orr[kOutCols];
 #pragma unroll
-          for (int c = 0; c < kD / 4; ++c)
+      for (int c = 0; c < kOutCols / 32; ++c)
+        tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&orr[c * 32]));
+      tmem_ld_wait();
+      float l_row = l;
+      if constexpr (kHalves > 1) {
+        xch->sum_part[tile][half][row] = l;
+        named_bar_sync(pair_bar, 64);
+        l_row += xch->sum_part[tile][half ^ 1][row];
+        // both halves have read the partner's sum before either reuses the slot
+        named_bar_sync(pair_bar, 64);
+      }
+      if (q_idx < Sq) {
+        const float inv_l = 1.f / l_row;
+        const size_t row_off = static_cast<size_t>(w.bh) * Sq + q_idx;
+        constexpr int kCols = kOutCols;
+        if constexpr (kOutF32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + row_off * kD +
+                                                  half * kCols);
+#pragma unroll
+          for (int c = 0; c < kCols / 4; ++c)
             dst[c] = make_float4(__uint_as_float(orr[4 * c]) * inv_l,
                                  __uint_as_float(orr[4 * c + 1]) * inv_l,
                                  __uint_as_float(orr[4 * c + 2]) * inv_l,
                                  __uint_as_float(orr[4 * c + 3]) * inv_l);
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + row_off * kD);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + row_off * kD +
+                                                half * kCols);
 #pragma unroll
-          for (int c = 0; c < kD / 8; ++c)
+          for (int c = 0; c < kCols / 8; ++c)
             dst[c] = make_uint4(
                 pack_bf16x2(__uint_as_float(orr[8 * c]) * inv_l, __uint_as_float(orr[8 * c + 1]) * inv_l),
                 pack_bf16x2(__uint_as_float(orr[8 * c + 2]) * inv_l, __uint_as_float(orr[8 * c + 3]) * inv_l),
                 pack_bf16x2(__uint_as_float(orr[8 * c + 4]) * inv_l, __uint_as_float(orr[8 * c + 5]) * inv_l),
                 pack_bf16x2(__uint_as_float(orr[8 * c + 6]) * inv_l, __uint_as_float(orr[8 * c + 7]) * inv_l));
         }
-        if (lse_out) lse_out[row_off] = (m_used + __log2f(l)) * kLn2;
-        if (max_out) max_out[row_off] = m_true * kLn2;
+        if (half == 0) {
+          if (lse_out) lse_out[row_off] = (m_used + __log2f(l_row)) * kLn2;
+          if (max_out) max_out[row_off] = m_true * kLn2;
+        }
       }
     }
+    if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutSoftmax);
   }
 
   tc_fence_before();
@@ -350,7 +573,13 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUten
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
-  dim3 grid(ceil_div(Sq, kRowsPerCta) * BH);
+  // Persistent CTAs: one per SM (at most one fits, by shared memory and TMEM).
+  int dev = 0, sms = 0;
+  e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const int n_items = ceil_div(Sq, kRowsPerCta) * BH;
+  dim3 grid(n_items < sms ? n_items : sms);
   kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, out, lse, mx, BH, Sq, Sk, scale_log2,
                                                device_error_word());
   return cudaGetLastError();

@@ -116,6 +116,23 @@ __device__ __forceinline__ void raise_abort(volatile int* abort_flag, int* err_w
   if (err_word != nullptr) atomicCAS(err_word, 0, code);
 }
 
+// Named barrier over `nthreads` threads (a multiple of 32) of this CTA.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Per-warpgroup register budget.  Every warp of a warpgroup executes the same
+// one; the sum over the block must stay within the launch's registers
+// (threads x registers per thread at launch), or an increase waits forever.
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+template <uint32_t kRegs>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
+}
+
 // -------------------------------------------------------------------- TMA --
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
