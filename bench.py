@@ -168,8 +168,10 @@ def run_reference(args):
     threads = os.cpu_count() or 1
     vals = []
     desc = ""
+    # each step is a bounded sample; the whole run stays within ~2 minutes
+    per_step = min(args.ref_seconds, 120.0 / max(1, args.warmup + args.steps))
     for i in range(args.warmup + args.steps):
-        v, threads, desc = cpu_prefill_sample(min_seconds=args.ref_seconds, nthreads=threads)
+        v, threads, desc = cpu_prefill_sample(min_seconds=per_step, nthreads=threads)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.median(vals)
@@ -282,8 +284,15 @@ def run_ours(args):
             ops.kv_decode_attn(qs[t - 1], kc, vc, DEC_L0 + t, k_new=kns[t - 1], v_new=vns[t - 1],
                                out=dout, lse=dlse)
 
+    # warm-up outside capture (sizes the library's decode scratch), then the
+    # 128 launch-bound steps are captured once in a CUDA graph and replayed
     for _ in range(max(1, args.warmup)):
         decode_pass()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        decode_pass()
+    graph.replay()
     torch.cuda.synchronize()
     barrier()
     d0 = torch.cuda.Event(enable_timing=True)
@@ -291,16 +300,50 @@ def run_ours(args):
     dec_reps = max(1, args.decode_reps)
     d0.record(stream)
     for _ in range(dec_reps):
-        decode_pass()
+        graph.replay()
     d1.record(stream)
     torch.cuda.synchronize()
     barrier()
     dec_ms_local = d0.elapsed_time(d1) / dec_reps
     dec_ms = max_over_ranks(dec_ms_local)
-    clocks = sampler.stop()
     dec_bytes_total = sum(dec_bytes(DEC_L0 + t) for t in range(1, DEC_T + 1))
     dec_tokens = world * DEC_B * DEC_T / (dec_ms * 1e-3)
     dec_gbs = dec_bytes_total / (dec_ms_local * 1e-3) / 1e9
+    del graph
+
+    # ---- fused linear + bias + GELU (the MLP-up of the 24-layer dim-1024
+    # model's prefill: 32 x 2048 tokens, 1024 -> 4096) and LayerNorm over the
+    # same tokens; each timed over `args.aux_reps` calls
+    gm, gn, gk = 65536, 4096, 1024
+    ga = torch.randn(gm, gk, device=dev, generator=gen).bfloat16()
+    gw = (0.02 * torch.randn(gn, gk, device=dev, generator=gen)).bfloat16()
+    gb = torch.zeros(gn, device=dev)
+    gy = torch.empty(gm, gn, device=dev, dtype=torch.bfloat16)
+    lx = torch.randn(gm, gk, device=dev, generator=gen)
+    ly = torch.empty(gm, gk, device=dev, dtype=torch.bfloat16)
+    lmean = torch.empty(gm, device=dev)
+    lrstd = torch.empty(gm, device=dev)
+
+    def time_calls(fn, reps):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(reps):
+            fn()
+        a1.record(stream)
+        torch.cuda.synchronize()
+        return a0.elapsed_time(a1) / reps
+
+    gemm_ms = time_calls(lambda: ops.linear(ga, gw, gb, act="sigmoid", out=gy), args.aux_reps)
+    gemm_tflops = 2.0 * gm * gn * gk / (gemm_ms * 1e-3) / 1e12
+    ln_ms = time_calls(lambda: ops.layernorm(lx, out=ly, mean=lmean, rstd=lrstd), args.aux_reps)
+    ln_bytes = gm * gk * (4 + 2) + gm * 8
+    ln_gbs = ln_bytes / (ln_ms * 1e-3) / 1e9
+    del ga, gw, gy, lx, ly
+    clocks = sampler.stop()
 
     # ---- end to end through the public API with host buffers (pinned)
     hq = torch.randn(B, H, S, D, generator=torch.Generator().manual_seed(7)).bfloat16().pin_memory()
@@ -367,10 +410,28 @@ def run_ours(args):
                 "value": dec_tokens, "unit": "tokens/s", "ms_per_pass": dec_ms,
                 "us_per_token_step": dec_ms * 1e3 / DEC_T,
                 "gpu_launches": dec_reps * DEC_T,
+                "launch": "128 steps captured in one CUDA graph, replayed",
                 "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peaks["hbm_gbs"],
                              "unit": "GB/s", "frac": dec_gbs / peaks["hbm_gbs"],
                              "traffic": dec_traffic,
                              "bytes_per_pass": dec_bytes_total},
+            },
+            "gemm_bias_gelu": {
+                "workload": f"Y = gelu_sigmoid(X W^T + b), X [{gm}][{gk}], W [{gn}][{gk}] bf16",
+                "value": gemm_tflops, "unit": "TFLOP/s", "ms_per_call": gemm_ms,
+                "gpu_launches": args.aux_reps,
+                "roofline": {"bound": "tensor", "achieved": gemm_tflops,
+                             "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": gemm_tflops / peaks["bf16_tflops"],
+                             "traffic": load_traffic("gemm_bias_gelu_m65536_n4096_k1024")},
+            },
+            "layernorm": {
+                "workload": f"LayerNorm rows={gm} d={gk}, fp32 in, bf16 out, fp32 stats",
+                "value": ln_gbs, "unit": "GB/s", "ms_per_call": ln_ms,
+                "gpu_launches": args.aux_reps,
+                "roofline": {"bound": "hbm", "achieved": ln_gbs, "peak": peaks["hbm_gbs"],
+                             "unit": "GB/s", "frac": ln_gbs / peaks["hbm_gbs"],
+                             "traffic": load_traffic("layernorm_rows65536_d1024")},
             },
         }
         print(json.dumps(line), flush=True)
@@ -388,6 +449,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--soak", type=float, default=2.0, help="seconds of load before timing")
     ap.add_argument("--decode-reps", type=int, default=5)
+    ap.add_argument("--aux-reps", type=int, default=10, help="timed GEMM / LayerNorm calls")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")

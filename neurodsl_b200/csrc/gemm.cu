@@ -9,8 +9,9 @@
 // A [M][K] and W [N][K] are bf16, K contiguous (W is the (out, in) weight of
 // a Linear layer).  Persistent CTAs walk 128 x BN output tiles; K is consumed
 // in blocks of 64 through a TMA ring that runs on across tiles.  Warp roles
-// (256 threads): warp 0 TMA producer, warp 1 TMEM allocator + UMMA issuer,
-// warps 4..7 epilogue (thread t owns accumulator row t = TMEM lane t).  Two
+// (384 threads): warp 0 TMA producer, warp 1 TMEM allocator + UMMA issuer,
+// warps 4..11 epilogue, two per TMEM lane quarter (thread = accumulator row
+// = TMEM lane; the pair splits the tile's 32-column chunks).  Two
 // TMEM accumulators alternate between tiles, so the epilogue of one tile
 // overlaps the main loop of the next.  The epilogue transposes each 32x32
 // chunk through padded shared memory so global stores (and residual loads)
@@ -29,17 +30,19 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr uint32_t kATileBytes = kBM * kBK * 2;  // 16 KB
 constexpr int kStagePitch = 33;                  // words per staged row (32 + 1 pad)
 
 template <int BN>
 struct GemmCfg {
+  // 4 x 48 KB (BN 256) or 6 x 32 KB (BN 128) stages + 33 KB staging + barriers
+  // = 231,680 bytes, within the 232,448-byte per-block limit.
   static constexpr int kStages = BN >= 256 ? 4 : 6;
   static constexpr uint32_t kBTileBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
   static constexpr uint32_t kOffStage = kStages * kStageBytes;          // epilogue staging
-  static constexpr uint32_t kStageAreaBytes = 4 * 32 * kStagePitch * 4; // 4 warps x 32x33 words
+  static constexpr uint32_t kStageAreaBytes = 8 * 32 * kStagePitch * 4; // 8 warps x 32x33 words
   static constexpr uint32_t kOffBar = kOffStage + kStageAreaBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
   static constexpr uint32_t kTmemCols = 2 * BN;   // two accumulators (power of two)
@@ -51,7 +54,7 @@ struct GemmBars {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t acc_full[2];    // accumulator b holds a finished tile (UMMA commit)
-  uint64_t acc_empty[2];   // epilogue has read accumulator b (128 threads)
+  uint64_t acc_empty[2];   // epilogue has read accumulator b (256 threads)
   uint64_t drained;
   uint32_t tmem_base;
   int abort_flag;
@@ -60,10 +63,12 @@ struct GemmBars {
 template <int kAct>
 __device__ __forceinline__ float apply_act(float z) {
   if constexpr (kAct == ND_ACT_GELU_SIGMOID) {
-    return z / (1.f + __expf(-1.702f * z));
+    return __fdividef(z, 1.f + __expf(-1.702f * z));
   } else if constexpr (kAct == ND_ACT_GELU_TANH) {
     const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-    return 0.5f * z * (1.f + tanhf(u));
+    float th;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(u));  // hardware tanh
+    return 0.5f * z * (1.f + th);
   } else if constexpr (kAct == ND_ACT_GELU_ERF) {
     return 0.5f * z * (1.f + erff(z * 0.7071067811865476f));
   } else {
@@ -113,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->acc_full[b], 1);
-      mbar_init(&bars->acc_empty[b], 128);
+      mbar_init(&bars->acc_empty[b], 256);
     }
     mbar_init(&bars->drained, 1);
     bars->abort_flag = 0;
@@ -194,9 +199,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // bias, the activation and the residual are applied and the output is
     // stored: every global access of a warp covers contiguous row segments.
     // The TMEM load of the next chunk is in flight during this column phase.
+    // Two warps per TMEM lane quarter: warp 4+q takes the even chunks of rows
+    // 32q..32q+31, warp 8+q the odd ones.
     const int quarter = warp & 3;
+    const int half = (warp >> 2) - 1;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    float* stage = reinterpret_cast<float*>(smem + Cfg::kOffStage) + quarter * 32 * kStagePitch;
+    float* stage = reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - 4) * 32 * kStagePitch;
     const int sub = lane >> 4;      // column phase: lanes 0..15 even rows, 16..31 odd rows
     const int cw = (lane & 15) * 2; // column pair within the chunk
     const bool pair_ok = (N % 2) == 0;
@@ -212,20 +220,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = tmem + lane_base + b * BN;
       const int n_chunks = min(BN / 32, (N - n_blk * BN + 31) / 32);
       uint32_t r[2][32];
-      tmem_ld32(acc, r[0]);
+      if (half < n_chunks) tmem_ld32(acc + half * 32, r[0]);
 #pragma unroll 1
-      for (int c = 0; c < n_chunks; ++c) {
+      for (int c = half, k = 0; c < n_chunks; c += 2, ++k) {
         const int col0 = n_blk * BN + c * 32;
         tmem_ld_wait();
-        // (c & 1) selects the register buffer; both branches are unrolled so
+        // (k & 1) selects the register buffer; both branches are unrolled so
         // the buffers stay in registers
 #define ND_STAGE_CHUNK(CUR, NXT)                                                  \
         {                                                                        \
           _Pragma("unroll") for (int e = 0; e < 32; ++e)                         \
             stage[lane * kStagePitch + e] = __uint_as_float(r[CUR][e]);          \
-          if (c + 1 < n_chunks) tmem_ld32(acc + (c + 1) * 32, r[NXT]);           \
+          if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);           \
         }
-        if (c & 1) ND_STAGE_CHUNK(1, 0) else ND_STAGE_CHUNK(0, 1)
+        if (k & 1) ND_STAGE_CHUNK(1, 0) else ND_STAGE_CHUNK(0, 1)
 #undef ND_STAGE_CHUNK
         __syncwarp();
         const int n = col0 + cw;
