@@ -108,25 +108,6 @@ struct Bars {
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
-// ---- packed fp32 helpers (two lanes per instruction) -----------------------
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 // bf16x2 pack of two non-negative finite floats on the integer pipe: round to
 // nearest (halfway cases up) by adding half an output ulp to the fp32 bits,
 // then keep the high halves.  The conversion instruction would run on the
@@ -159,12 +140,6 @@ constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
 // not by the exponential unit (which sustains 16/clk/SM), so moving work to
 // the FMA pipe only adds instructions: 0 is the fastest setting.
 constexpr int kPolyPairsPer8 = 0;
-
-__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
 
 // Probabilities for 2·kHalfCols/2 scores: p = 2^(s·scale - m) packed to bf16
 // in pk, row-sum partials accumulated in acc (four f32x2 chains).

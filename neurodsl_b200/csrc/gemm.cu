@@ -13,10 +13,10 @@
 // warps 4..11 epilogue, two per TMEM lane quarter (thread = accumulator row
 // = TMEM lane; the pair splits the tile's 32-column chunks).  Two
 // TMEM accumulators alternate between tiles, so the epilogue of one tile
-// overlaps the main loop of the next.  The epilogue transposes each 32x32
-// chunk through padded shared memory so global stores (and residual loads)
-// cover contiguous row segments instead of one row per lane; the activation
-// is a template parameter, so the epilogue carries no per-element branches.
+// overlaps the main loop of the next.  The epilogue keeps each row in
+// registers: bias, activation and residual are applied two columns per
+// instruction (f32x2) and the row segment leaves in 16-byte stores; the
+// activation is a template parameter, so there are no per-element branches.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -32,19 +32,17 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 384;
 constexpr uint32_t kATileBytes = kBM * kBK * 2;  // 16 KB
-constexpr int kStagePitch = 33;                  // words per staged row (32 + 1 pad)
 
 template <int BN>
 struct GemmCfg {
-  // 4 x 48 KB (BN 256) or 6 x 32 KB (BN 128) stages + 33 KB staging + barriers
-  // = 231,680 bytes, within the 232,448-byte per-block limit.
-  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  // 4 x 48 KB (BN 256), 7 x 32 KB (BN 128) or 9 x 24 KB (BN 64) stages plus
+  // barriers, within the 232,448-byte per-block limit.
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 7 : 9);
   static constexpr uint32_t kBTileBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
-  static constexpr uint32_t kOffStage = kStages * kStageBytes;          // epilogue staging
-  static constexpr uint32_t kStageAreaBytes = 8 * 32 * kStagePitch * 4; // 8 warps x 32x33 words
-  static constexpr uint32_t kOffBar = kOffStage + kStageAreaBytes;
+  static constexpr uint32_t kOffBar = kStages * kStageBytes;
   static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
+  static_assert(kSmemBytes <= 232448, "dynamic shared memory per block");
   static constexpr uint32_t kTmemCols = 2 * BN;   // two accumulators (power of two)
   static constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, BN, false, false);
 };
@@ -60,19 +58,133 @@ struct GemmBars {
   int abort_flag;
 };
 
+// GELU constants: sqrt(2/pi) and sqrt(2/pi) * 0.044715 for the tanh form.
+constexpr float kGeluC0 = 0.7978845608028654f;
+constexpr float kGeluC1 = 0.7978845608028654f * 0.044715f;
+
+// The activation of two pre-activation values, packed as f32x2.
+//   sigmoid form  z·σ(1.702 z) = ½z + ½z·tanh(0.851 z), using the identity
+//                 σ(a) = (1 + tanh(a/2)) / 2: one hardware tanh per value;
+//   tanh form     ½z (1 + tanh(√(2/π) (z + 0.044715 z³)));
+//   erf form      ½z (1 + erf(z / √2)) (CUDA's erff).
 template <int kAct>
-__device__ __forceinline__ float apply_act(float z) {
-  if constexpr (kAct == ND_ACT_GELU_SIGMOID) {
-    return __fdividef(z, 1.f + __expf(-1.702f * z));
-  } else if constexpr (kAct == ND_ACT_GELU_TANH) {
-    const float u = 0.7978845608028654f * (z + 0.044715f * z * z * z);
-    float th;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(u));  // hardware tanh
-    return 0.5f * z * (1.f + th);
+__device__ __forceinline__ uint64_t act2(uint64_t z) {
+  if constexpr (kAct == ND_ACT_GELU_SIGMOID || kAct == ND_ACT_GELU_TANH) {
+    const uint64_t hz = f2_mul(z, f2_pack(0.5f, 0.5f));
+    uint64_t u;
+    if constexpr (kAct == ND_ACT_GELU_SIGMOID) {
+      u = f2_mul(z, f2_pack(0.851f, 0.851f));
+    } else {
+      const uint64_t c = f2_fma(f2_mul(z, z), f2_pack(kGeluC1, kGeluC1), f2_pack(kGeluC0, kGeluC0));
+      u = f2_mul(c, z);
+    }
+    float u0, u1;
+    f2_unpack(u, u0, u1);
+    return f2_fma(hz, f2_pack(tanh_approx(u0), tanh_approx(u1)), hz);
   } else if constexpr (kAct == ND_ACT_GELU_ERF) {
-    return 0.5f * z * (1.f + erff(z * 0.7071067811865476f));
+    float z0, z1;
+    f2_unpack(z, z0, z1);
+    return f2_pack(0.5f * z0 * (1.f + erff(z0 * 0.7071067811865476f)),
+                   0.5f * z1 * (1.f + erff(z1 * 0.7071067811865476f)));
   } else {
     return z;
+  }
+}
+template <int kAct>
+__device__ __forceinline__ float act1(float z) {
+  float a, b;
+  f2_unpack(act2<kAct>(f2_pack(z, 0.f)), a, b);
+  return a;
+}
+
+// One 32-column chunk of one output row: y = act(acc + bias) + residual.
+// `vec` says the row segments may be moved in 16-byte pieces (N % 8 == 0 and
+// 16-byte aligned pointers); the ragged last chunk goes column by column.
+template <bool kOutF32, int kAct>
+__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const float* __restrict__ bias,
+                                            const void* __restrict__ residual, int residual_f32,
+                                            void* __restrict__ Y, int m, int M, int col0, int N,
+                                            int vec) {
+  if (vec && col0 + 32 <= N) {
+    uint64_t z[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) z[q] = f2_pack(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+    if (bias != nullptr) {
+      // every lane reads the same 128 bytes: a broadcast from L1
+      const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 bb = __ldg(b4 + q);
+        z[2 * q] = f2_add(z[2 * q], f2_pack(bb.x, bb.y));
+        z[2 * q + 1] = f2_add(z[2 * q + 1], f2_pack(bb.z, bb.w));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 16; ++q) z[q] = act2<kAct>(z[q]);
+    if (m >= M) return;
+    const size_t idx = static_cast<size_t>(m) * N + col0;
+    if (residual != nullptr) {
+      if (residual_f32) {
+        const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(residual) + idx);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 rv = rp[q];
+          z[2 * q] = f2_add(z[2 * q], f2_pack(rv.x, rv.y));
+          z[2 * q + 1] = f2_add(z[2 * q + 1], f2_pack(rv.z, rv.w));
+        }
+      } else {
+        // bf16 -> fp32 is exact: the 16 bits become the high half of the word
+        const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(residual) + idx);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 rv = rp[q];
+          const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h)
+            z[4 * q + h] = f2_add(z[4 * q + h], f2_pack(__uint_as_float(w[h] << 16),
+                                                        __uint_as_float(w[h] & 0xffff0000u)));
+        }
+      }
+    }
+    if constexpr (kOutF32) {
+      float4* yp = reinterpret_cast<float4*>(static_cast<float*>(Y) + idx);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float a, b, c, d;
+        f2_unpack(z[2 * q], a, b);
+        f2_unpack(z[2 * q + 1], c, d);
+        yp[q] = make_float4(a, b, c, d);
+      }
+    } else {
+      uint4* yp = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(Y) + idx);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          float lo, hi;
+          f2_unpack(z[4 * q + h], lo, hi);
+          w[h] = pack_bf16x2(lo, hi);
+        }
+        yp[q] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  } else {
+    if (m >= M) return;
+    const size_t idx = static_cast<size_t>(m) * N + col0;
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      const int n = col0 + e;
+      if (n >= N) continue;
+      float z = __uint_as_float(r[e]);
+      if (bias != nullptr) z += __ldg(bias + n);
+      z = act1<kAct>(z);
+      if (residual != nullptr)
+        z += residual_f32 ? static_cast<const float*>(residual)[idx + e]
+                          : __bfloat162float(static_cast<const __nv_bfloat16*>(residual)[idx + e]);
+      if constexpr (kOutF32) static_cast<float*>(Y)[idx + e] = z;
+      else static_cast<__nv_bfloat16*>(Y)[idx + e] = __float2bfloat16_rn(z);
+    }
   }
 }
 
@@ -94,7 +206,7 @@ template <int BN, bool kOutF32, int kAct>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                 const float* __restrict__ bias, const void* __restrict__ residual,
-                int residual_f32, void* __restrict__ Y, int M, int N, int K,
+                int residual_f32, void* __restrict__ Y, int M, int N, int K, int vec,
                 int* __restrict__ err_word) {
   using Cfg = GemmCfg<BN>;
   constexpr int kStages = Cfg::kStages;
@@ -194,20 +306,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------- epilogue
-    // Per 32-column chunk: the raw fp32 accumulators are staged row-per-lane
-    // in padded shared memory, then read back column-per-lane, where the
-    // bias, the activation and the residual are applied and the output is
-    // stored: every global access of a warp covers contiguous row segments.
-    // The TMEM load of the next chunk is in flight during this column phase.
-    // Two warps per TMEM lane quarter: warp 4+q takes the even chunks of rows
-    // 32q..32q+31, warp 8+q the odd ones.
+    // Thread = accumulator row = TMEM lane.  Per 32-column chunk the row's
+    // fp32 accumulators come out of tensor memory into registers
+    // (tcgen05.ld 32x32b) and store_chunk finishes and writes them.  Two warps
+    // per TMEM lane quarter: warp 4+q takes the even chunks of rows
+    // 32q..32q+31, warp 8+q the odd ones; the next chunk's TMEM load is in
+    // flight while one is processed.
     const int quarter = warp & 3;
     const int half = (warp >> 2) - 1;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    float* stage = reinterpret_cast<float*>(smem + Cfg::kOffStage) + (warp - 4) * 32 * kStagePitch;
-    const int sub = lane >> 4;      // column phase: lanes 0..15 even rows, 16..31 odd rows
-    const int cw = (lane & 15) * 2; // column pair within the chunk
-    const bool pair_ok = (N % 2) == 0;
     bool ok = true;
     int lt = 0;
     for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
@@ -216,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = lt & 1;
       if (!warp_wait(&bars->acc_full[b], (lt >> 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const int row0 = m_blk * kBM + quarter * 32;  // first row of this warp's 32
+      const int m = m_blk * kBM + quarter * 32 + lane;  // this thread's output row
       const uint32_t acc = tmem + lane_base + b * BN;
       const int n_chunks = min(BN / 32, (N - n_blk * BN + 31) / 32);
       uint32_t r[2][32];
@@ -227,63 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
         // (k & 1) selects the register buffer; both branches are unrolled so
         // the buffers stay in registers
-#define ND_STAGE_CHUNK(CUR, NXT)                                                  \
-        {                                                                        \
-          _Pragma("unroll") for (int e = 0; e < 32; ++e)                         \
-            stage[lane * kStagePitch + e] = __uint_as_float(r[CUR][e]);          \
-          if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);           \
+#define ND_EPILOGUE_CHUNK(CUR, NXT)                                                        \
+        {                                                                                 \
+          if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);                    \
+          store_chunk<kOutF32, kAct>(r[CUR], bias, residual, residual_f32, Y, m, M, col0, N, \
+                                     vec);                                                \
         }
-        if (k & 1) ND_STAGE_CHUNK(1, 0) else ND_STAGE_CHUNK(0, 1)
-#undef ND_STAGE_CHUNK
-        __syncwarp();
-        const int n = col0 + cw;
-        float b0 = 0.f, b1 = 0.f;
-        if (bias != nullptr) {
-          if (n < N) b0 = __ldg(bias + n);
-          if (n + 1 < N) b1 = __ldg(bias + n + 1);
-        }
-#pragma unroll 4
-        for (int i = 0; i < 16; ++i) {
-          const int rr = 2 * i + sub;
-          const int m = row0 + rr;
-          float z0 = apply_act<kAct>(stage[rr * kStagePitch + cw] + b0);
-          float z1 = apply_act<kAct>(stage[rr * kStagePitch + cw + 1] + b1);
-          if (m < M) {
-            const size_t idx = static_cast<size_t>(m) * N + n;
-            if (pair_ok && n + 1 < N) {
-              if (residual != nullptr) {
-                if (residual_f32) {
-                  const float2 rv = *reinterpret_cast<const float2*>(static_cast<const float*>(residual) + idx);
-                  z0 += rv.x;
-                  z1 += rv.y;
-                } else {
-                  const __nv_bfloat162 rv =
-                      *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(residual) + idx);
-                  z0 += __low2float(rv);
-                  z1 += __high2float(rv);
-                }
-              }
-              if constexpr (kOutF32)
-                *reinterpret_cast<float2*>(static_cast<float*>(Y) + idx) = make_float2(z0, z1);
-              else
-                *reinterpret_cast<uint32_t*>(static_cast<__nv_bfloat16*>(Y) + idx) = pack_bf16x2(z0, z1);
-            } else {
-              float zz[2] = {z0, z1};
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                if (n + q < N) {
-                  float zq = zz[q];
-                  if (residual != nullptr)
-                    zq += residual_f32 ? static_cast<const float*>(residual)[idx + q]
-                                       : __bfloat162float(static_cast<const __nv_bfloat16*>(residual)[idx + q]);
-                  if constexpr (kOutF32) static_cast<float*>(Y)[idx + q] = zq;
-                  else static_cast<__nv_bfloat16*>(Y)[idx + q] = __float2bfloat16_rn(zq);
-                }
-              }
-            }
-          }
-        }
-        __syncwarp();
+        if (k & 1) ND_EPILOGUE_CHUNK(1, 0) else ND_EPILOGUE_CHUNK(0, 1)
+#undef ND_EPILOGUE_CHUNK
       }
       // accumulator b fully read: the MMA warp may reuse it
       tc_fence_before();
@@ -311,8 +369,10 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUten
   if (e != cudaSuccess) return e;
   const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
   dim3 grid(tiles < sms ? tiles : sms);
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int vec = (N % 8 == 0) && al16(Y) && al16(residual) && al16(bias) ? 1 : 0;
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tw, bias, residual, residual_f32 ? 1 : 0,
-                                                    Y, M, N, K, device_error_word());
+                                                    Y, M, N, K, vec, device_error_word());
   return cudaGetLastError();
 }
 
