@@ -97,15 +97,51 @@ __device__ __forceinline__ float act1(float z) {
   return a;
 }
 
-// One 32-column chunk of one output row: y = act(acc + bias) + residual.
+// The residual segment of one output row for one 32-column chunk, as f32x2
+// pairs; requested before the accumulators are read so the loads overlap.
+// Only the 16-byte path (see store_chunk) uses it.
+__device__ __forceinline__ void load_residual_chunk(uint64_t (&res)[16], const void* __restrict__ residual,
+                                                    int residual_f32, int m, int M, int col0, int N,
+                                                    int vec) {
+  if (vec && col0 + 32 <= N && m < M) {
+    const size_t idx = static_cast<size_t>(m) * N + col0;
+    {
+      if (residual_f32) {
+        const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(residual) + idx);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 rv = rp[q];
+          res[2 * q] = f2_pack(rv.x, rv.y);
+          res[2 * q + 1] = f2_pack(rv.z, rv.w);
+        }
+      } else {
+        // bf16 -> fp32 is exact: the 16 bits become the high half of the word
+        const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(residual) + idx);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 rv = rp[q];
+          const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h)
+            res[4 * q + h] = f2_pack(__uint_as_float(w[h] << 16), __uint_as_float(w[h] & 0xffff0000u));
+        }
+      }
+    }
+  }
+}
+
+// One 32-column chunk of one output row: y = act(acc + bias) + residual, the
+// residual taken from `res` (load_residual_chunk) on the 16-byte path.
 // `vec` says the row segments may be moved in 16-byte pieces (N % 8 == 0 and
 // 16-byte aligned pointers); the ragged last chunk goes column by column.
-template <bool kOutF32, int kAct>
-__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const float* __restrict__ bias,
+template <bool kOutF32, int kAct, bool kRes>
+__device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const uint64_t (&res)[16],
+                                            const float* __restrict__ bias,
                                             const void* __restrict__ residual, int residual_f32,
                                             void* __restrict__ Y, int m, int M, int col0, int N,
                                             int vec) {
   if (vec && col0 + 32 <= N) {
+    const size_t idx = static_cast<size_t>(m) * N + col0;
     uint64_t z[16];
 #pragma unroll
     for (int q = 0; q < 16; ++q) z[q] = f2_pack(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
@@ -122,29 +158,9 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const float
 #pragma unroll
     for (int q = 0; q < 16; ++q) z[q] = act2<kAct>(z[q]);
     if (m >= M) return;
-    const size_t idx = static_cast<size_t>(m) * N + col0;
-    if (residual != nullptr) {
-      if (residual_f32) {
-        const float4* rp = reinterpret_cast<const float4*>(static_cast<const float*>(residual) + idx);
+    if constexpr (kRes) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 rv = rp[q];
-          z[2 * q] = f2_add(z[2 * q], f2_pack(rv.x, rv.y));
-          z[2 * q + 1] = f2_add(z[2 * q + 1], f2_pack(rv.z, rv.w));
-        }
-      } else {
-        // bf16 -> fp32 is exact: the 16 bits become the high half of the word
-        const uint4* rp = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(residual) + idx);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 rv = rp[q];
-          const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-          for (int h = 0; h < 4; ++h)
-            z[4 * q + h] = f2_add(z[4 * q + h], f2_pack(__uint_as_float(w[h] << 16),
-                                                        __uint_as_float(w[h] & 0xffff0000u)));
-        }
-      }
+      for (int q = 0; q < 16; ++q) z[q] = f2_add(z[q], res[q]);
     }
     if constexpr (kOutF32) {
       float4* yp = reinterpret_cast<float4*>(static_cast<float*>(Y) + idx);
@@ -179,7 +195,7 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const float
       float z = __uint_as_float(r[e]);
       if (bias != nullptr) z += __ldg(bias + n);
       z = act1<kAct>(z);
-      if (residual != nullptr)
+      if constexpr (kRes)
         z += residual_f32 ? static_cast<const float*>(residual)[idx + e]
                           : __bfloat162float(static_cast<const __nv_bfloat16*>(residual)[idx + e]);
       if constexpr (kOutF32) static_cast<float*>(Y)[idx + e] = z;
@@ -202,7 +218,7 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   n_blk = r / rows;
 }
 
-template <int BN, bool kOutF32, int kAct>
+template <int BN, bool kOutF32, int kAct, bool kRes>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                 const float* __restrict__ bias, const void* __restrict__ residual,
@@ -317,31 +333,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
     int lt = 0;
+    auto prefetch_residual = [&](int t) {
+      int pm, pn;
+      tile_coords(t, m_tiles, n_tiles, pm, pn);
+      const int row = pm * kBM + quarter * 32 + lane;
+      const int chunks = min(BN / 32, (N - pn * BN + 31) / 32);
+      if (row >= M) return;
+      const size_t esz = residual_f32 ? 4 : 2;
+      const char* base =
+          static_cast<const char*>(residual) + (static_cast<size_t>(row) * N + pn * BN) * esz;
+      for (int c = half; c < chunks; c += 2) prefetch_l2(base + c * 32 * esz);
+    };
+    if constexpr (kRes)
+      if (static_cast<int>(blockIdx.x) < n_tiles_total) prefetch_residual(blockIdx.x);
     for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
       int m_blk, n_blk;
       tile_coords(t, m_tiles, n_tiles, m_blk, n_blk);
       const int b = lt & 1;
+      const int m = m_blk * kBM + quarter * 32 + lane;  // this thread's output row
+      const int n_chunks = min(BN / 32, (N - n_blk * BN + 31) / 32);
+      // The next tile's residual row segments go to L2 while this tile is
+      // finished, so the epilogue's loads do not wait on DRAM.
+      if constexpr (kRes)
+        if (t + static_cast<int>(gridDim.x) < n_tiles_total) prefetch_residual(t + gridDim.x);
       if (!warp_wait(&bars->acc_full[b], (lt >> 1) & 1, abort_flag)) { ok = false; break; }
       tc_fence_after();
-      const int m = m_blk * kBM + quarter * 32 + lane;  // this thread's output row
       const uint32_t acc = tmem + lane_base + b * BN;
-      const int n_chunks = min(BN / 32, (N - n_blk * BN + 31) / 32);
-      uint32_t r[2][32];
-      if (half < n_chunks) tmem_ld32(acc + half * 32, r[0]);
+      if constexpr (kRes) {
+        // One TMEM buffer: the registers go to the residual segment instead,
+        // whose global loads are the longer wait.
 #pragma unroll 1
-      for (int c = half, k = 0; c < n_chunks; c += 2, ++k) {
-        const int col0 = n_blk * BN + c * 32;
-        tmem_ld_wait();
-        // (k & 1) selects the register buffer; both branches are unrolled so
-        // the buffers stay in registers
-#define ND_EPILOGUE_CHUNK(CUR, NXT)                                                        \
-        {                                                                                 \
-          if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);                    \
-          store_chunk<kOutF32, kAct>(r[CUR], bias, residual, residual_f32, Y, m, M, col0, N, \
-                                     vec);                                                \
+        for (int c = half; c < n_chunks; c += 2) {
+          const int col0 = n_blk * BN + c * 32;
+          uint32_t r[32];
+          uint64_t res[16];
+          tmem_ld32(acc + c * 32, r);
+          load_residual_chunk(res, residual, residual_f32, m, M, col0, N, vec);
+          tmem_ld_wait();
+          store_chunk<kOutF32, kAct, true>(r, res, bias, residual, residual_f32, Y, m, M, col0, N, vec);
         }
-        if (k & 1) ND_EPILOGUE_CHUNK(1, 0) else ND_EPILOGUE_CHUNK(0, 1)
+      } else {
+        const uint64_t no_res[16] = {};
+        uint32_t r[2][32];
+        if (half < n_chunks) tmem_ld32(acc + half * 32, r[0]);
+#pragma unroll 1
+        for (int c = half, k = 0; c < n_chunks; c += 2, ++k) {
+          const int col0 = n_blk * BN + c * 32;
+          tmem_ld_wait();
+          // (k & 1) selects the register buffer; both branches are unrolled so
+          // the buffers stay in registers
+#define ND_EPILOGUE_CHUNK(CUR, NXT)                                                        \
+          {                                                                               \
+            if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);                  \
+            store_chunk<kOutF32, kAct, false>(r[CUR], no_res, bias, residual, residual_f32, Y, \
+                                              m, M, col0, N, vec);                        \
+          }
+          if (k & 1) ND_EPILOGUE_CHUNK(1, 0) else ND_EPILOGUE_CHUNK(0, 1)
 #undef ND_EPILOGUE_CHUNK
+        }
       }
       // accumulator b fully read: the MMA warp may reuse it
       tc_fence_before();
@@ -358,12 +407,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool kOutF32, int kAct>
+template <int BN, bool kOutF32, int kAct, bool kRes>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tw,
                          const float* bias, const void* residual, bool residual_f32, void* Y,
                          int M, int N, int K, int sms) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_kernel<BN, kOutF32, kAct>;
+  auto kern = gemm_kernel<BN, kOutF32, kAct, kRes>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -382,13 +431,21 @@ cudaError_t launch_act(int act, cudaStream_t stream, const CUtensorMap& ta, cons
                        int N, int K, int sms) {
   switch (act) {
     case ND_ACT_GELU_SIGMOID:
-      return launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+      return residual != nullptr
+                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
+                 : launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
     case ND_ACT_GELU_TANH:
-      return launch_typed<BN, kOutF32, ND_ACT_GELU_TANH>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+      return residual != nullptr
+                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_TANH, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
+                 : launch_typed<BN, kOutF32, ND_ACT_GELU_TANH, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
     case ND_ACT_GELU_ERF:
-      return launch_typed<BN, kOutF32, ND_ACT_GELU_ERF>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+      return residual != nullptr
+                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_ERF, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
+                 : launch_typed<BN, kOutF32, ND_ACT_GELU_ERF, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
     default:
-      return launch_typed<BN, kOutF32, ND_ACT_NONE>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+      return residual != nullptr
+                 ? launch_typed<BN, kOutF32, ND_ACT_NONE, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
+                 : launch_typed<BN, kOutF32, ND_ACT_NONE, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
   }
 }
 

@@ -158,6 +158,11 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Bring the global line holding `p` into L2 (no registers written).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // Order this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (UMMA operands written by threads).
 __device__ __forceinline__ void fence_async_shared() {
