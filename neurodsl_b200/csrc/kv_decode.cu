@@ -49,6 +49,13 @@ __device__ __forceinline__ uint4 ld_stream(const uint4* p) {
   return r;
 }
 
+// atomicAdd with acquire-release ordering at gpu scope; returns the old value.
+__device__ __forceinline__ unsigned int atom_add_acq_rel_gpu(unsigned int* p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 template <bool kOutF32>
 __device__ __forceinline__ void store_out(void* out, size_t idx, float v) {
   if constexpr (kOutF32) {
@@ -209,16 +216,18 @@ __global__ void __launch_bounds__(kThreads)
     mine->m = cm;
     mine->l = cl;
   }
-  __threadfence();
+  // The barrier orders this CTA's partial writes before thread 0's ticket
+  // increment, whose release (gpu scope, cumulative over what the barrier
+  // ordered) publishes them; the CTA that draws the last ticket acquires
+  // every earlier release, and its barrier orders the merge reads after it.
+  // One fence-carrying atomic per CTA instead of a fence in every thread.
   __syncthreads();
-
   __shared__ unsigned int s_ticket;
-  if (threadIdx.x == 0) s_ticket = atomicAdd(&tickets[bh], 1u);
+  if (threadIdx.x == 0) s_ticket = atom_add_acq_rel_gpu(&tickets[bh], 1u);
   __syncthreads();
   if (s_ticket != static_cast<unsigned int>(nchunks - 1)) return;
 
   // Last CTA of this head: merge every chunk's partial.
-  __threadfence();
   const ChunkPartial* all = partials + static_cast<size_t>(bh) * nchunks;
   float gm = -INFINITY;
   for (int c = 0; c < nchunks; ++c) gm = fmaxf(gm, __ldcg(&all[c].m));
