@@ -18,6 +18,10 @@
  *                       src/flash_attention.jl:116-134, reached from the
  *                       :flash_attn custom op _dispatch_flash_attn!
  *                       src/flash_attention.jl:175-200 (register_op! :203-208)
+ *   nd_flash_attn_fwd_strided  the same, plus MultiHeadFlashAttention's
+ *                       per-head :slice_cols / :hcat_heads copies
+ *                       src/flash_attention.jl:225-256 (read and written
+ *                       in place through strides)
  *   nd_kv_decode_attn   no reference counterpart (KV-cache decode is absent);
  *                       defined as flash_attn_fwd_cpu_simple!
  *                       (src/flash_attention.jl:49-69) with one query row
@@ -88,6 +92,24 @@ int nd_device_error(int *code);
 int nd_flash_attn_fwd(void *stream, const void *Q, const void *K, const void *V, void *O,
                       int o_dtype, float *lse, float *row_max, int B, int H, int Sq, int Sk,
                       int D, float scale, int causal);
+
+/*
+ * Attention prefill on strided tensors: the same computation as
+ * nd_flash_attn_fwd, with each of Q, K, V and O given as element strides
+ * {row, head, batch} (the D values of a row contiguous).  This reads an
+ * (S, H·D) projection output directly (token-major: {H·D, D, S·H·D}) and
+ * writes the (S, H·D) input of the output projection, replacing the per-head
+ * :slice_cols and the :hcat_heads of MultiHeadFlashAttention
+ * (src/flash_attention.jl:225-256, dispatch.jl:349-361,544-553).
+ *   Strides: positive multiples of 8 elements; the batch stride the largest
+ *   of a tensor's three; K and V both head-major (head stride > row stride)
+ *   or both token-major.  lse, row_max stay [B][H][Sq] contiguous.
+ */
+int nd_flash_attn_fwd_strided(void *stream, const void *Q, const int64_t *q_strides,
+                              const void *K, const int64_t *k_strides, const void *V,
+                              const int64_t *v_strides, void *O, const int64_t *o_strides,
+                              int o_dtype, float *lse, float *row_max, int B, int H, int Sq,
+                              int Sk, int D, float scale, int causal);
 
 /*
  * Scratch bytes needed by nd_kv_decode_attn for (B, H, L).  0 means the call

@@ -36,12 +36,15 @@ _i = ctypes.c_int
 _f = ctypes.c_float
 _fp = ctypes.POINTER(ctypes.c_float)
 _sz = ctypes.c_size_t
+_i64p = ctypes.POINTER(ctypes.c_int64)
 SIGNATURES = {
     "nd_version": (_i, []),
     "nd_last_error_string": (ctypes.c_char_p, []),
     "nd_device_check": (_i, [_i]),
     "nd_device_error": (_i, [ctypes.POINTER(_i)]),
     "nd_flash_attn_fwd": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _f, _i]),
+    "nd_flash_attn_fwd_strided": (_i, [_vp, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _i,
+                                       _vp, _vp, _i, _i, _i, _i, _i, _f, _i]),
     "nd_kv_decode_workspace_size": (_i, [_i, _i, _i, _i, ctypes.POINTER(_sz)]),
     "nd_kv_decode_attn": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i, _f,
                                _vp, _sz]),

@@ -200,26 +200,53 @@ __attribute__((visibility("default"))) int nd_device_error(int* code) {
   return ok();
 }
 
-__attribute__((visibility("default"))) int nd_flash_attn_fwd(void* stream, const void* Q,
-                                                             const void* K, const void* V, void* O,
-                                                             int o_dtype, float* lse,
-                                                             float* row_max, int B, int H, int Sq,
-                                                             int Sk, int D, float scale,
-                                                             int causal) {
+namespace {
+// Shared argument checks and launch of the two prefill entry points.
+// The stride of a dimension of extent 1 is never applied; give it a value
+// that passes the layout checks (head-major, batch outermost).
+void normalize_unit_strides(long long (&s)[3], int S, int H, int B) {
+  if (H == 1) s[1] = s[0] * (S > 0 ? S : 1);
+  if (B == 1) {
+    const long long a = s[0] * (S > 0 ? S : 1), b = s[1] * (H > 0 ? H : 1);
+    s[2] = a > b ? a : b;
+  }
+}
+
+int flash_attn_common(const char* fn, void* stream, const void* Q, const void* K, const void* V,
+                      void* O, int o_dtype, float* lse, float* row_max, int B, int H, int Sq,
+                      int Sk, int D, float scale, int causal, nd::FlashStrides st) {
+  normalize_unit_strides(st.q, Sq, H, B);
+  normalize_unit_strides(st.o, Sq, H, B);
+  normalize_unit_strides(st.k, Sk, H, B);
+  normalize_unit_strides(st.v, Sk, H, B);
   if (B < 0 || H < 0 || Sq < 0 || Sk < 0)
-    return fail(ND_ERR_INVALID_ARG, "nd_flash_attn_fwd: negative size (B=%d H=%d Sq=%d Sk=%d)", B, H, Sq, Sk);
-  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "nd_flash_attn_fwd: head_dim %d not supported (64 only)", D);
-  if (!valid_dtype(o_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_flash_attn_fwd: bad o_dtype %d", o_dtype);
+    return fail(ND_ERR_INVALID_ARG, "%s: negative size (B=%d H=%d Sq=%d Sk=%d)", fn, B, H, Sq, Sk);
+  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "%s: head_dim %d not supported (64 only)", fn, D);
+  if (!valid_dtype(o_dtype)) return fail(ND_ERR_UNSUPPORTED, "%s: bad o_dtype %d", fn, o_dtype);
   if (causal && Sq != Sk)
-    return fail(ND_ERR_SHAPE, "nd_flash_attn_fwd: causal attention needs Sq == Sk (got %d, %d)", Sq, Sk);
+    return fail(ND_ERR_SHAPE, "%s: causal attention needs Sq == Sk (got %d, %d)", fn, Sq, Sk);
   if (!causal && Sk == 0 && Sq > 0)
-    return fail(ND_ERR_SHAPE, "nd_flash_attn_fwd: no keys (Sk = 0) for %d queries", Sq);
+    return fail(ND_ERR_SHAPE, "%s: no keys (Sk = 0) for %d queries", fn, Sq);
   if (static_cast<long long>(B) * H * ((Sq + 127) / 128) > 0x7fffffffLL)
-    return fail(ND_ERR_SHAPE, "nd_flash_attn_fwd: grid too large");
+    return fail(ND_ERR_SHAPE, "%s: grid too large", fn);
   if (B == 0 || H == 0 || Sq == 0) return ok();
-  if (!Q || !K || !V || !O) return fail(ND_ERR_INVALID_ARG, "nd_flash_attn_fwd: null tensor pointer");
+  if (!Q || !K || !V || !O) return fail(ND_ERR_INVALID_ARG, "%s: null tensor pointer", fn);
   if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
-    return fail(ND_ERR_ALIGNMENT, "nd_flash_attn_fwd: Q/K/V/O must be 16-byte aligned");
+    return fail(ND_ERR_ALIGNMENT, "%s: Q/K/V/O must be 16-byte aligned", fn);
+  const long long* all[4] = {st.q, st.k, st.v, st.o};
+  const char* names = "QKVO";
+  for (int t = 0; t < 4; ++t) {
+    for (int i = 0; i < 3; ++i) {
+      const long long x = all[t][i];
+      if (x <= 0 || x % 8 != 0 || x >= (1LL << 38))
+        return fail(ND_ERR_SHAPE, "%s: %c stride[%d] = %lld must be a positive multiple of 8 elements below 2^38",
+                    fn, names[t], i, x);
+    }
+    if (t < 3 && all[t][2] < (all[t][0] > all[t][1] ? all[t][0] : all[t][1]))
+      return fail(ND_ERR_SHAPE, "%s: %c batch stride must be the outermost (>= row and head strides)", fn, names[t]);
+  }
+  if ((st.k[1] < st.k[0]) != (st.v[1] < st.v[0]))
+    return fail(ND_ERR_SHAPE, "%s: K and V must share one layout (both head-major or both token-major)", fn);
   int rc = check_current_device(nullptr);
   if (rc) return rc;
   const char* msg = nullptr;
@@ -227,9 +254,38 @@ __attribute__((visibility("default"))) int nd_flash_attn_fwd(void* stream, const
                                        static_cast<const __nv_bfloat16*>(Q),
                                        static_cast<const __nv_bfloat16*>(K),
                                        static_cast<const __nv_bfloat16*>(V), O, o_dtype == ND_F32,
-                                       lse, row_max, B, H, Sq, Sk, scale, causal != 0, &msg);
-  if (e != cudaSuccess) return cuda_fail(e, "nd_flash_attn_fwd", msg);
+                                       lse, row_max, B, H, Sq, Sk, scale, causal != 0, st, &msg);
+  if (e != cudaSuccess) return cuda_fail(e, fn, msg);
   return ok();
+}
+}  // namespace
+
+__attribute__((visibility("default"))) int nd_flash_attn_fwd(void* stream, const void* Q,
+                                                             const void* K, const void* V, void* O,
+                                                             int o_dtype, float* lse,
+                                                             float* row_max, int B, int H, int Sq,
+                                                             int Sk, int D, float scale,
+                                                             int causal) {
+  return flash_attn_common("nd_flash_attn_fwd", stream, Q, K, V, O, o_dtype, lse, row_max, B, H,
+                           Sq, Sk, D, scale, causal,
+                           nd::flash_head_major_strides(H < 1 ? 1 : H, Sq, Sk));
+}
+
+__attribute__((visibility("default"))) int nd_flash_attn_fwd_strided(
+    void* stream, const void* Q, const int64_t* q_strides, const void* K, const int64_t* k_strides,
+    const void* V, const int64_t* v_strides, void* O, const int64_t* o_strides, int o_dtype,
+    float* lse, float* row_max, int B, int H, int Sq, int Sk, int D, float scale, int causal) {
+  if (!q_strides || !k_strides || !v_strides || !o_strides)
+    return fail(ND_ERR_INVALID_ARG, "nd_flash_attn_fwd_strided: null stride array");
+  nd::FlashStrides st;
+  for (int i = 0; i < 3; ++i) {
+    st.q[i] = q_strides[i];
+    st.k[i] = k_strides[i];
+    st.v[i] = v_strides[i];
+    st.o[i] = o_strides[i];
+  }
+  return flash_attn_common("nd_flash_attn_fwd_strided", stream, Q, K, V, O, o_dtype, lse, row_max,
+                           B, H, Sq, Sk, D, scale, causal, st);
 }
 
 __attribute__((visibility("default"))) int nd_kv_decode_workspace_size(int B, int H, int L, int D,

@@ -199,6 +199,26 @@ __device__ __forceinline__ WorkItem decode_item(int k, int BH, int n_blk, int n_
   return w;
 }
 
+// Where one (batch, head)'s rows live.  Q, K and V are read through 4-D
+// tensor maps whose dims are {64, S, H, B} (head-major) or {64, H, S, B}
+// (token-major: rows of all heads interleaved, as a projection writes them);
+// either way a box is 128 rows of 128 bytes, the same shared-memory tile.
+struct FlashLayout {
+  int H;                 // heads; bh = b * H + h
+  int q_token_major;     // Q map dims {64, H, S, B}
+  int kv_token_major;    // K and V maps dims {64, H, S, B}
+  long long o_s, o_h, o_b;  // output element strides of a row, a head, a batch
+};
+
+// 128 rows starting at `row` of head h, batch b, into one shared tile.
+__device__ __forceinline__ void load_rows(const CUtensorMap* map, uint64_t* bar, void* dst,
+                                          int row, int h, int b, int token_major) {
+  if (token_major)
+    tma_load_4d(map, bar, dst, 0, h, row, b);
+  else
+    tma_load_4d(map, bar, dst, 0, row, h, b);
+}
+
 // The n-th item of CTA `cta` out of `grid` persistent CTAs: items are visited
 // in rounds of `grid`, alternating direction so each CTA's heavy and light
 // items pair up (the cost list is sorted heaviest first).
@@ -206,11 +226,14 @@ __device__ __forceinline__ int item_of(int n, int cta, int grid) {
   return n * grid + ((n & 1) ? (grid - 1 - cta) : cta);
 }
 
-template <bool kCausal, bool kOutF32>
+// kStrided: Q/K/V through 4-D maps and O through FlashLayout strides; the
+// contiguous head-major case keeps 3-D maps {64, S, B·H} and bh·S row offsets.
+template <bool kCausal, bool kOutF32, bool kStrided>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, void* __restrict__ out,
+                     const FlashLayout lay,
                      float* __restrict__ lse_out, float* __restrict__ max_out, int BH, int Sq,
                      int Sk, float scale_log2, int* __restrict__ err_word) {
   extern __shared__ uint8_t smem_raw[];
@@ -272,10 +295,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        const int h = kStrided ? w.bh % lay.H : 0, b = kStrided ? w.bh / lay.H : 0;
         mbar_arrive_expect_tx(&bars->q_full[qb], kTiles * kTileBytes);
-        for (int i = 0; i < kTiles; ++i)
-          tma_load_3d(&tm_q, &bars->q_full[qb], smem + kOffQ + (qb * kTiles + i) * kTileBytes, 0,
-                      w.blk * kRowsPerCta + i * kBM, w.bh);
+        for (int i = 0; i < kTiles; ++i) {
+          void* dst = smem + kOffQ + (qb * kTiles + i) * kTileBytes;
+          const int row = w.blk * kRowsPerCta + i * kBM;
+          if constexpr (kStrided)
+            load_rows(&tm_q, &bars->q_full[qb], dst, row, h, b, lay.q_token_major);
+          else
+            tma_load_3d(&tm_q, &bars->q_full[qb], dst, 0, row, w.bh);
+        }
         for (int j = 0; j < w.n_total; ++j, ++kv_it) {
           const int s = kv_it % kStages;
           if (kv_it >= kStages &&
@@ -284,8 +313,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
-          tma_load_3d(&tm_k, &bars->kv_full[s], smem + kOffK + s * kTileBytes, 0, j * kBN, w.bh);
-          tma_load_3d(&tm_v, &bars->kv_full[s], smem + kOffV + s * kTileBytes, 0, j * kBN, w.bh);
+          if constexpr (kStrided) {
+            load_rows(&tm_k, &bars->kv_full[s], smem + kOffK + s * kTileBytes, j * kBN, h, b,
+                      lay.kv_token_major);
+            load_rows(&tm_v, &bars->kv_full[s], smem + kOffV + s * kTileBytes, j * kBN, h, b,
+                      lay.kv_token_major);
+          } else {
+            tma_load_3d(&tm_k, &bars->kv_full[s], smem + kOffK + s * kTileBytes, 0, j * kBN, w.bh);
+            tma_load_3d(&tm_v, &bars->kv_full[s], smem + kOffV + s * kTileBytes, 0, j * kBN, w.bh);
+          }
         }
       }
       if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutProducer);
@@ -502,9 +538,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (q_idx < Sq) {
         const float inv_l = 1.f / l_row;
         const size_t row_off = static_cast<size_t>(w.bh) * Sq + q_idx;
+        const long long o_off =
+            kStrided ? (w.bh / lay.H) * lay.o_b + (w.bh % lay.H) * lay.o_h +
+                           static_cast<long long>(q_idx) * lay.o_s
+                     : static_cast<long long>(row_off) * kD;
         constexpr int kCols = kOutCols;
         if constexpr (kOutF32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + row_off * kD +
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + o_off +
                                                   half * kCols);
 #pragma unroll
           for (int c = 0; c < kCols / 4; ++c)
@@ -513,7 +553,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  __uint_as_float(orr[4 * c + 2]) * inv_l,
                                  __uint_as_float(orr[4 * c + 3]) * inv_l);
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + row_off * kD +
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + o_off +
                                                 half * kCols);
 #pragma unroll
           for (int c = 0; c < kCols / 8; ++c)
@@ -540,11 +580,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool kCausal, bool kOutF32>
+template <bool kCausal, bool kOutF32, bool kStrided>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUtensorMap& tk,
-                         const CUtensorMap& tv, void* out, float* lse, float* mx, int BH, int Sq,
-                         int Sk, float scale_log2) {
-  auto kern = flash_fwd_kernel<kCausal, kOutF32>;
+                         const CUtensorMap& tv, void* out, const FlashLayout& lay, float* lse,
+                         float* mx, int BH, int Sq, int Sk, float scale_log2) {
+  auto kern = flash_fwd_kernel<kCausal, kOutF32, kStrided>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -555,42 +595,97 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUten
   if (e != cudaSuccess) return e;
   const int n_items = ceil_div(Sq, kRowsPerCta) * BH;
   dim3 grid(n_items < sms ? n_items : sms);
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, out, lse, mx, BH, Sq, Sk, scale_log2,
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, out, lay, lse, mx, BH, Sq, Sk, scale_log2,
                                                device_error_word());
   return cudaGetLastError();
 }
 
 }  // namespace
 
+FlashStrides flash_head_major_strides(int H, int Sq, int Sk) {
+  FlashStrides st;
+  const long long q[3] = {kD, static_cast<long long>(Sq) * kD, static_cast<long long>(H) * Sq * kD};
+  const long long k[3] = {kD, static_cast<long long>(Sk) * kD, static_cast<long long>(H) * Sk * kD};
+  for (int i = 0; i < 3; ++i) {
+    st.q[i] = q[i];
+    st.o[i] = q[i];
+    st.k[i] = k[i];
+    st.v[i] = k[i];
+  }
+  return st;
+}
+
+namespace {
+// 4-D map over rows of S positions x H heads x B batches, 64 bf16 per row;
+// the row and head dims are ordered by stride (a tensor map's dims go from
+// the finest stride outwards).  Returns whether the head dim is the inner one.
+cudaError_t make_rows_map(CUtensorMap* map, const void* base, int S, int H, int B,
+                          const long long (&st)[3], int* token_major, const char** err_msg) {
+  const bool tok = st[1] < st[0];
+  const uint64_t s = static_cast<uint64_t>(S), h = static_cast<uint64_t>(H);
+  const uint64_t dims[4] = {kD, tok ? h : s, tok ? s : h, static_cast<uint64_t>(B)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(tok ? st[1] : st[0]) * 2,
+                               static_cast<uint64_t>(tok ? st[0] : st[1]) * 2,
+                               static_cast<uint64_t>(st[2]) * 2};
+  const uint32_t box[4] = {kD, tok ? 1u : static_cast<uint32_t>(kBM), tok ? static_cast<uint32_t>(kBM) : 1u, 1};
+  *token_major = tok ? 1 : 0;
+  return make_tmap_bf16_sw128(map, base, 4, dims, strides, box, err_msg);
+}
+}  // namespace
+
 cudaError_t launch_flash_fwd(cudaStream_t stream, const __nv_bfloat16* Q, const __nv_bfloat16* K,
                              const __nv_bfloat16* V, void* O, bool out_f32, float* lse,
                              float* row_max, int B, int H, int Sq, int Sk, float scale,
-                             bool causal, const char** err_msg) {
+                             bool causal, const FlashStrides& st, const char** err_msg) {
   const int BH = B * H;
   if (BH == 0 || Sq == 0) return cudaSuccess;
   CUtensorMap tq, tk, tv;
-  const uint32_t box[3] = {kD, kBM, 1};
-  {
-    const uint64_t dims[3] = {kD, static_cast<uint64_t>(Sq), static_cast<uint64_t>(BH)};
-    const uint64_t strides[2] = {kD * 2, static_cast<uint64_t>(Sq) * kD * 2};
-    cudaError_t e = make_tmap_bf16_sw128(&tq, Q, 3, dims, strides, box, err_msg);
+  FlashLayout lay;
+  lay.H = H;
+  lay.o_s = st.o[0];
+  lay.o_h = st.o[1];
+  lay.o_b = st.o[2];
+  lay.q_token_major = lay.kv_token_major = 0;
+  const FlashStrides hm = flash_head_major_strides(H, Sq, Sk);
+  bool strided = false;
+  for (int i = 0; i < 3; ++i)
+    strided = strided || st.q[i] != hm.q[i] || st.k[i] != hm.k[i] || st.v[i] != hm.v[i] ||
+              st.o[i] != hm.o[i];
+  cudaError_t e = cudaSuccess;
+  if (strided) {
+    int k_tok = 0, v_tok = 0;
+    e = make_rows_map(&tq, Q, Sq, H, B, st.q, &lay.q_token_major, err_msg);
+    if (e == cudaSuccess) e = make_rows_map(&tk, K, Sk, H, B, st.k, &k_tok, err_msg);
+    if (e == cudaSuccess) e = make_rows_map(&tv, V, Sk, H, B, st.v, &v_tok, err_msg);
     if (e != cudaSuccess) return e;
-  }
-  {
-    const uint64_t dims[3] = {kD, static_cast<uint64_t>(Sk), static_cast<uint64_t>(BH)};
-    const uint64_t strides[2] = {kD * 2, static_cast<uint64_t>(Sk) * kD * 2};
-    cudaError_t e = make_tmap_bf16_sw128(&tk, K, 3, dims, strides, box, err_msg);
-    if (e != cudaSuccess) return e;
-    e = make_tmap_bf16_sw128(&tv, V, 3, dims, strides, box, err_msg);
+    if (k_tok != v_tok) {
+      if (err_msg) *err_msg = "K and V must share one layout (both head-major or both token-major)";
+      return cudaErrorInvalidValue;
+    }
+    lay.kv_token_major = k_tok;
+  } else {
+    // contiguous head-major: 3-D maps {64, S, B·H}, so a ragged S is
+    // zero-filled per head, never read from the next head
+    const uint32_t box[3] = {kD, kBM, 1};
+    const uint64_t qdims[3] = {kD, static_cast<uint64_t>(Sq), static_cast<uint64_t>(BH)};
+    const uint64_t qstr[2] = {kD * 2, static_cast<uint64_t>(Sq) * kD * 2};
+    const uint64_t kdims[3] = {kD, static_cast<uint64_t>(Sk), static_cast<uint64_t>(BH)};
+    const uint64_t kstr[2] = {kD * 2, static_cast<uint64_t>(Sk) * kD * 2};
+    e = make_tmap_bf16_sw128(&tq, Q, 3, qdims, qstr, box, err_msg);
+    if (e == cudaSuccess) e = make_tmap_bf16_sw128(&tk, K, 3, kdims, kstr, box, err_msg);
+    if (e == cudaSuccess) e = make_tmap_bf16_sw128(&tv, V, 3, kdims, kstr, box, err_msg);
     if (e != cudaSuccess) return e;
   }
   const float sl2 = scale * kLog2e;
-  if (causal) {
-    return out_f32 ? launch_typed<true, true>(stream, tq, tk, tv, O, lse, row_max, BH, Sq, Sk, sl2)
-                   : launch_typed<true, false>(stream, tq, tk, tv, O, lse, row_max, BH, Sq, Sk, sl2);
+#define ND_FLASH_LAUNCH(C, F, S_)                                                              \
+  launch_typed<C, F, S_>(stream, tq, tk, tv, O, lay, lse, row_max, BH, Sq, Sk, sl2)
+  if (strided) {
+    if (causal) return out_f32 ? ND_FLASH_LAUNCH(true, true, true) : ND_FLASH_LAUNCH(true, false, true);
+    return out_f32 ? ND_FLASH_LAUNCH(false, true, true) : ND_FLASH_LAUNCH(false, false, true);
   }
-  return out_f32 ? launch_typed<false, true>(stream, tq, tk, tv, O, lse, row_max, BH, Sq, Sk, sl2)
-                 : launch_typed<false, false>(stream, tq, tk, tv, O, lse, row_max, BH, Sq, Sk, sl2);
+  if (causal) return out_f32 ? ND_FLASH_LAUNCH(true, true, false) : ND_FLASH_LAUNCH(true, false, false);
+  return out_f32 ? ND_FLASH_LAUNCH(false, true, false) : ND_FLASH_LAUNCH(false, false, false);
+#undef ND_FLASH_LAUNCH
 }
 
 }  // namespace nd

@@ -241,6 +241,8 @@ def _infer_output_shape(op: str, inputs, attrs):
         return (inputs[0].shape[0], sum(x.shape[1] for x in inputs))
     if op == "slice_cols":
         return (inputs[0].shape[0], attrs["end_col"] - attrs["start_col"] + 1)
+    if op == "flash_attention" and len(inputs) == 1:
+        return (inputs[0].shape[0], inputs[0].shape[1] // 3)   # fused (S, 3d) projection
     if op in ("add", "identity", "flash_attn", "flash_attention", "layernorm", "gelu"):
         return tuple(inputs[0].shape)
     if op == "kv_decode_attn":
@@ -422,36 +424,56 @@ def _dispatch_flash_attn(dev, output_buffer, inputs, attrs, out_sym, out_node, c
     return output_buffer
 
 
-def _heads_major(x, S, H, D):
-    """(S, H·D) row-major -> [1][H][S][D] bf16 (the per-head :slice_cols of
-    src/flash_attention.jl:241-246 done as one device transpose)."""
-    return _bf16_rows(x).view(S, H, D).permute(1, 0, 2).contiguous().view(1, H, S, D)
+def _token_major_view(x, S, H, D):
+    """An (S, H·D) row-major matrix seen as [1][H][S][D] without copying: the
+    per-head :slice_cols of src/flash_attention.jl:241-246 become strides."""
+    return x.view(S, H, D).permute(1, 0, 2).unsqueeze(0)
 
 
 def _dispatch_flash_attention(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
     """:flash_attention — all heads of q_full/k_full/v_full (S, H·D) in one
     launch; replaces H × (3 :slice_cols + :flash_attn) and :hcat_heads
-    (src/flash_attention.jl:232-256)."""
-    q, k, v = inputs[0], inputs[1], inputs[2]
-    S, d = q.shape
+    (src/flash_attention.jl:232-256).  The kernel reads the projections and
+    writes the (S, H·D) output in place through strides."""
     H = attrs["n_heads"]
-    D = attrs.get("d_head", d // H)
     causal = attrs.get("causal", True)
-    if H * D != d:
-        raise NeuroDSLError(2, f"n_heads {H} x d_head {D} != dim {d}")
-    Sk = k.shape[0]
-    q4 = _heads_major(q, S, H, D)
-    k4 = _heads_major(k, Sk, H, D)
-    v4 = _heads_major(v, Sk, H, D)
-    o4, lse, m = ops.flash_attn_fwd(q4, k4, v4, causal=causal, scale=1.0 / math.sqrt(D),
-                                    out_dtype=output_buffer.dtype)
-    output_buffer.copy_(o4.view(H, S, D).permute(1, 0, 2).reshape(S, d))
-    out_node.aux_data["flash_l"] = lse.view(H, S)
-    out_node.aux_data["flash_m"] = m.view(H, S)
+    if len(inputs) == 1:
+        # one fused projection [q | k | v] of shape (S, 3·H·D)
+        qkv = _bf16_rows(inputs[0])
+        S, d3 = qkv.shape
+        d = d3 // 3
+        D = attrs.get("d_head", d // H)
+        if 3 * H * D != d3:
+            raise NeuroDSLError(2, f"fused qkv width {d3} != 3 x n_heads {H} x d_head {D}")
+        parts = qkv.view(S, 3, H, D).permute(1, 2, 0, 3).unsqueeze(1)  # [3][1][H][S][D]
+        q4, k4, v4 = parts[0], parts[1], parts[2]
+        q = k = v = inputs[0]
+        Sk = S
+    else:
+        q, k, v = inputs[0], inputs[1], inputs[2]
+        S, d = q.shape
+        D = attrs.get("d_head", d // H)
+        if H * D != d:
+            raise NeuroDSLError(2, f"n_heads {H} x d_head {D} != dim {d}")
+        Sk = k.shape[0]
+        q4 = _token_major_view(_bf16_rows(q), S, H, D)
+        k4 = _token_major_view(_bf16_rows(k), Sk, H, D)
+        v4 = _token_major_view(_bf16_rows(v), Sk, H, D)
+    lse = out_node.aux_data.get("flash_l")
+    if lse is None or tuple(lse.shape) != (H, S):
+        lse = torch.empty((H, S), dtype=torch.float32, device=dev.torch_device)
+        out_node.aux_data["flash_l"] = lse
+        out_node.aux_data["flash_m"] = torch.empty_like(lse)
+    m = out_node.aux_data["flash_m"]
+    buf, aliased = _alias_safe(output_buffer, out_node, inputs)
+    ops.flash_attn_fwd(q4, k4, v4, causal=causal, scale=1.0 / math.sqrt(D),
+                       out=_token_major_view(buf, S, H, D), lse=lse.view(1, H, S),
+                       row_max=m.view(1, H, S))
+    if aliased:
+        output_buffer.copy_(buf)
     _store_ctx(ctx_store, out_sym, {"Q": q, "K": k, "V": v, "out": output_buffer,
-                                    "l": out_node.aux_data["flash_l"],
-                                    "m": out_node.aux_data["flash_m"], "d_head": D,
-                                    "causal": causal, "n_heads": H})
+                                    "l": lse, "m": m, "d_head": D, "causal": causal,
+                                    "n_heads": H})
     return output_buffer
 
 

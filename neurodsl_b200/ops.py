@@ -29,15 +29,22 @@ def _stream(stream=None):
     return ctypes.c_void_p(s.cuda_stream)
 
 
-def _need(t, name, dtype=None, dims=None):
+def _need(t, name, dtype=None, dims=None, contiguous=True):
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise TypeError(f"{name} must be a CUDA tensor")
     if dtype is not None and t.dtype != dtype:
         raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
     if dims is not None and t.dim() != dims:
         raise ValueError(f"{name} must have {dims} dims, got shape {tuple(t.shape)}")
-    if not t.is_contiguous():
+    if contiguous and not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
+
+
+def _row_strides(t, name):
+    """{row, head, batch} element strides of a [B][H][S][64] view, D contiguous."""
+    if t.stride(3) != 1:
+        raise ValueError(f"{name}: the 64 head dims of a row must be contiguous")
+    return (ctypes.c_int64 * 3)(t.stride(2), t.stride(1), t.stride(0))
 
 
 def flash_attn_fwd(Q, K, V, causal=True, scale=None, out=None, out_dtype=torch.bfloat16,
@@ -46,10 +53,13 @@ def flash_attn_fwd(Q, K, V, causal=True, scale=None, out=None, out_dtype=torch.b
 
     Mirrors flash_attn_fwd!(dev, out, Q, K, V, d_head; causal)
     (src/flash_attention.jl:113-134); returns (O, lse, row_max) like the
-    reference's (out, l, m).
+    reference's (out, l, m).  Q, K, V and `out` may be strided views, e.g.
+    token-major slices of an (S, 3·H·64) QKV projection viewed as
+    [B][H][S][64]; they are then read and written in place
+    (nd_flash_attn_fwd_strided) instead of being copied per head.
     """
     for n, t in (("Q", Q), ("K", K), ("V", V)):
-        _need(t, n, torch.bfloat16, 4)
+        _need(t, n, torch.bfloat16, 4, contiguous=False)
     B, H, Sq, D = Q.shape
     Sk = K.shape[2]
     if K.shape != (B, H, Sk, D) or V.shape != K.shape:
@@ -58,14 +68,23 @@ def flash_attn_fwd(Q, K, V, causal=True, scale=None, out=None, out_dtype=torch.b
         scale = 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty((B, H, Sq, D), dtype=out_dtype, device=Q.device)
-    _need(out, "out", None, 4)
+    _need(out, "out", None, 4, contiguous=False)
+    if tuple(out.shape) != (B, H, Sq, D):
+        raise ValueError(f"out{tuple(out.shape)} != {(B, H, Sq, D)}")
     if lse is None:
         lse = torch.empty((B, H, Sq), dtype=torch.float32, device=Q.device)
     if row_max is None:
         row_max = torch.empty((B, H, Sq), dtype=torch.float32, device=Q.device)
-    check(_lib.load().nd_flash_attn_fwd(_stream(stream), _ptr(Q), _ptr(K), _ptr(V), _ptr(out),
-                                        _DT[out.dtype], _ptr(lse), _ptr(row_max), B, H, Sq, Sk,
-                                        D, float(scale), int(bool(causal))))
+    lib = _lib.load()
+    if all(t.is_contiguous() for t in (Q, K, V, out)):
+        check(lib.nd_flash_attn_fwd(_stream(stream), _ptr(Q), _ptr(K), _ptr(V), _ptr(out),
+                                    _DT[out.dtype], _ptr(lse), _ptr(row_max), B, H, Sq, Sk,
+                                    D, float(scale), int(bool(causal))))
+    else:
+        check(lib.nd_flash_attn_fwd_strided(
+            _stream(stream), _ptr(Q), _row_strides(Q, "Q"), _ptr(K), _row_strides(K, "K"),
+            _ptr(V), _row_strides(V, "V"), _ptr(out), _row_strides(out, "out"), _DT[out.dtype],
+            _ptr(lse), _ptr(row_max), B, H, Sq, Sk, D, float(scale), int(bool(causal))))
     return out, lse, row_max
 
 

@@ -72,6 +72,27 @@ def test_multihead_flash_attention_rule():
         check(out[:, sl], o_ref)
 
 
+def test_multihead_flash_attention_fused_qkv():
+    """One (S, 3·H·D) projection as the single input: q, k, v are read from
+    its column blocks in place."""
+    g_ = G()
+    rng = np.random.default_rng(5)
+    S, Hh, D = 200, 4, 64
+    qkv = oracle.bf16_round(rng.standard_normal((S, 3 * Hh * D), dtype=np.float32))
+    g = g_.NeuroGraph()
+    g_.set_(g, "qkv", qkv)
+    g_.addrule(g, g_.GraphRule("attn", ["qkv"], "flash_attention",
+                               {"n_heads": Hh, "causal": True}))
+    out = g_.demand(g, "attn").cpu().numpy()
+    assert out.shape == (S, Hh * D)
+    d = Hh * D
+    for h in range(Hh):
+        sl = slice(h * D, (h + 1) * D)
+        o_ref, _, _ = oracle.attn_simple(qkv[:, sl], qkv[:, d:][:, sl], qkv[:, 2 * d:][:, sl],
+                                         causal=True)
+        check(out[:, sl], o_ref)
+
+
 def build_block(g_, g, x, params, n_heads):
     """Pre-LN causal block from GraphRules:
     LN -> Q,K,V linear -> multi-head causal flash attention -> out-proj + x
