@@ -35,6 +35,12 @@
  *                       src/kernels.jl:48-64,104-131, used by :rmsnorm
  *                       src/dispatch.jl:426-438)
  *   nd_convert_2d       Backend.to_device / Array() copies, src/backend.jl:20-26
+ *   nd_embed            :embedding src/dispatch.jl:476-491 (on the device) plus the
+ *                       learned-position add of the GPT-2 graph
+ *   nd_argmax           the greedy argmax over LM-head logits (:matmul trans_b
+ *                       src/dispatch.jl:213-243 feeds it)
+ *   nd_kv_store         no reference counterpart (prefill fills the decode cache)
+ *   nd_add_layernorm    residual :add src/dispatch.jl:386-417 + :layernorm
  */
 #ifndef NEURODSL_B200_H
 #define NEURODSL_B200_H
@@ -192,6 +198,44 @@ int nd_layernorm(void *stream, const void *x, int x_dtype, const float *gamma, c
  */
 int nd_convert_2d(void *stream, const void *src, int src_dtype, int src_col_major, void *dst,
                   int dst_dtype, int rows, int cols);
+
+/*
+ * Token embedding with learned positions: y[t] = wte[ids[t]] + wpe[pos[t]].
+ *   ids, pos int32 [T] (pos NULL: no position add); wte [vocab][d], wpe
+ *   [n_pos][d], y [T][d] bf16; d % 8 == 0.  An id or position out of range
+ *   gives a zero row and sets the device error word (nd_device_error).
+ */
+int nd_embed(void *stream, const int32_t *ids, const int32_t *pos, const void *wte,
+             const void *wpe, void *y, int T, int d, int vocab, int n_pos);
+
+/*
+ * Greedy decoding: idx[r] = the first index of the largest value of logits
+ * row r (rows x V, row stride ld elements, ND_BF16 or ND_F32), val[r] that
+ * value (val may be NULL).  NaN never wins over a number.
+ */
+int nd_argmax(void *stream, const void *logits, int dtype, int64_t ld, int rows, int V,
+              int32_t *idx, float *val);
+
+/*
+ * Prefill cache fill: the K and V rows of token (b, s) at columns k_col and
+ * v_col of src [B·S][ld] bf16 (a QKV projection) are written to position
+ * pos0 + s of k_cache, v_cache [B][H][L_max][D] bf16.  D must be 64; ld,
+ * k_col and v_col multiples of 8; pos0 + S <= L_max.
+ */
+int nd_kv_store(void *stream, const void *src, int64_t ld, int k_col, int v_col, void *k_cache,
+                void *v_cache, int B, int S, int H, int L_max, int pos0, int D);
+
+/*
+ * Residual add fused with the next LayerNorm (the residual :add
+ * src/dispatch.jl:386-417 followed by :layernorm):
+ *   s = x + p (+ bias),  y = (s - mean) / sqrt(var + eps) * gamma + beta
+ *   x, s_out, y [rows][d] bf16 (s_out may be x); p [rows][d] in p_dtype
+ *   (e.g. an all-reduced partial sum); bias, gamma, beta fp32 [d] or NULL.
+ *   d % 8 == 0, d <= 2048.
+ */
+int nd_add_layernorm(void *stream, const void *x, const void *p, int p_dtype, const float *bias,
+                     const float *gamma, const float *beta, void *s_out, void *y, int rows,
+                     int d, float eps);
 
 #ifdef __cplusplus
 }

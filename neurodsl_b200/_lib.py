@@ -54,6 +54,10 @@ SIGNATURES = {
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
     "nd_layernorm": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _f]),
     "nd_convert_2d": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i]),
+    "nd_embed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),
+    "nd_argmax": (_i, [_vp, _vp, _i, ctypes.c_int64, _i, _i, _vp, _vp]),
+    "nd_kv_store": (_i, [_vp, _vp, ctypes.c_int64, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i]),
+    "nd_add_layernorm": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _f]),
 }
 
 

@@ -19,6 +19,7 @@
 #include "gemm.h"
 #include "kv_decode.h"
 #include "layernorm.h"
+#include "model_ops.h"
 
 namespace {
 // Device error word: one int per device (a __device__ variable exists once
@@ -482,6 +483,93 @@ __attribute__((visibility("default"))) int nd_convert_2d(void* stream, const voi
   else if (dst_dtype == ND_F32) e = launch_convert<__nv_bfloat16, float>(st, src, dst, rows, cols, cm);
   else e = launch_convert<__nv_bfloat16, __nv_bfloat16>(st, src, dst, rows, cols, cm);
   if (e != cudaSuccess) return cuda_fail(e, "nd_convert_2d");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_embed(void* stream, const int32_t* ids,
+                                                    const int32_t* pos, const void* wte,
+                                                    const void* wpe, void* y, int T, int d,
+                                                    int vocab, int n_pos) {
+  if (T < 0 || d < 0 || vocab < 0 || n_pos < 0) return fail(ND_ERR_INVALID_ARG, "nd_embed: negative size");
+  if (d % 8 != 0) return fail(ND_ERR_SHAPE, "nd_embed: d = %d must be a multiple of 8", d);
+  if (T == 0 || d == 0) return ok();
+  if (!ids || !wte || !y || (pos && !wpe)) return fail(ND_ERR_INVALID_ARG, "nd_embed: null pointer");
+  if (!aligned16(wte) || !aligned16(y) || (wpe && !aligned16(wpe)))
+    return fail(ND_ERR_ALIGNMENT, "nd_embed: wte/wpe/y must be 16-byte aligned");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_embed(static_cast<cudaStream_t>(stream), ids, pos,
+                                   static_cast<const __nv_bfloat16*>(wte),
+                                   static_cast<const __nv_bfloat16*>(wpe),
+                                   static_cast<__nv_bfloat16*>(y), T, d, vocab, n_pos,
+                                   nd::device_error_word());
+  if (e != cudaSuccess) return cuda_fail(e, "nd_embed");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_argmax(void* stream, const void* logits, int dtype,
+                                                     int64_t ld, int rows, int V, int32_t* idx,
+                                                     float* val) {
+  if (rows < 0 || V < 0) return fail(ND_ERR_INVALID_ARG, "nd_argmax: negative size");
+  if (!valid_dtype(dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_argmax: bad dtype %d", dtype);
+  if (ld < V) return fail(ND_ERR_SHAPE, "nd_argmax: ld %lld < V %d", static_cast<long long>(ld), V);
+  if (rows == 0) return ok();
+  if (V == 0) return fail(ND_ERR_SHAPE, "nd_argmax: empty rows (V = 0)");
+  if (!logits || !idx) return fail(ND_ERR_INVALID_ARG, "nd_argmax: null pointer");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_argmax(static_cast<cudaStream_t>(stream), logits, dtype == ND_F32, ld,
+                                    rows, V, idx, val);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_argmax");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_kv_store(void* stream, const void* src, int64_t ld,
+                                                       int k_col, int v_col, void* k_cache,
+                                                       void* v_cache, int B, int S, int H,
+                                                       int L_max, int pos0, int D) {
+  if (B < 0 || S < 0 || H < 0 || L_max < 0 || pos0 < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_store: negative size");
+  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "nd_kv_store: head_dim %d not supported (64 only)", D);
+  if (pos0 + static_cast<long long>(S) > L_max)
+    return fail(ND_ERR_SHAPE, "nd_kv_store: pos0 %d + S %d exceeds L_max %d", pos0, S, L_max);
+  if (ld % 8 || k_col % 8 || v_col % 8 || k_col < 0 || v_col < 0 ||
+      k_col + static_cast<long long>(H) * 64 > ld || v_col + static_cast<long long>(H) * 64 > ld)
+    return fail(ND_ERR_SHAPE, "nd_kv_store: columns k=%d v=%d (+%d) must be multiples of 8 inside ld=%lld",
+                k_col, v_col, H * 64, static_cast<long long>(ld));
+  if (B == 0 || S == 0 || H == 0) return ok();
+  if (!src || !k_cache || !v_cache) return fail(ND_ERR_INVALID_ARG, "nd_kv_store: null pointer");
+  if (!aligned16(src) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(ND_ERR_ALIGNMENT, "nd_kv_store: tensors must be 16-byte aligned");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_kv_store(static_cast<cudaStream_t>(stream),
+                                      static_cast<const __nv_bfloat16*>(src), ld, k_col, v_col,
+                                      static_cast<__nv_bfloat16*>(k_cache),
+                                      static_cast<__nv_bfloat16*>(v_cache), B, S, H, L_max, pos0);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_kv_store");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_add_layernorm(void* stream, const void* x,
+                                                            const void* p, int p_dtype,
+                                                            const float* bias, const float* gamma,
+                                                            const float* beta, void* s_out,
+                                                            void* y, int rows, int d, float eps) {
+  if (rows < 0 || d < 0) return fail(ND_ERR_INVALID_ARG, "nd_add_layernorm: negative size");
+  if (!valid_dtype(p_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_add_layernorm: bad p dtype %d", p_dtype);
+  if (d % 8 != 0 || d > 2048 || d == 0)
+    return fail(ND_ERR_SHAPE, "nd_add_layernorm: d = %d must be a multiple of 8 in [8, 2048]", d);
+  if (rows == 0) return ok();
+  if (!x || !p || !s_out || !y) return fail(ND_ERR_INVALID_ARG, "nd_add_layernorm: null pointer");
+  if (!aligned16(x) || !aligned16(p) || !aligned16(s_out) || !aligned16(y))
+    return fail(ND_ERR_ALIGNMENT, "nd_add_layernorm: tensors must be 16-byte aligned");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_add_layernorm(
+      static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x), p, p_dtype == ND_F32,
+      bias, gamma, beta, static_cast<__nv_bfloat16*>(s_out), static_cast<__nv_bfloat16*>(y), rows, d,
+      eps);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_add_layernorm");
   return ok();
 }
 

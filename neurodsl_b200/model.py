@@ -1,0 +1,310 @@
+"""GPT-style decoder built from the library's entry points (prefill and
+greedy KV-cache decode), optionally tensor-parallel over ranks.
+
+This is the GPU form of the reference's GPT-2 graph (notebook/GPT2.ipynb
+cells 4 and 10: token + position :embedding, per block a pre-norm, the
+multi-head flash attention of src/flash_attention.jl:225-256, residual :add,
+pre-norm MLP with GELU, residual :add; a final norm and the LM head
+:matmul trans_b against the token embedding) with LayerNorm as the norm and
+one of the GELU forms of fused_linear_gelu as the activation.  Every op runs
+in libneurodsl_b200.so:
+
+  embedding             nd_embed
+  LayerNorm             nd_layernorm, then nd_add_layernorm (residual add,
+                        bias and the next LayerNorm in one pass)
+  QKV / out / MLP       nd_gemm_bias_act (bias and GELU in the epilogue)
+  prefill attention     nd_flash_attn_fwd_strided on the fused QKV projection
+                        (no per-head copies), K/V into the caches by nd_kv_store
+  decode attention      nd_kv_decode_attn with the new token appended in place
+  greedy token          nd_argmax on the LM-head logits
+
+Tensor parallelism (Megatron layout): rank r of `tp` holds heads
+[r·H/tp, (r+1)·H/tp) with their Q/K/V rows and output-projection columns,
+MLP columns [r·F/tp, (r+1)·F/tp) of the up projection and the matching
+columns of the down projection, and vocabulary rows [r·V/tp, ...) of the LM
+head.  The output and down projections produce partial sums that are
+all-reduced (NCCL) before the fused residual + LayerNorm; the LM head gives a
+local (max, index) per row that is all-gathered and reduced to the global
+first maximum.  Weights are generated from one seed on every rank and sliced,
+so any `tp` computes the same model.
+"""
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+
+@dataclass(frozen=True)
+class GPTConfig:
+    n_layer: int
+    d_model: int
+    n_head: int
+    d_ff: int
+    vocab: int
+    n_pos: int
+    act: str = "tanh"      # GELU form: "sigmoid" (z·σ(1.702 z)), "tanh" or "erf"
+    eps: float = 1e-5
+
+    @property
+    def d_head(self):
+        return self.d_model // self.n_head
+
+
+# The GPT-2-small shape and a 24-layer d=1024 model (16 heads x 64, MLP 4096).
+GPT2_SMALL = GPTConfig(n_layer=12, d_model=768, n_head=12, d_ff=3072, vocab=50257, n_pos=1024)
+GPT_24L_1024 = GPTConfig(n_layer=24, d_model=1024, n_head=16, d_ff=4096, vocab=50257, n_pos=4096)
+
+
+def _shard(n, tp, rank):
+    if n % tp:
+        raise ValueError(f"{n} is not divisible by tp={tp}")
+    k = n // tp
+    return rank * k, (rank + 1) * k
+
+
+class GPT:
+    """Weights of one rank plus the buffers of one (batch, length) shape."""
+
+    def __init__(self, cfg: GPTConfig, seed=0, device=None, tp=1, rank=0, group=None,
+                 weight_std=0.02, bias_std=0.0):
+        if cfg.d_head != 64:
+            raise ValueError("head_dim must be 64")
+        self.cfg = cfg
+        self.tp, self.rank, self.group = tp, rank, group
+        self.device = torch.device(device or "cuda")
+        dev = self.device
+        d, F, V = cfg.d_model, cfg.d_ff, cfg.vocab
+        h0, h1 = _shard(cfg.n_head, tp, rank)
+        self.n_head_local = h1 - h0
+        self.d_local = self.n_head_local * 64
+        f0, f1 = _shard(F, tp, rank)
+        self.v0 = rank * ((V + tp - 1) // tp)
+        self.v1 = min(V, self.v0 + (V + tp - 1) // tp)
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+
+        def randn(*shape, std=weight_std):
+            return (torch.randn(*shape, generator=g, device=dev) * std)
+
+        def bias(n):
+            return randn(n, std=bias_std) if bias_std else torch.zeros(n, device=dev)
+
+        bf = torch.bfloat16
+        self.wte = randn(V, d).to(bf)
+        self.wpe = randn(cfg.n_pos, d).to(bf)
+        self.layers = []
+        cols = slice(h0 * 64, h1 * 64)
+        for _ in range(cfg.n_layer):
+            ln1_g = 1 + randn(d, std=0.1) if bias_std else torch.ones(d, device=dev)
+            ln1_b = bias(d)
+            w_qkv = randn(3 * d, d)
+            b_qkv = bias(3 * d)
+            w_o = randn(d, d)
+            b_o = bias(d)
+            ln2_g = 1 + randn(d, std=0.1) if bias_std else torch.ones(d, device=dev)
+            ln2_b = bias(d)
+            w_1 = randn(F, d)
+            b_1 = bias(F)
+            w_2 = randn(d, F)
+            b_2 = bias(d)
+            q, k, v = w_qkv.view(3, d, d)
+            bq, bk, bv = b_qkv.view(3, d)
+            self.layers.append({
+                "ln1_g": ln1_g, "ln1_b": ln1_b,
+                # local Q, K, V rows stacked: [3·d_local][d]
+                "w_qkv": torch.cat([q[cols], k[cols], v[cols]]).to(bf).contiguous(),
+                "b_qkv": torch.cat([bq[cols], bk[cols], bv[cols]]).contiguous(),
+                "w_o": w_o[:, cols].to(bf).contiguous(), "b_o": b_o,
+                "ln2_g": ln2_g, "ln2_b": ln2_b,
+                "w_1": w_1[f0:f1].to(bf).contiguous(), "b_1": b_1[f0:f1].contiguous(),
+                "w_2": w_2[:, f0:f1].to(bf).contiguous(), "b_2": b_2,
+            })
+        self.lnf_g = torch.ones(d, device=dev)
+        self.lnf_b = torch.zeros(d, device=dev)
+        self.w_head = self.wte[self.v0:self.v1]           # tied LM head, local vocab rows
+        self._shape = None
+
+    # ------------------------------------------------------------- buffers
+    def _alloc(self, B, S, steps):
+        """Buffers for prompts of S tokens and `steps` decode steps, batch B."""
+        if self._shape == (B, S, steps):
+            return
+        cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+        d, dl, Fl = cfg.d_model, self.d_local, self.layers[0]["w_1"].shape[0]
+        L_max = S + steps
+        if L_max > cfg.n_pos:
+            raise ValueError(f"prompt {S} + steps {steps} exceeds n_pos {cfg.n_pos}")
+        T = B * S
+        self.buf = {
+            "x": torch.empty(T, d, device=dev, dtype=bf), "h": torch.empty(T, d, device=dev, dtype=bf),
+            "qkv": torch.empty(T, 3 * dl, device=dev, dtype=bf),
+            "attn": torch.empty(T, dl, device=dev, dtype=bf),
+            "part": torch.empty(T, d, device=dev, dtype=bf),
+            "u": torch.empty(T, Fl, device=dev, dtype=bf),
+            "last": torch.empty(B, d, device=dev, dtype=bf),
+            "xd": torch.empty(B, d, device=dev, dtype=bf), "hd": torch.empty(B, d, device=dev, dtype=bf),
+            "qd": torch.empty(B, dl, device=dev, dtype=bf), "kd": torch.empty(B, dl, device=dev, dtype=bf),
+            "vd": torch.empty(B, dl, device=dev, dtype=bf), "ad": torch.empty(B, dl, device=dev, dtype=bf),
+            "pd": torch.empty(B, d, device=dev, dtype=bf), "ud": torch.empty(B, Fl, device=dev, dtype=bf),
+            "logits": torch.empty(B, self.v1 - self.v0, device=dev, dtype=torch.float32),
+            "val": torch.empty(B, device=dev, dtype=torch.float32),
+            "idx": torch.empty(B, device=dev, dtype=torch.int32),
+            # ids of step t in row t; row t+1 is written by step t's argmax
+            "ids": torch.zeros(steps + 1, B, device=dev, dtype=torch.int32),
+            "pos_prefill": torch.arange(S, device=dev, dtype=torch.int32).repeat(B),
+            "pos_decode": (S + torch.arange(steps, device=dev, dtype=torch.int32))
+            .view(steps, 1).repeat(1, B).contiguous(),
+        }
+        ws = ops.kv_decode_workspace_size(B, self.n_head_local, L_max)
+        # decode scratch owned here (zero-filled once, left ready by every call)
+        self.buf["ws"] = torch.zeros(max(ws, 16), device=dev, dtype=torch.uint8)
+        self.k_cache = [torch.zeros(B, self.n_head_local, L_max, 64, device=dev, dtype=bf)
+                        for _ in range(cfg.n_layer)]
+        self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
+        if self.tp > 1:
+            self.buf["gval"] = torch.empty(self.tp, B, device=dev, dtype=torch.float32)
+            self.buf["gidx"] = torch.empty(self.tp, B, device=dev, dtype=torch.int32)
+        self._shape = (B, S, steps)
+
+    def _all_reduce(self, t):
+        if self.tp > 1:
+            torch.distributed.all_reduce(t, group=self.group)
+
+    def _next_token(self, h_rows, out_ids):
+        """Greedy token of each row of h_rows [B][d] into out_ids [B]."""
+        b = self.buf
+        ops.linear(h_rows, self.w_head, out=b["logits"])
+        if self.tp == 1:
+            ops.argmax(b["logits"], idx=out_ids)
+            return
+        ops.argmax(b["logits"], idx=b["idx"], val=b["val"])
+        b["idx"] += self.v0
+        torch.distributed.all_gather_into_tensor(b["gval"], b["val"], group=self.group)
+        torch.distributed.all_gather_into_tensor(b["gidx"], b["idx"], group=self.group)
+        # ranks hold increasing vocabulary ranges: the first rank with the
+        # maximum has the smallest index among equal values
+        best = torch.argmax(b["gval"], dim=0)
+        out_ids.copy_(b["gidx"].gather(0, best.view(1, -1)).view(-1))
+
+    # ------------------------------------------------------------- prefill
+    def prefill(self, ids, steps=0):
+        """Run the prompt ids [B][S] (int32, device); fill the caches and
+        write the first generated token into row 1 of the ids table.
+        Returns the logits of the last position (local vocabulary slice)."""
+        B, S = ids.shape
+        self._alloc(B, S, max(steps, 1))
+        cfg, b = self.cfg, self.buf
+        H, dl = self.n_head_local, self.d_local
+        x, h = b["x"], b["h"]
+        ops.embed(ids.reshape(-1), self.wte, self.wpe, b["pos_prefill"], out=x)
+        ops.layernorm(x, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=h,
+                      stats=False)
+        parts = b["qkv"].view(B, S, 3, H, 64).permute(2, 0, 3, 1, 4)   # [3][B][H][S][64]
+        o4 = b["attn"].view(B, S, H, 64).permute(0, 2, 1, 3)
+        for i, L in enumerate(self.layers):
+            ops.linear(h, L["w_qkv"], L["b_qkv"], out=b["qkv"])
+            ops.kv_store(b["qkv"], dl, 2 * dl, self.k_cache[i], self.v_cache[i], B, S, 0)
+            ops.flash_attn_fwd(parts[0], parts[1], parts[2], causal=True, out=o4)
+            ops.linear(b["attn"], L["w_o"], out=b["part"])
+            self._all_reduce(b["part"])
+            ops.add_layernorm(x, b["part"], L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=x, out=h)
+            ops.linear(h, L["w_1"], L["b_1"], act=cfg.act, out=b["u"])
+            ops.linear(b["u"], L["w_2"], out=b["part"])
+            self._all_reduce(b["part"])
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
+            ops.add_layernorm(x, b["part"], L["b_2"], g_, b_, cfg.eps, s_out=x, out=h)
+        b["last"].copy_(h.view(B, S, -1)[:, -1])
+        self._next_token(b["last"], b["ids"][1])
+        b["ids"][0].copy_(ids[:, -1])
+        return b["logits"]
+
+    # -------------------------------------------------------------- decode
+    def decode_step(self, t):
+        """Decode step t (0-based): the token in row t of the ids table is
+        appended at position S + t and attended; the greedy next token goes to
+        row t + 1.  Launches only (no host synchronisation)."""
+        cfg, b = self.cfg, self.buf
+        B, S, steps = self._shape
+        if not 0 <= t < steps:
+            raise ValueError(f"step {t} outside [0, {steps})")
+        H, dl = self.n_head_local, self.d_local
+        xd, hd = b["xd"], b["hd"]
+        ops.embed(b["ids"][t + 1], self.wte, self.wpe, b["pos_decode"][t], out=xd)
+        ops.layernorm(xd, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=hd,
+                      stats=False)
+        Lc = S + t + 1
+        for i, L in enumerate(self.layers):
+            w, bb = L["w_qkv"], L["b_qkv"]
+            ops.linear(hd, w[:dl], bb[:dl], out=b["qd"])
+            ops.linear(hd, w[dl:2 * dl], bb[dl:2 * dl], out=b["kd"])
+            ops.linear(hd, w[2 * dl:], bb[2 * dl:], out=b["vd"])
+            ops.kv_decode_attn(b["qd"].view(B, H, 64), self.k_cache[i], self.v_cache[i], Lc,
+                               k_new=b["kd"].view(B, H, 64), v_new=b["vd"].view(B, H, 64),
+                               out=b["ad"].view(B, H, 64), workspace=b["ws"], want_lse=False)
+            ops.linear(b["ad"], L["w_o"], out=b["pd"])
+            self._all_reduce(b["pd"])
+            ops.add_layernorm(xd, b["pd"], L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=xd, out=hd)
+            ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
+            ops.linear(b["ud"], L["w_2"], out=b["pd"])
+            self._all_reduce(b["pd"])
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
+            ops.add_layernorm(xd, b["pd"], L["b_2"], g_, b_, cfg.eps, s_out=xd, out=hd)
+        self._next_token(hd, b["ids"][t + 2] if t + 2 <= steps else b["idx"])
+        return b["logits"]
+
+    def tokens(self):
+        """Generated tokens so far: [B][steps] (prefill's token first)."""
+        return self.buf["ids"][1:].t()
+
+    def generate(self, ids, steps, graph_chunk=0):
+        """Greedy generation of `steps` tokens after the prompt ids [B][S].
+        graph_chunk > 0 captures that many decode steps per CUDA graph (the
+        graphs are kept and replayed by later calls of the same shape)."""
+        self.prefill(ids, steps)
+        n_dec = steps - 1
+        if graph_chunk <= 0:
+            for t in range(n_dec):
+                self.decode_step(t)
+            return self.tokens()
+        key = (self._shape, graph_chunk)
+        if getattr(self, "_graphs_key", None) != key:
+            self._graphs = []
+            self._graphs_key = key
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            for t0 in range(0, n_dec, graph_chunk):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    for t in range(t0, min(n_dec, t0 + graph_chunk)):
+                        self.decode_step(t)
+                self._graphs.append(g)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+        for g in self._graphs:
+            g.replay()
+        return self.tokens()
+
+    def release_graphs(self):
+        """Drop captured graphs (those holding NCCL calls go before the
+        process group is destroyed)."""
+        self._graphs = []
+        self._graphs_key = None
+
+
+def flops_prefill(cfg: GPTConfig, B, S):
+    """Algorithmic FLOPs of a prefill of B prompts of S tokens: the layer
+    GEMMs, causal attention (QKᵀ and P·V over the unmasked triangle) and the
+    LM head for the last position of each prompt."""
+    d, F, n = cfg.d_model, cfg.d_ff, cfg.n_layer
+    gemm = 2 * B * S * (3 * d * d + d * d + 2 * d * F) * n
+    attn = 4 * B * cfg.n_head * 64 * (S * (S + 1) // 2) * n
+    return gemm + attn + 2 * B * d * cfg.vocab
+
+
+def decode_weight_bytes(cfg: GPTConfig):
+    """bf16 weight bytes read by one decode step (layers and the LM head)."""
+    d, F, n = cfg.d_model, cfg.d_ff, cfg.n_layer
+    return 2 * (n * (4 * d * d + 2 * d * F) + cfg.vocab * d)

@@ -95,7 +95,8 @@ def kv_decode_workspace_size(B, H, L, D=64):
 
 
 def kv_decode_attn(q, k_cache, v_cache, L, k_new=None, v_new=None, scale=None, out=None,
-                   out_dtype=torch.bfloat16, lse=None, workspace=None, stream=None):
+                   out_dtype=torch.bfloat16, lse=None, workspace=None, want_lse=True,
+                   stream=None):
     """Single-token decode over keys [0, L) of [B][H][L_max][64] bf16 caches.
 
     With k_new/v_new the token at L-1 is appended to the caches in the same
@@ -117,7 +118,7 @@ def kv_decode_attn(q, k_cache, v_cache, L, k_new=None, v_new=None, scale=None, o
         scale = 1.0 / math.sqrt(D)
     if out is None:
         out = torch.empty((B, H, D), dtype=out_dtype, device=q.device)
-    if lse is None:
+    if lse is None and want_lse:
         lse = torch.empty((B, H), dtype=torch.float32, device=q.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(_lib.load().nd_kv_decode_attn(_stream(stream), _ptr(q), _ptr(k_new), _ptr(v_new),
@@ -169,15 +170,17 @@ def linear(A, W, bias=None, residual=None, act="none", out=None, out_dtype=torch
 
 
 def layernorm(x, gamma=None, beta=None, eps=1e-5, out=None, out_dtype=None, mean=None,
-              rstd=None, stream=None):
-    """Row LayerNorm of x [rows][d]; returns (y, mean, rstd)."""
+              rstd=None, stats=True, stream=None):
+    """Row LayerNorm of x [rows][d]; returns (y, mean, rstd).  With
+    stats=False and no mean/rstd buffers the statistics are not written
+    (mean and rstd come back as None)."""
     _need(x, "x", None, 2)
     rows, d = x.shape
     if out is None:
         out = torch.empty((rows, d), dtype=out_dtype or x.dtype, device=x.device)
-    if mean is None:
+    if mean is None and stats:
         mean = torch.empty(rows, dtype=torch.float32, device=x.device)
-    if rstd is None:
+    if rstd is None and stats:
         rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
     for n, t in (("gamma", gamma), ("beta", beta)):
         if t is not None:
@@ -206,3 +209,64 @@ def device_error():
     c = ctypes.c_int(0)
     check(_lib.load().nd_device_error(ctypes.byref(c)))
     return c.value
+
+
+def embed(ids, wte, wpe=None, pos=None, out=None, stream=None):
+    """y[t] = wte[ids[t]] + wpe[pos[t]] (bf16 [T][d]); ids/pos int32 [T]."""
+    _need(ids, "ids", torch.int32, 1)
+    _need(wte, "wte", torch.bfloat16, 2)
+    T = ids.numel()
+    vocab, d = wte.shape
+    n_pos = 0
+    if pos is not None:
+        _need(pos, "pos", torch.int32, 1)
+        _need(wpe, "wpe", torch.bfloat16, 2)
+        n_pos = wpe.shape[0]
+    if out is None:
+        out = torch.empty((T, d), dtype=torch.bfloat16, device=wte.device)
+    _need(out, "out", torch.bfloat16, 2)
+    check(_lib.load().nd_embed(_stream(stream), _ptr(ids), _ptr(pos), _ptr(wte), _ptr(wpe),
+                               _ptr(out), T, d, vocab, n_pos))
+    return out
+
+
+def argmax(logits, idx=None, val=None, stream=None):
+    """First index of the largest value of each row of logits [rows][V]."""
+    _need(logits, "logits", None, 2, contiguous=False)
+    if logits.stride(1) != 1:
+        raise ValueError("logits rows must be contiguous")
+    rows, V = logits.shape
+    if idx is None:
+        idx = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    check(_lib.load().nd_argmax(_stream(stream), _ptr(logits), _DT[logits.dtype],
+                                logits.stride(0), rows, V, _ptr(idx), _ptr(val)))
+    return idx
+
+
+def kv_store(src, k_col, v_col, k_cache, v_cache, B, S, pos0=0, stream=None):
+    """K/V rows of a [B·S][ld] bf16 projection into [B][H][L_max][64] caches."""
+    _need(src, "src", torch.bfloat16, 2, contiguous=False)
+    if src.stride(1) != 1:
+        raise ValueError("src rows must be contiguous")
+    _need(k_cache, "k_cache", torch.bfloat16, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, 4)
+    _, H, L_max, D = k_cache.shape
+    check(_lib.load().nd_kv_store(_stream(stream), _ptr(src), src.stride(0), k_col, v_col,
+                                  _ptr(k_cache), _ptr(v_cache), B, S, H, L_max, pos0, D))
+
+
+def add_layernorm(x, p, bias=None, gamma=None, beta=None, eps=1e-5, s_out=None, out=None,
+                  stream=None):
+    """s = x + p (+ bias) (bf16, s_out may be x), y = LayerNorm(s); returns (s, y)."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(p, "p", None, 2)
+    rows, d = x.shape
+    if s_out is None:
+        s_out = torch.empty_like(x)
+    if out is None:
+        out = torch.empty_like(x)
+    check(_lib.load().nd_add_layernorm(_stream(stream), _ptr(x), _ptr(p), _DT[p.dtype],
+                                       _ptr(bias), _ptr(gamma), _ptr(beta), _ptr(s_out),
+                                       _ptr(out), rows, d, float(eps)))
+    return s_out, out
+

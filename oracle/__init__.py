@@ -209,3 +209,54 @@ def bf16_round(a):
         out = out.copy()
         out[nan] = np.nan
     return out
+
+
+def gpt_last_logits(W, ids, act="tanh", eps=1e-5, reduce=None):
+    """LM-head logits of the last position of each sequence ids [B][T] for a
+    pre-LayerNorm GPT decoder — the composition of the reference's GPT-2 graph
+    (notebook/GPT2.ipynb cells 4 and 10): token + position :embedding
+    (src/dispatch.jl:476-491) and :add, per block LayerNorm -> Q/K/V :linear
+    (:363-384) -> causal attention per head (flash_attn_fwd_cpu_simple!,
+    src/flash_attention.jl:49-69) -> output :linear -> residual :add
+    (:386-417) -> LayerNorm -> :linear + GELU (fused_linear_gelu) -> :linear
+    -> residual :add; final LayerNorm and the LM head :matmul trans_b
+    (:213-243) against the embedding rows.
+
+    W holds float32 arrays (the bf16 weight values): wte [V][d], wpe, w_head
+    [V_local][d] (LM-head rows), lnf_g, lnf_b and layers: a list of dicts with
+    ln1_g, ln1_b, w_qkv [3·d_local][d] (Q, K, V rows of the local heads),
+    b_qkv, w_o [d][d_local], b_o, ln2_g, ln2_b, w_1 [F_local][d], b_1,
+    w_2 [d][F_local], b_2.  `reduce(x)` sums a partial result over the ranks
+    of a tensor-parallel split (identity for one rank).  Values that the GPU
+    path stores in bf16 are rounded to bf16 at the same points, so the two
+    differ only in accumulation order and approximate functions.
+    """
+    ids = np.asarray(ids)
+    B, T = ids.shape
+    red = reduce if reduce is not None else (lambda a: a)
+    x = bf16_round(W["wte"][ids.reshape(-1)] + W["wpe"][np.tile(np.arange(T), B)])
+    L0 = W["layers"][0]
+    h = bf16_round(layernorm(x, L0["ln1_g"], L0["ln1_b"], eps)[0])
+    n = len(W["layers"])
+    for i, L in enumerate(W["layers"]):
+        dl = L["w_qkv"].shape[0] // 3
+        H = dl // 64
+        qkv = bf16_round(linear(h, L["w_qkv"], L["b_qkv"])).reshape(B, T, 3, H, 64)
+        attn = np.zeros((B, T, H, 64), np.float32)
+        for b in range(B):
+            for hh in range(H):
+                o, _, _ = attn_simple(qkv[b, :, 0, hh], qkv[b, :, 1, hh], qkv[b, :, 2, hh],
+                                      causal=True)
+                attn[b, :, hh] = o
+        attn = bf16_round(attn.reshape(B * T, dl))
+        part = bf16_round(red(bf16_round(linear(attn, L["w_o"]))))
+        x = bf16_round(x + (part + L["b_o"]))
+        h = bf16_round(layernorm(x, L["ln2_g"], L["ln2_b"], eps)[0])
+        u = bf16_round(linear(h, L["w_1"], L["b_1"], act=act))
+        part = bf16_round(red(bf16_round(linear(u, L["w_2"]))))
+        x = bf16_round(x + (part + L["b_2"]))
+        nxt = W["layers"][i + 1] if i + 1 < n else None
+        g, be = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (W["lnf_g"], W["lnf_b"])
+        h = bf16_round(layernorm(x, g, be, eps)[0])
+    last = h.reshape(B, T, -1)[:, -1]
+    return linear(last, W["w_head"])

@@ -1,0 +1,121 @@
+"""GPU checks of the decoder's auxiliary ops through the C ABI: token +
+position embedding, greedy argmax, prefill KV-cache fill and the residual add
+fused with LayerNorm.  Integer and copy work is compared bit-exactly; the
+LayerNorm output (bf16) within max-abs 2e-2 of the fp32 oracle.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import oracle  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from neurodsl_b200 import ops
+    return ops
+
+
+def _bf16(a):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).cuda().to(torch.bfloat16)
+
+
+def test_embed_tokens_and_positions_exact():
+    ops = _ops()
+    rng = np.random.default_rng(0)
+    V, P, d, T = 1000, 64, 256, 77
+    wte = oracle.bf16_round(rng.standard_normal((V, d), dtype=np.float32) * 0.02)
+    wpe = oracle.bf16_round(rng.standard_normal((P, d), dtype=np.float32) * 0.02)
+    ids = rng.integers(0, V, T).astype(np.int32)
+    pos = (np.arange(T) % P).astype(np.int32)
+    y = ops.embed(torch.from_numpy(ids).cuda(), _bf16(wte), _bf16(wpe), torch.from_numpy(pos).cuda())
+    ref = oracle.bf16_round(wte[ids] + wpe[pos])
+    np.testing.assert_array_equal(y.float().cpu().numpy(), ref)
+    y2 = ops.embed(torch.from_numpy(ids).cuda(), _bf16(wte))
+    np.testing.assert_array_equal(y2.float().cpu().numpy(), wte[ids])
+
+
+def test_embed_out_of_range_id_sets_error_and_zero_row():
+    ops = _ops()
+    wte = torch.ones((10, 64), device="cuda", dtype=torch.bfloat16)
+    ids = torch.tensor([3, 10, -1, 2], device="cuda", dtype=torch.int32)
+    assert ops.device_error() == 0
+    y = ops.embed(ids, wte)
+    assert ops.device_error() == 16
+    yn = y.float().cpu().numpy()
+    assert (yn[0] == 1).all() and (yn[3] == 1).all()
+    assert (yn[1] == 0).all() and (yn[2] == 0).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_argmax_first_maximum(dtype):
+    ops = _ops()
+    rng = np.random.default_rng(1)
+    rows, V = 16, 50257
+    x = rng.standard_normal((rows, V), dtype=np.float32)
+    x[3, 100] = x[3, 200] = 50.0          # tie: the first index wins
+    x[5, :] = -np.inf
+    x[5, 7] = 0.0
+    x[6, 0] = np.nan                      # NaN never wins over numbers
+    t = torch.from_numpy(x).cuda().to(dtype)
+    idx = ops.argmax(t).cpu().numpy()
+    xr = t.float().cpu().numpy()
+    ref = np.array([np.nanargmax(r) for r in xr])
+    np.testing.assert_array_equal(idx, ref)
+    assert idx[3] == 100 and idx[5] == 7
+    # strided rows (a column window of a wider matrix)
+    wide = torch.zeros((rows, V + 40), device="cuda", dtype=dtype)
+    wide[:, 8:8 + V] = t
+    idx2 = ops.argmax(wide[:, 8:8 + V]).cpu().numpy()
+    np.testing.assert_array_equal(idx2, ref)
+
+
+def test_kv_store_from_qkv_projection_exact():
+    ops = _ops()
+    rng = np.random.default_rng(2)
+    B, S, H, L_max, pos0 = 2, 37, 3, 64, 5
+    d = H * 64
+    qkv = oracle.bf16_round(rng.standard_normal((B * S, 3 * d), dtype=np.float32))
+    kc = torch.zeros((B, H, L_max, 64), device="cuda", dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    ops.kv_store(_bf16(qkv), d, 2 * d, kc, vc, B, S, pos0)
+    x = qkv.reshape(B, S, 3, H, 64)
+    k_ref = np.zeros((B, H, L_max, 64), np.float32)
+    v_ref = np.zeros_like(k_ref)
+    k_ref[:, :, pos0:pos0 + S] = x[:, :, 1].transpose(0, 2, 1, 3)
+    v_ref[:, :, pos0:pos0 + S] = x[:, :, 2].transpose(0, 2, 1, 3)
+    np.testing.assert_array_equal(kc.float().cpu().numpy(), k_ref)
+    np.testing.assert_array_equal(vc.float().cpu().numpy(), v_ref)
+
+
+@pytest.mark.parametrize("d,p_f32", [(768, False), (1024, True), (2048, False), (200, True)])
+def test_add_layernorm(d, p_f32):
+    ops = _ops()
+    rng = np.random.default_rng(3)
+    rows = 300
+    x = oracle.bf16_round(rng.standard_normal((rows, d), dtype=np.float32))
+    p = rng.standard_normal((rows, d), dtype=np.float32)
+    if not p_f32:
+        p = oracle.bf16_round(p)
+    bias = rng.standard_normal(d, dtype=np.float32) * 0.1
+    g = 1 + 0.1 * rng.standard_normal(d, dtype=np.float32)
+    b = 0.1 * rng.standard_normal(d, dtype=np.float32)
+    xt = _bf16(x)
+    pt = torch.from_numpy(p).cuda() if p_f32 else _bf16(p)
+    cuda = lambda a: torch.from_numpy(a).cuda()
+    s, y = ops.add_layernorm(xt, pt, cuda(bias), cuda(g), cuda(b), eps=1e-5, s_out=xt)
+    s_ref = oracle.bf16_round(x + (p + bias))
+    np.testing.assert_array_equal(s.float().cpu().numpy(), s_ref)   # in place: s is x
+    y_ref, _, _ = oracle.layernorm(s_ref, g, b, 1e-5)
+    err = np.abs(y.float().cpu().numpy() - y_ref).max()
+    assert err <= 2e-2, err
+
+
+def test_add_layernorm_rejects_bad_width():
+    ops = _ops()
+    from neurodsl_b200._lib import NeuroDSLError
+    x = torch.zeros((4, 12), device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(NeuroDSLError):
+        ops.add_layernorm(x, x)
