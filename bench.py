@@ -8,7 +8,10 @@ library's prefill kernel over all 128 (batch, head) pairs.  Metric: attention
 TFLOP/s with the algorithmic causal count 4·B·H·D·S(S+1)/2 per step.  The same
 JSON line carries the KV-cache decode workload (batch 64, 12 heads, head_dim
 64, cache 1024 -> 1152 over 128 appending steps) as tokens/s, each with its
-roofline against the measured B200 peaks.
+roofline against the measured B200 peaks, and two whole decoders assembled
+from the library (prefill tokens/s and greedy-decode tokens/s): GPT-2 small
+(batch 16, prompt 512, 256 tokens; one replica per GPU) and a 24-layer d=1024
+model (batch 32, prompt 2048, 512 tokens; tensor-parallel over all GPUs).
 
 Multi-GPU: one process per GPU (torchrun); every rank runs its own full
 workload (independent batches, no collective on the data path) and the job
@@ -194,6 +197,79 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------- GPU arm ---
+
+def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks, barrier,
+               peaks, reps, chunk):
+    """Prefill and greedy decode of a GPT-style decoder built from the library
+    (neurodsl_b200.model).  tp == world: one tensor-parallel model over all
+    ranks (Megatron shards, NCCL all-reduces; strong scaling); tp == 1: every
+    rank runs its own replica on its own batch (weak scaling)."""
+    import torch
+
+    from neurodsl_b200.model import GPT, decode_weight_bytes, flops_prefill
+    group = torch.distributed.group.WORLD if (pg is not None and tp > 1) else None
+    model = GPT(cfg, seed=0, device=dev, tp=tp, rank=rank if tp > 1 else 0, group=group)
+    gen = torch.Generator(device=dev).manual_seed(99 + (0 if tp > 1 else rank))
+    ids = torch.randint(0, cfg.vocab, (B, S), device=dev, dtype=torch.int32, generator=gen)
+    graphs = True
+    try:
+        model.generate(ids, steps, graph_chunk=chunk)
+    except Exception:  # collectives that cannot be captured: decode eagerly
+        graphs = False
+        model.release_graphs()
+        torch.cuda.synchronize()
+        model.generate(ids, steps)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    tp_ms, td_ms = [], []
+    for _ in range(reps):
+        barrier()
+        torch.cuda.synchronize()
+        ev[0].record()
+        model.prefill(ids, steps)
+        ev[1].record()
+        if graphs:
+            for g in model._graphs:
+                g.replay()
+        else:
+            for t in range(steps - 1):
+                model.decode_step(t)
+        ev[2].record()
+        torch.cuda.synchronize()
+        tp_ms.append(ev[0].elapsed_time(ev[1]))
+        td_ms.append(ev[1].elapsed_time(ev[2]))
+    p_ms = max_over_ranks(min(tp_ms))
+    d_ms = max_over_ranks(min(td_ms))
+    tokens = model.tokens()[:, :4].cpu().tolist()
+    model.release_graphs()
+    del model
+    torch.cuda.synchronize()
+    replicas = 1 if tp > 1 else world
+    n_dec = steps - 1
+    fl = flops_prefill(cfg, B, S)
+    kv = sum(2 * B * cfg.n_layer * cfg.n_head * (S + t + 1) * 64 * 2 for t in range(n_dec))
+    dec_bytes = decode_weight_bytes(cfg) * n_dec + kv   # whole model, all ranks together
+    p_tflops = replicas * fl / (p_ms * 1e-3) / 1e12
+    d_gbs = replicas * dec_bytes / (d_ms * 1e-3) / 1e9
+    return {
+        "workload": f"{name}: {cfg.n_layer} layers d={cfg.d_model} {cfg.n_head}x64 heads "
+                    f"F={cfg.d_ff} vocab {cfg.vocab}, batch {B}, prompt {S}, {steps} greedy tokens",
+        "parallelism": f"tp{tp}" if tp > 1 else f"dp{world} replicas",
+        "scaling": "strong" if tp > 1 else "weak",
+        "prefill": {"value": replicas * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
+                    "roofline": {"bound": "tensor", "achieved": p_tflops / world,
+                                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
+                                 "frac": p_tflops / world / peaks["bf16_tflops"]}},
+        "decode": {"value": replicas * B * n_dec / (d_ms * 1e-3), "unit": "tokens/s", "ms": d_ms,
+                   "us_per_step": d_ms * 1e3 / n_dec,
+                   "launch": "CUDA graphs" if graphs else "eager launches",
+                   "roofline": {"bound": "hbm", "achieved": d_gbs / world,
+                                "peak": peaks["hbm_gbs"], "unit": "GB/s per GPU",
+                                "frac": d_gbs / world / peaks["hbm_gbs"],
+                                "bytes": "bf16 weights + K/V read per step"}},
+        "first_tokens": tokens[0],
+    }
+
 
 def run_ours(args):
     import torch
@@ -383,6 +459,13 @@ def run_ours(args):
         cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port", "sample": desc}
 
     peaks = load_peaks()
+    models = {}
+    if not args.no_model:
+        from neurodsl_b200.model import GPT2_SMALL, GPT_24L_1024
+        models["gpt2_small"] = model_line("GPT-2 small", GPT2_SMALL, 16, 512, 256, 1, rank, world,
+                                          dev, pg, max_over_ranks, barrier, peaks, 2, 32)
+        models["gpt_24l_1024"] = model_line("24-layer", GPT_24L_1024, 32, 2048, 512, world, rank,
+                                            world, dev, pg, max_over_ranks, barrier, peaks, 2, 64)
     traffic = load_traffic("flash_fwd_causal_b8_h16_s2048_d64")
     dec_traffic = load_traffic("kv_decode_b64_h12_l1024_d64")
     if rank == 0:
@@ -434,6 +517,7 @@ def run_ours(args):
                              "traffic": load_traffic("layernorm_rows65536_d1024")},
             },
         }
+        line.update(models)
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.barrier()
@@ -453,6 +537,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the GPT-2-small and 24-layer decoder lines")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -460,6 +460,142 @@ cudaError_t launch_bn(int BN, int act, cudaStream_t stream, const CUtensorMap& t
   return launch_act<64, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
 }
 
+// ---- skinny path: M <= 32 rows (decode-time activations) -------------------
+// A 128-row tensor-core tile would compute mostly padding and leave N/BN
+// CTAs streaming the weights; with M <= 32 the op is bound by reading W.
+// Here a CTA owns 8 rows of W and its 8 warps split K, so N/8 CTAs keep many
+// 16-byte loads of W in flight.  Each lane reads 16 bytes (8 k values) of
+// one W row and of each A row per 32-wide k chunk and feeds two
+// mma.m16n8k16 steps; the k values are assigned to fragment positions by
+// the same permutation for A and W, which leaves every dot product intact.
+// The warps' 16x8 (or 32x8) partial tiles are summed through shared memory
+// and the epilogue adds bias, activation and residual like the main path.
+constexpr int kSkinnyWarps = 8;
+constexpr int kSkinnyBatch = 4;  // k chunks whose loads are issued together
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+      "{%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 ldg16_or_zero(const __nv_bfloat16* p, bool ok) {
+  return ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
+}
+
+template <int kMB, bool kOutF32, int kAct, bool kRes>
+__global__ void __launch_bounds__(kSkinnyWarps * 32)
+    skinny_gemm_kernel(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ W,
+                       const float* __restrict__ bias, const void* __restrict__ residual,
+                       int residual_f32, void* __restrict__ Y, int M, int N, int K) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;  // fragment group (row / column) and slot
+  const int n0 = blockIdx.x * 8;
+  const bool w_ok = n0 + g < N;
+  const __nv_bfloat16* wrow = W + static_cast<size_t>(w_ok ? n0 + g : 0) * K + t * 8;
+  const __nv_bfloat16* arow[kMB][2];
+  bool a_ok[kMB][2];
+#pragma unroll
+  for (int mb = 0; mb < kMB; ++mb)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = mb * 16 + h * 8 + g;
+      a_ok[mb][h] = m < M;
+      arow[mb][h] = A + static_cast<size_t>(a_ok[mb][h] ? m : 0) * K + t * 8;
+    }
+  float c[kMB][4];
+#pragma unroll
+  for (int mb = 0; mb < kMB; ++mb)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) c[mb][i] = 0.f;
+  const int n_chunks = K / 32;
+  for (int c0 = warp; c0 < n_chunks; c0 += kSkinnyWarps * kSkinnyBatch) {
+    uint4 wv[kSkinnyBatch], av[kSkinnyBatch][kMB][2];
+#pragma unroll
+    for (int u = 0; u < kSkinnyBatch; ++u) {
+      const int ch = c0 + u * kSkinnyWarps;
+      const bool in = ch < n_chunks;
+      wv[u] = ldg16_or_zero(wrow + ch * 32, in && w_ok);
+#pragma unroll
+      for (int mb = 0; mb < kMB; ++mb)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) av[u][mb][h] = ldg16_or_zero(arow[mb][h] + ch * 32, in && a_ok[mb][h]);
+    }
+#pragma unroll
+    for (int u = 0; u < kSkinnyBatch; ++u) {
+      const uint32_t w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+      for (int mb = 0; mb < kMB; ++mb) {
+        const uint32_t lo[4] = {av[u][mb][0].x, av[u][mb][0].y, av[u][mb][0].z, av[u][mb][0].w};
+        const uint32_t hi[4] = {av[u][mb][1].x, av[u][mb][1].y, av[u][mb][1].z, av[u][mb][1].w};
+#pragma unroll
+        for (int s = 0; s < 2; ++s)
+          mma_bf16_16816(c[mb], lo[2 * s], hi[2 * s], lo[2 * s + 1], hi[2 * s + 1], w[2 * s],
+                         w[2 * s + 1]);
+      }
+    }
+  }
+  // sum the warps' partial tiles: red[warp][m][n] for the 16·kMB x 8 tile
+  __shared__ float red[kSkinnyWarps][kMB * 16][8];
+#pragma unroll
+  for (int mb = 0; mb < kMB; ++mb) {
+    red[warp][mb * 16 + g][2 * t] = c[mb][0];
+    red[warp][mb * 16 + g][2 * t + 1] = c[mb][1];
+    red[warp][mb * 16 + g + 8][2 * t] = c[mb][2];
+    red[warp][mb * 16 + g + 8][2 * t + 1] = c[mb][3];
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < kMB * 16 * 8; o += blockDim.x) {
+    const int m = o >> 3, n = n0 + (o & 7);
+    if (m >= M || n >= N) continue;
+    float z = 0.f;
+#pragma unroll
+    for (int w = 0; w < kSkinnyWarps; ++w) z += red[w][m][o & 7];
+    if (bias != nullptr) z += bias[n];
+    z = act1<kAct>(z);
+    const size_t idx = static_cast<size_t>(m) * N + n;
+    if constexpr (kRes)
+      z += residual_f32 ? static_cast<const float*>(residual)[idx]
+                        : __bfloat162float(static_cast<const __nv_bfloat16*>(residual)[idx]);
+    if constexpr (kOutF32) static_cast<float*>(Y)[idx] = z;
+    else static_cast<__nv_bfloat16*>(Y)[idx] = __float2bfloat16_rn(z);
+  }
+}
+
+template <int kMB, bool kOutF32, int kAct>
+cudaError_t launch_skinny_act(cudaStream_t stream, const __nv_bfloat16* A, const __nv_bfloat16* W,
+                              const float* bias, const void* residual, bool residual_f32, void* Y,
+                              int M, int N, int K) {
+  const dim3 grid((N + 7) / 8);
+  if (residual != nullptr)
+    skinny_gemm_kernel<kMB, kOutF32, kAct, true><<<grid, kSkinnyWarps * 32, 0, stream>>>(
+        A, W, bias, residual, residual_f32 ? 1 : 0, Y, M, N, K);
+  else
+    skinny_gemm_kernel<kMB, kOutF32, kAct, false><<<grid, kSkinnyWarps * 32, 0, stream>>>(
+        A, W, bias, residual, 0, Y, M, N, K);
+  return cudaGetLastError();
+}
+
+template <int kMB, bool kOutF32>
+cudaError_t launch_skinny(int act, cudaStream_t stream, const __nv_bfloat16* A,
+                          const __nv_bfloat16* W, const float* bias, const void* residual,
+                          bool residual_f32, void* Y, int M, int N, int K) {
+  switch (act) {
+    case ND_ACT_GELU_SIGMOID:
+      return launch_skinny_act<kMB, kOutF32, ND_ACT_GELU_SIGMOID>(stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+    case ND_ACT_GELU_TANH:
+      return launch_skinny_act<kMB, kOutF32, ND_ACT_GELU_TANH>(stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+    case ND_ACT_GELU_ERF:
+      return launch_skinny_act<kMB, kOutF32, ND_ACT_GELU_ERF>(stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+    default:
+      return launch_skinny_act<kMB, kOutF32, ND_ACT_NONE>(stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_bfloat16* W,
@@ -467,6 +603,15 @@ cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_
                         bool out_f32, int M, int N, int K, int act, const char** err_msg) {
   if (M == 0 || N == 0) return cudaSuccess;
   if (K == 0) return cudaErrorInvalidValue;
+  if (M <= 32 && K % 32 == 0) {
+    // few rows: the weight-streaming path (A and W rows are 16-byte aligned
+    // because K % 32 == 0 and the bases are)
+    if (M <= 16)
+      return out_f32 ? launch_skinny<1, true>(act, stream, A, W, bias, residual, residual_f32, Y, M, N, K)
+                     : launch_skinny<1, false>(act, stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+    return out_f32 ? launch_skinny<2, true>(act, stream, A, W, bias, residual, residual_f32, Y, M, N, K)
+                   : launch_skinny<2, false>(act, stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+  }
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

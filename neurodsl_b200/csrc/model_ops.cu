@@ -98,23 +98,36 @@ __device__ __forceinline__ void better(float& v, int& i, float v2, int i2) {
   }
 }
 
+constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxUnroll = 8;  // independent loads in flight per thread
+
 template <typename T>
-__global__ void __launch_bounds__(512)
+__global__ void __launch_bounds__(kArgmaxThreads)
     argmax_kernel(const T* __restrict__ logits, long long ld, int V, int* __restrict__ idx,
                   float* __restrict__ val) {
   const int row = blockIdx.x;
   const T* r = logits + static_cast<size_t>(row) * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) better(bv, bi, ld_f<T>(r + j), j);
+  for (int j0 = threadIdx.x; j0 < V; j0 += kArgmaxThreads * kArgmaxUnroll) {
+    float v[kArgmaxUnroll];
+#pragma unroll
+    for (int u = 0; u < kArgmaxUnroll; ++u) {
+      const int j = j0 + u * kArgmaxThreads;
+      v[u] = j < V ? ld_f<T>(r + j) : -INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < kArgmaxUnroll; ++u)
+      if (j0 + u * kArgmaxThreads < V) better(bv, bi, v[u], j0 + u * kArgmaxThreads);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
     const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
     better(bv, bi, v2, i2);
   }
-  __shared__ float sv[16];
-  __shared__ int si[16];
+  __shared__ float sv[kArgmaxThreads / 32];
+  __shared__ int si[kArgmaxThreads / 32];
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   if (lane == 0) {
     sv[w] = bv;
@@ -262,9 +275,9 @@ cudaError_t launch_argmax(cudaStream_t stream, const void* logits, bool f32, lon
                           int rows, int V, int* idx, float* val) {
   if (rows == 0) return cudaSuccess;
   if (f32)
-    argmax_kernel<float><<<rows, 512, 0, stream>>>(static_cast<const float*>(logits), ld, V, idx, val);
+    argmax_kernel<float><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const float*>(logits), ld, V, idx, val);
   else
-    argmax_kernel<__nv_bfloat16><<<rows, 512, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits),
+    argmax_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits),
                                                            ld, V, idx, val);
   return cudaGetLastError();
 }

@@ -59,6 +59,26 @@ def test_shapes_vs_torch(M, N, K, act):
     check(y.cpu().numpy(), z.cpu().numpy())
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 768, 768), (7, 300, 96), (16, 2304, 768),
+                                   (17, 50257, 768), (32, 1024, 4096), (30, 8, 32)])
+@pytest.mark.parametrize("act,res", [("none", False), ("tanh", True), ("sigmoid", False)])
+def test_few_rows_vs_oracle(M, N, K, act, res):
+    """M <= 32 takes the weight-streaming path; compared with the oracle on
+    bf16-rounded inputs, bf16 and fp32 outputs, with and without residual."""
+    ops = _ops()
+    rng = np.random.default_rng(M * 7 + N + K)
+    A = oracle.bf16_round(rng.standard_normal((M, K), dtype=np.float32))
+    W = oracle.bf16_round((0.03 * rng.standard_normal((N, K))).astype(np.float32))
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    R = oracle.bf16_round(rng.standard_normal((M, N), dtype=np.float32)) if res else None
+    ref = oracle.linear(A, W, b, residual=R, act=act)
+    for out_dtype in (torch.float32, torch.bfloat16):
+        y = ops.linear(_t(A), _t(W), _t(b, torch.float32), residual=None if R is None else _t(R),
+                       act=act, out_dtype=out_dtype)
+        torch.cuda.synchronize()
+        check(y.float().cpu().numpy(), ref)
+
+
 def test_residual_bf16_and_bf16_out():
     ops = _ops()
     rng = np.random.default_rng(4)
