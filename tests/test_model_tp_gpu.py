@@ -1,0 +1,101 @@
+"""Tensor-parallel decoder on two GPUs (NCCL): the tp=2 model built from the
+same seed must reproduce the one-GPU model — LM-head logits within relative
+L2 1e-2 and max-abs 5e-2 (logits spread ~0.8 here; each rank's partial sum
+is rounded to bf16 before the all-reduce, one extra rounding per sub-layer)
+and the greedy tokens wherever the one-GPU top-2 margin exceeds 5e-2 — and
+its graph-captured decode must give the same tokens as its eager decode.  Skipped with fewer than 2 GPUs.
+Each rank runs the same collectives in the same order; the process group has
+a 60 s timeout so a lost rank ends the others with an error.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from _gpt_util import top2_margin  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(n_layer=2, d_model=256, n_head=4, d_ff=1024, vocab=1000, n_pos=64, act="tanh")
+B, S, STEPS = 2, 24, 6
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _prompt():
+    return np.random.default_rng(9).integers(0, CFG["vocab"], (B, S)).astype(np.int32)
+
+
+def _run(model, ids):
+    logits = [model.prefill(ids, STEPS).clone()]
+    for t in range(STEPS - 1):
+        logits.append(model.decode_step(t).clone())
+    return logits, model.tokens().clone()
+
+
+def _rank_main(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from neurodsl_b200.model import GPT, GPTConfig
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        m = GPT(GPTConfig(**CFG), seed=21, device=dev, tp=world, rank=rank,
+                group=dist.group.WORLD, weight_std=0.05, bias_std=0.02)
+        ids = torch.from_numpy(_prompt()).to(dev)
+        logits, tokens = _run(m, ids)
+        full = []
+        for lg in logits:
+            parts = [torch.empty_like(lg) for _ in range(world)]
+            dist.all_gather(parts, lg)
+            full.append(torch.cat(parts, dim=1).cpu().numpy())
+        graphed = m.generate(ids, STEPS, graph_chunk=2).clone()
+        torch.cuda.synchronize()
+        m.release_graphs()
+        if rank == 0:
+            np.save(os.path.join(out_dir, "logits.npy"), np.stack(full))
+            np.save(os.path.join(out_dir, "tokens.npy"), tokens.cpu().numpy())
+            np.save(os.path.join(out_dir, "graphed.npy"), graphed.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_matches_single_gpu(tmp_path):
+    import torch.multiprocessing as mp
+    from neurodsl_b200.model import GPT, GPTConfig
+    mp.start_processes(_rank_main, args=(2, _port(), str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    ref = GPT(GPTConfig(**CFG), seed=21, device="cuda:0", weight_std=0.05, bias_std=0.02)
+    ref_logits, ref_tokens = _run(ref, torch.from_numpy(_prompt()).cuda())
+    ref_logits = np.stack([x.cpu().numpy() for x in ref_logits])
+    ref_tokens = ref_tokens.cpu().numpy()
+    logits = np.load(tmp_path / "logits.npy")
+    tokens = np.load(tmp_path / "tokens.npy")
+    graphed = np.load(tmp_path / "graphed.npy")
+    np.testing.assert_array_equal(graphed, tokens)
+    def close(a, b):
+        rel = float(np.linalg.norm(a - b) / np.linalg.norm(b))
+        return float(np.abs(a - b).max()) <= 5e-2 and rel <= 1e-2
+
+    # the first step sees the same prompt on both sides
+    assert close(logits[0], ref_logits[0])
+    for k in range(STEPS):
+        clear = top2_margin(ref_logits[k]) > 5e-2
+        if (tokens[:, :k] == ref_tokens[:, :k]).all():
+            assert close(logits[k], ref_logits[k]), k
+            np.testing.assert_array_equal(tokens[clear, k], ref_tokens[clear, k])
