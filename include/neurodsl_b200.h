@@ -41,6 +41,8 @@
  *                       src/dispatch.jl:213-243 feeds it)
  *   nd_kv_store         no reference counterpart (prefill fills the decode cache)
  *   nd_add_layernorm    residual :add src/dispatch.jl:386-417 + :layernorm
+ *   nd_comm_*, nd_allreduce_add_layernorm  no reference counterpart (multi-GPU
+ *                       tensor-parallel reduction fused with :add + :layernorm)
  */
 #ifndef NEURODSL_B200_H
 #define NEURODSL_B200_H
@@ -236,6 +238,37 @@ int nd_kv_store(void *stream, const void *src, int64_t ld, int k_col, int v_col,
 int nd_add_layernorm(void *stream, const void *x, const void *p, int p_dtype, const float *bias,
                      const float *gamma, const float *beta, void *s_out, void *y, int rows,
                      int d, float eps);
+
+/*
+ * Tensor-parallel reduction over NVLink peer memory, fused with the residual
+ * add, bias and LayerNorm that follow a row-parallel projection (the
+ * out-projection and MLP-down of a Megatron block).  No reference
+ * counterpart: the reference runs on one device; this replaces an NCCL
+ * all-reduce followed by nd_add_layernorm for small messages (decode).
+ *
+ * Every rank owns one "region" (nd_comm_region_bytes for rows_max x d),
+ * allocated by nd_comm_alloc, whose 64-byte IPC handle the caller sends to
+ * the other ranks; each opens the others' regions with nd_comm_open.  A
+ * rank's partial sum [rows][d] bf16 is written by its GEMM into slot `slot`
+ * of its own region (offset nd_comm_slot_offset(slot, rows_max, d)); then
+ * every rank calls nd_allreduce_add_layernorm with the same arguments except
+ * `rank` (regions[r] = rank r's region as mapped in this process) and gets
+ *   s_out = x + Σ_r partial_r + bias (bf16),  y = LayerNorm(s_out)
+ * computed with the same bits on every rank.  Calls must alternate slots
+ * (0, 1, 0, ...), every rank makes the same calls in the same order, and a
+ * peer that does not arrive within the library's wait limit (2 s) leaves
+ * garbage in the outputs and sets the device error word (nd_device_error).
+ */
+int nd_comm_region_bytes(int rows_max, int d, size_t *bytes);
+int nd_comm_slot_offset(int slot, int rows_max, int d, size_t *offset);
+int nd_comm_alloc(size_t bytes, void **region, void *ipc_handle /* 64 bytes out */);
+int nd_comm_open(const void *ipc_handle, void **peer_region);
+int nd_comm_close(void *peer_region);
+int nd_comm_free(void *region);
+int nd_allreduce_add_layernorm(void *stream, void *const *regions, int tp, int rank,
+                               size_t region_bytes, int rows_max, int slot, const void *x,
+                               const float *bias, const float *gamma, const float *beta,
+                               void *s_out, void *y, int rows, int d, float eps);
 
 #ifdef __cplusplus
 }

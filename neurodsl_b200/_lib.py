@@ -58,6 +58,14 @@ SIGNATURES = {
     "nd_argmax": (_i, [_vp, _vp, _i, ctypes.c_int64, _i, _i, _vp, _vp]),
     "nd_kv_store": (_i, [_vp, _vp, ctypes.c_int64, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i]),
     "nd_add_layernorm": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp, _vp, _vp, _i, _i, _f]),
+    "nd_comm_region_bytes": (_i, [_i, _i, ctypes.POINTER(_sz)]),
+    "nd_comm_slot_offset": (_i, [_i, _i, _i, ctypes.POINTER(_sz)]),
+    "nd_comm_alloc": (_i, [_sz, ctypes.POINTER(_vp), _vp]),
+    "nd_comm_open": (_i, [_vp, ctypes.POINTER(_vp)]),
+    "nd_comm_close": (_i, [_vp]),
+    "nd_comm_free": (_i, [_vp]),
+    "nd_allreduce_add_layernorm": (_i, [_vp, ctypes.POINTER(_vp), _i, _i, _sz, _i, _i, _vp, _vp,
+                                        _vp, _vp, _vp, _vp, _i, _i, _f]),
 }
 
 

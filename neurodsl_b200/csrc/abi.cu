@@ -20,6 +20,7 @@
 #include "kv_decode.h"
 #include "layernorm.h"
 #include "model_ops.h"
+#include "tp_comm.h"
 
 namespace {
 // Device error word: one int per device (a __device__ variable exists once
@@ -570,6 +571,116 @@ __attribute__((visibility("default"))) int nd_add_layernorm(void* stream, const 
       bias, gamma, beta, static_cast<__nv_bfloat16*>(s_out), static_cast<__nv_bfloat16*>(y), rows, d,
       eps);
   if (e != cudaSuccess) return cuda_fail(e, "nd_add_layernorm");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_comm_region_bytes(int rows_max, int d,
+                                                                size_t* bytes) {
+  if (!bytes) return fail(ND_ERR_INVALID_ARG, "nd_comm_region_bytes: bytes is NULL");
+  if (rows_max < 1 || d < 8 || d % 8 || d > 2048)
+    return fail(ND_ERR_SHAPE, "nd_comm_region_bytes: rows_max %d, d %d (d a multiple of 8 in [8, 2048])",
+                rows_max, d);
+  *bytes = nd::comm_region_bytes(rows_max, d);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_comm_slot_offset(int slot, int rows_max, int d,
+                                                               size_t* offset) {
+  if (!offset) return fail(ND_ERR_INVALID_ARG, "nd_comm_slot_offset: offset is NULL");
+  if ((slot != 0 && slot != 1) || rows_max < 1 || d < 8 || d % 8 || d > 2048)
+    return fail(ND_ERR_SHAPE, "nd_comm_slot_offset: slot %d, rows_max %d, d %d", slot, rows_max, d);
+  *offset = nd::comm_slot_offset(slot, rows_max, d);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_comm_alloc(size_t bytes, void** region,
+                                                         void* ipc_handle) {
+  if (!region || !ipc_handle) return fail(ND_ERR_INVALID_ARG, "nd_comm_alloc: null pointer");
+  if (bytes < nd::comm_region_bytes(1, 8)) return fail(ND_ERR_SHAPE, "nd_comm_alloc: %zu bytes is too small", bytes);
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_comm_alloc: cudaMalloc");
+  // flags and sequence counters start at zero; finished before any peer sees the handle
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "nd_comm_alloc");
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *region = p;
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_comm_open(const void* ipc_handle, void** peer_region) {
+  if (!ipc_handle || !peer_region) return fail(ND_ERR_INVALID_ARG, "nd_comm_open: null pointer");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_comm_open: cudaIpcOpenMemHandle");
+  *peer_region = p;
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_comm_close(void* peer_region) {
+  if (!peer_region) return ok();
+  cudaError_t e = cudaIpcCloseMemHandle(peer_region);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_comm_close");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_comm_free(void* region) {
+  if (!region) return ok();
+  cudaError_t e = cudaFree(region);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_comm_free");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_allreduce_add_layernorm(
+    void* stream, void* const* regions, int tp, int rank, size_t region_bytes, int rows_max,
+    int slot, const void* x, const float* bias, const float* gamma, const float* beta,
+    void* s_out, void* y, int rows, int d, float eps) {
+  if (!regions) return fail(ND_ERR_INVALID_ARG, "nd_allreduce_add_layernorm: regions is NULL");
+  if (tp < 1 || tp > nd::kCommMaxRanks || rank < 0 || rank >= tp)
+    return fail(ND_ERR_INVALID_ARG, "nd_allreduce_add_layernorm: tp %d / rank %d (tp <= %d)", tp, rank,
+                nd::kCommMaxRanks);
+  if (slot != 0 && slot != 1) return fail(ND_ERR_INVALID_ARG, "nd_allreduce_add_layernorm: slot %d (0 or 1)", slot);
+  if (d < 8 || d % 8 || d > 2048)
+    return fail(ND_ERR_SHAPE, "nd_allreduce_add_layernorm: d = %d must be a multiple of 8 in [8, 2048]", d);
+  if (rows < 0 || rows > rows_max)
+    return fail(ND_ERR_SHAPE, "nd_allreduce_add_layernorm: rows %d outside [0, rows_max %d]", rows, rows_max);
+  if (nd::comm_region_bytes(rows_max, d) > region_bytes)
+    return fail(ND_ERR_SHAPE, "nd_allreduce_add_layernorm: %zu-byte regions cannot hold %d x %d slots",
+                region_bytes, rows_max, d);
+  if (rows == 0) return ok();
+  if (!x || !s_out || !y) return fail(ND_ERR_INVALID_ARG, "nd_allreduce_add_layernorm: null tensor pointer");
+  if (!aligned16(x) || !aligned16(s_out) || !aligned16(y))
+    return fail(ND_ERR_ALIGNMENT, "nd_allreduce_add_layernorm: x/s_out/y must be 16-byte aligned");
+  nd::CommRegions regs = {};
+  for (int r = 0; r < tp; ++r) {
+    if (!regions[r] || !aligned16(regions[r]))
+      return fail(ND_ERR_INVALID_ARG, "nd_allreduce_add_layernorm: region %d is NULL or unaligned", r);
+    regs.r[r] = regions[r];
+  }
+  int dev = 0;
+  int rc = check_current_device(&dev);
+  if (rc) return rc;
+  int sms = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess)
+    e = nd::launch_allreduce_add_layernorm(
+        static_cast<cudaStream_t>(stream), regs, tp, rank, slot, rows_max,
+        static_cast<const __nv_bfloat16*>(x), bias, gamma, beta,
+        static_cast<__nv_bfloat16*>(s_out), static_cast<__nv_bfloat16*>(y), rows, d, eps, sms,
+        nd::device_error_word());
+  if (e != cudaSuccess) return cuda_fail(e, "nd_allreduce_add_layernorm");
   return ok();
 }
 

@@ -28,6 +28,7 @@ enum DeviceError : int {
   kDevErrTimeoutMma = 2,
   kDevErrTimeoutSoftmax = 3,
   kDevErrTimeoutEpilogue = 4,
+  kDevErrTimeoutComm = 5,       // a peer rank's flag did not arrive in time
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

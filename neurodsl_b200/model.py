@@ -23,7 +23,10 @@ Tensor parallelism (Megatron layout): rank r of `tp` holds heads
 MLP columns [r·F/tp, (r+1)·F/tp) of the up projection and the matching
 columns of the down projection, and vocabulary rows [r·V/tp, ...) of the LM
 head.  The output and down projections produce partial sums that are
-all-reduced (NCCL) before the fused residual + LayerNorm; the LM head gives a
+all-reduced before the fused residual + LayerNorm — with NCCL, or for decode
+batches of up to `nvlink_rows` rows by one kernel that reads the peers'
+partials over NVLink and applies the residual and LayerNorm itself
+(neurodsl_b200.comm, nd_allreduce_add_layernorm); the LM head gives a
 local (max, index) per row that is all-gathered and reduced to the global
 first maximum.  Weights are generated from one seed on every rank and sliced,
 so any `tp` computes the same model.
@@ -68,7 +71,7 @@ class GPT:
     """Weights of one rank plus the buffers of one (batch, length) shape."""
 
     def __init__(self, cfg: GPTConfig, seed=0, device=None, tp=1, rank=0, group=None,
-                 weight_std=0.02, bias_std=0.0):
+                 weight_std=0.02, bias_std=0.0, nvlink_rows=0):
         if cfg.d_head != 64:
             raise ValueError("head_dim must be 64")
         self.cfg = cfg
@@ -125,6 +128,12 @@ class GPT:
         self.lnf_b = torch.zeros(d, device=dev)
         self.w_head = self.wte[self.v0:self.v1]           # tied LM head, local vocab rows
         self._shape = None
+        # Decode batches of up to nvlink_rows rows reduce over NVLink peer
+        # memory (one fused kernel per reduction) instead of NCCL.
+        self.comm = None
+        if tp > 1 and nvlink_rows > 0:
+            from .comm import PeerReduce
+            self.comm = PeerReduce(nvlink_rows, d, group=group, device=dev)
 
     # ------------------------------------------------------------- buffers
     def _alloc(self, B, S, steps):
@@ -236,6 +245,7 @@ class GPT:
         ops.layernorm(xd, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=hd,
                       stats=False)
         Lc = S + t + 1
+        peer = self.comm is not None and B <= self.comm.rows_max
         for i, L in enumerate(self.layers):
             w, bb = L["w_qkv"], L["b_qkv"]
             ops.linear(hd, w[:dl], bb[:dl], out=b["qd"])
@@ -244,14 +254,21 @@ class GPT:
             ops.kv_decode_attn(b["qd"].view(B, H, 64), self.k_cache[i], self.v_cache[i], Lc,
                                k_new=b["kd"].view(B, H, 64), v_new=b["vd"].view(B, H, 64),
                                out=b["ad"].view(B, H, 64), workspace=b["ws"], want_lse=False)
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
+            if peer:
+                ops.linear(b["ad"], L["w_o"], out=self.comm.partial(B))
+                self.comm.add_layernorm(xd, L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, xd, hd)
+                ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
+                ops.linear(b["ud"], L["w_2"], out=self.comm.partial(B))
+                self.comm.add_layernorm(xd, L["b_2"], g_, b_, cfg.eps, xd, hd)
+                continue
             ops.linear(b["ad"], L["w_o"], out=b["pd"])
             self._all_reduce(b["pd"])
             ops.add_layernorm(xd, b["pd"], L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=xd, out=hd)
             ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
             ops.linear(b["ud"], L["w_2"], out=b["pd"])
             self._all_reduce(b["pd"])
-            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
-            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
             ops.add_layernorm(xd, b["pd"], L["b_2"], g_, b_, cfg.eps, s_out=xd, out=hd)
         self._next_token(hd, b["ids"][t + 2] if t + 2 <= steps else b["idx"])
         return b["logits"]
@@ -292,6 +309,14 @@ class GPT:
         process group is destroyed)."""
         self._graphs = []
         self._graphs_key = None
+
+    def close(self):
+        """Release graphs and the NVLink reduction regions (collective when
+        tensor-parallel: every rank calls it before the group is destroyed)."""
+        self.release_graphs()
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
 
 def flops_prefill(cfg: GPTConfig, B, S):

@@ -270,3 +270,50 @@ def add_layernorm(x, p, bias=None, gamma=None, beta=None, eps=1e-5, s_out=None, 
                                        _ptr(out), rows, d, float(eps)))
     return s_out, out
 
+
+# ---- tensor-parallel reduction over NVLink peer memory ----------------------
+def comm_region_bytes(rows_max, d):
+    n = ctypes.c_size_t(0)
+    check(_lib.load().nd_comm_region_bytes(rows_max, d, ctypes.byref(n)))
+    return n.value
+
+
+def comm_slot_offset(slot, rows_max, d):
+    n = ctypes.c_size_t(0)
+    check(_lib.load().nd_comm_slot_offset(slot, rows_max, d, ctypes.byref(n)))
+    return n.value
+
+
+def comm_alloc(nbytes):
+    """A zero-filled region on the current device; returns (pointer, 64-byte IPC handle)."""
+    p = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    check(_lib.load().nd_comm_alloc(nbytes, ctypes.byref(p), h))
+    return p.value, h.raw
+
+
+def comm_open(handle):
+    p = ctypes.c_void_p()
+    check(_lib.load().nd_comm_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(p)))
+    return p.value
+
+
+def comm_close(ptr):
+    check(_lib.load().nd_comm_close(ctypes.c_void_p(ptr)))
+
+
+def comm_free(ptr):
+    check(_lib.load().nd_comm_free(ctypes.c_void_p(ptr)))
+
+
+def allreduce_add_layernorm(regions, rank, region_bytes, rows_max, slot, x, bias, gamma, beta,
+                            s_out, out, eps=1e-5, stream=None):
+    """s_out = x + Σ_r (rank r's partial in `slot`) + bias, out = LayerNorm(s_out)."""
+    _need(x, "x", torch.bfloat16, 2)
+    rows, d = x.shape
+    arr = (ctypes.c_void_p * len(regions))(*regions)
+    check(_lib.load().nd_allreduce_add_layernorm(
+        _stream(stream), arr, len(regions), rank, region_bytes, rows_max, slot, _ptr(x),
+        _ptr(bias), _ptr(gamma), _ptr(beta), _ptr(s_out), _ptr(out), rows, d, float(eps)))
+    return s_out, out
+

@@ -3,7 +3,10 @@ same seed must reproduce the one-GPU model — LM-head logits within relative
 L2 1e-2 and max-abs 5e-2 (logits spread ~0.8 here; each rank's partial sum
 is rounded to bf16 before the all-reduce, one extra rounding per sub-layer)
 and the greedy tokens wherever the one-GPU top-2 margin exceeds 5e-2 — and
-its graph-captured decode must give the same tokens as its eager decode.  Skipped with fewer than 2 GPUs.
+its graph-captured decode must give the same tokens as its eager decode.
+The same holds for the tp=2 model whose decode reductions run over NVLink
+peer memory (nd_allreduce_add_layernorm) instead of NCCL.  Skipped with fewer
+than 2 GPUs.
 Each rank runs the same collectives in the same order; the process group has
 a 60 s timeout so a lost rank ends the others with an error.
 """
@@ -64,11 +67,32 @@ def _rank_main(rank, world, port, out_dir):
             full.append(torch.cat(parts, dim=1).cpu().numpy())
         graphed = m.generate(ids, STEPS, graph_chunk=2).clone()
         torch.cuda.synchronize()
-        m.release_graphs()
+        m.close()
         if rank == 0:
             np.save(os.path.join(out_dir, "logits.npy"), np.stack(full))
             np.save(os.path.join(out_dir, "tokens.npy"), tokens.cpu().numpy())
             np.save(os.path.join(out_dir, "graphed.npy"), graphed.cpu().numpy())
+        # decode reductions over NVLink peer memory
+        m2 = GPT(GPTConfig(**CFG), seed=21, device=dev, tp=world, rank=rank,
+                 group=dist.group.WORLD, weight_std=0.05, bias_std=0.02, nvlink_rows=8)
+        logits2, tokens2 = _run(m2, ids)
+        full2 = []
+        for lg in logits2:
+            parts = [torch.empty_like(lg) for _ in range(world)]
+            dist.all_gather(parts, lg)
+            full2.append(torch.cat(parts, dim=1).cpu().numpy())
+        graphed2 = m2.generate(ids, STEPS, graph_chunk=2).clone()
+        again2 = m2.generate(ids, STEPS, graph_chunk=2).clone()
+        torch.cuda.synchronize()
+        from neurodsl_b200 import ops
+        err = ops.device_error()
+        m2.close()
+        if rank == 0:
+            np.save(os.path.join(out_dir, "logits_nv.npy"), np.stack(full2))
+            np.save(os.path.join(out_dir, "tokens_nv.npy"), tokens2.cpu().numpy())
+            np.save(os.path.join(out_dir, "graphed_nv.npy"),
+                    np.stack([graphed2.cpu().numpy(), again2.cpu().numpy()]))
+            np.save(os.path.join(out_dir, "err_nv.npy"), np.array([err]))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -99,3 +123,15 @@ def test_tp2_matches_single_gpu(tmp_path):
         if (tokens[:, :k] == ref_tokens[:, :k]).all():
             assert close(logits[k], ref_logits[k]), k
             np.testing.assert_array_equal(tokens[clear, k], ref_tokens[clear, k])
+    # the NVLink-reduced decode
+    assert int(np.load(tmp_path / "err_nv.npy")[0]) == 0
+    logits_nv = np.load(tmp_path / "logits_nv.npy")
+    tokens_nv = np.load(tmp_path / "tokens_nv.npy")
+    g_nv = np.load(tmp_path / "graphed_nv.npy")
+    np.testing.assert_array_equal(g_nv[0], tokens_nv)
+    np.testing.assert_array_equal(g_nv[1], tokens_nv)
+    for k in range(STEPS):
+        clear = top2_margin(ref_logits[k]) > 5e-2
+        if (tokens_nv[:, :k] == ref_tokens[:, :k]).all():
+            assert close(logits_nv[k], ref_logits[k]), k
+            np.testing.assert_array_equal(tokens_nv[clear, k], ref_tokens[clear, k])
