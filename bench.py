@@ -208,7 +208,8 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
 
     from neurodsl_b200.model import GPT, decode_weight_bytes, flops_prefill
     group = torch.distributed.group.WORLD if (pg is not None and tp > 1) else None
-    model = GPT(cfg, seed=0, device=dev, tp=tp, rank=rank if tp > 1 else 0, group=group)
+    model = GPT(cfg, seed=0, device=dev, tp=tp, rank=rank if tp > 1 else 0, group=group,
+                nvlink_rows=B if tp > 1 else 0)
     gen = torch.Generator(device=dev).manual_seed(99 + (0 if tp > 1 else rank))
     ids = torch.randint(0, cfg.vocab, (B, S), device=dev, dtype=torch.int32, generator=gen)
     graphs = True
@@ -241,7 +242,7 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
     p_ms = max_over_ranks(min(tp_ms))
     d_ms = max_over_ranks(min(td_ms))
     tokens = model.tokens()[:, :4].cpu().tolist()
-    model.release_graphs()
+    model.close()
     del model
     torch.cuda.synchronize()
     replicas = 1 if tp > 1 else world
@@ -255,6 +256,8 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
         "workload": f"{name}: {cfg.n_layer} layers d={cfg.d_model} {cfg.n_head}x64 heads "
                     f"F={cfg.d_ff} vocab {cfg.vocab}, batch {B}, prompt {S}, {steps} greedy tokens",
         "parallelism": f"tp{tp}" if tp > 1 else f"dp{world} replicas",
+        "reduction": ("prefill: NCCL all-reduce; decode: one-shot NVLink peer reduction fused "
+                      "with residual + LayerNorm") if tp > 1 else None,
         "scaling": "strong" if tp > 1 else "weak",
         "prefill": {"value": replicas * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
                     "roofline": {"bound": "tensor", "achieved": p_tflops / world,
