@@ -25,11 +25,15 @@
  *   nd_kv_decode_attn   no reference counterpart (KV-cache decode is absent);
  *                       defined as flash_attn_fwd_cpu_simple!
  *                       (src/flash_attention.jl:49-69) with one query row
+ *   nd_kv_decode_attn_qkv  nd_kv_decode_attn reading a fused QKV projection row
  *   nd_kv_append        no reference counterpart (cache append for decode)
+ *   nd_set_pdl          no reference counterpart (launch mode of the decode steps)
  *   nd_gemm_bias_act    :linear src/dispatch.jl:363-384, :fused_matmul_add
  *                       :281-296, :matmul trans_b :213-243, residual :add
  *                       :386-417, fused_linear_gelu notebook/compiler.ipynb
  *                       cell 15 (rule name src/compiler_config.jl:154-158)
+ *   nd_ln_gemm          residual :add src/dispatch.jl:386-417 + :layernorm +
+ *                       :linear :363-384 for a decode step's few rows
  *   nd_layernorm        the :layernorm rule symbol src/compiler_config.jl:168-172
  *                       (the reference ships only RMSNorm, rmsnorm_fwd!
  *                       src/kernels.jl:48-64,104-131, used by :rmsnorm
@@ -142,6 +146,34 @@ int nd_kv_decode_attn(void *stream, const void *q, const void *k_new, const void
                       size_t workspace_bytes);
 
 /*
+ * KV-cache decode attention straight from a fused QKV projection.
+ *   Row b of qkv (bf16, rows qkv_ld elements apart; qkv_ld >= 3*H*D and a
+ *   multiple of 8) holds q [H][D], then k_new [H][D], then v_new [H][D]:
+ *   the output of one linear layer whose weight stacks the query, key and
+ *   value projections.  Same results as nd_kv_decode_attn with q, k_new and
+ *   v_new taken from those column blocks (k_new / v_new are appended at
+ *   position L-1); the other arguments are those of nd_kv_decode_attn.
+ */
+int nd_kv_decode_attn_qkv(void *stream, const void *qkv, int64_t qkv_ld, void *k_cache,
+                          void *v_cache, void *out, int o_dtype, float *lse, int B, int H, int L,
+                          int L_max, int D, float scale, void *workspace, size_t workspace_bytes);
+
+/*
+ * Programmatic dependent launch (PDL) for the calling host thread, off by
+ * default; *previous (if not NULL) receives the earlier setting.  When on,
+ * the decode-step kernels (nd_gemm_bias_act with M <= 32, nd_layernorm,
+ * nd_add_layernorm, nd_allreduce_add_layernorm, nd_embed, nd_argmax and the
+ * nd_kv_decode_attn family) are launched so that each may start while the
+ * previous kernel on the stream is still running.  Before the previous
+ * kernel finishes they read only operands the caller promises are not being
+ * written: weights, biases and LayerNorm parameters, and in decode attention
+ * the cached keys/values below position L-1.  Everything else (activations,
+ * all writes) waits for the previous kernel.  Launches captured in a CUDA
+ * graph keep the setting they were captured with.
+ */
+int nd_set_pdl(int enable, int *previous);
+
+/*
  * Allocation-free KV-cache decode attention.  No counterpart in the
  * reference: it exists for callers that may not allocate device memory while
  * they run decode — a host runtime whose device memory all comes from its
@@ -182,6 +214,20 @@ int nd_kv_append(void *stream, const void *k_new, const void *v_new, void *k_cac
 int nd_gemm_bias_act(void *stream, const void *A, const void *W, const float *bias,
                      const void *residual, int residual_dtype, void *Y, int y_dtype, int M, int N,
                      int K, int act);
+
+/*
+ * Few-row linear layer with the residual add and LayerNorm in its prologue
+ * (the decode-step form of residual :add + :layernorm + :linear):
+ *   s = bf16(x + (p + p_bias));  Y = act(LayerNorm(s) · Wᵀ + bias)
+ *   x, p [M][K] bf16 (p NULL: s = x); p_bias, gamma, beta, bias fp32 or NULL
+ *   (gamma NULL = 1, beta NULL = 0); LayerNorm over K with `eps`, computed
+ *   like nd_add_layernorm.  s_out [M][K] bf16 receives s when not NULL and
+ *   must not overlap x or p.  W [N][K] bf16; Y [M][N] in y_dtype.
+ *   M <= 32, K % 32 == 0 and K <= 1024; every pointer 16-byte aligned.
+ */
+int nd_ln_gemm(void *stream, const void *x, const void *p, const float *p_bias,
+               const float *gamma, const float *beta, float eps, void *s_out, const void *W,
+               const float *bias, void *Y, int y_dtype, int M, int N, int K, int act);
 
 /*
  * LayerNorm over the last dimension of x [rows][d]:

@@ -50,8 +50,12 @@ SIGNATURES = {
                                _vp, _sz]),
     "nd_kv_decode_attn_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i,
                                        _i, _i, _f]),
+    "nd_kv_decode_attn_qkv": (_i, [_vp, _vp, ctypes.c_int64, _vp, _vp, _vp, _i, _vp, _i, _i, _i,
+                                   _i, _i, _f, _vp, _sz]),
+    "nd_set_pdl": (_i, [_i, ctypes.POINTER(_i)]),
     "nd_kv_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
+    "nd_ln_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_layernorm": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _f]),
     "nd_convert_2d": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i]),
     "nd_embed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),

@@ -18,6 +18,7 @@
 #include "flash_fwd.h"
 #include "gemm.h"
 #include "kv_decode.h"
+#include "launch.cuh"
 #include "layernorm.h"
 #include "model_ops.h"
 #include "tp_comm.h"
@@ -40,6 +41,11 @@ int* device_error_word() {
   }
   return cached[dev];
 }
+namespace {
+thread_local bool t_pdl = false;
+}  // namespace
+bool pdl_enabled() { return t_pdl; }
+void set_pdl_enabled(bool on) { t_pdl = on; }
 }  // namespace nd
 
 namespace {
@@ -169,6 +175,50 @@ cudaError_t launch_convert(cudaStream_t st, const void* src, void* dst, int rows
 bool valid_dtype(int t) { return t == ND_F32 || t == ND_BF16; }
 
 }  // namespace
+
+static int kv_decode_impl(const char* fn, void* stream, const void* q, const void* k_new,
+                          const void* v_new, long long qkv_ld, void* k_cache, void* v_cache,
+                          void* out, int o_dtype, float* lse, int B, int H, int L, int L_max,
+                          int D, float scale, void* workspace, size_t workspace_bytes) {
+  if (B < 0 || H < 0) return fail(ND_ERR_INVALID_ARG, "%s: negative size", fn);
+  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "%s: head_dim %d not supported (64 only)", fn, D);
+  if (L < 1 || L > L_max)
+    return fail(ND_ERR_SHAPE, "%s: need 1 <= L <= L_max (L=%d, L_max=%d)", fn, L, L_max);
+  if (!valid_dtype(o_dtype)) return fail(ND_ERR_UNSUPPORTED, "%s: bad o_dtype %d", fn, o_dtype);
+  if ((k_new == nullptr) != (v_new == nullptr))
+    return fail(ND_ERR_INVALID_ARG, "%s: k_new and v_new must both be given or both NULL", fn);
+  if (static_cast<long long>(B) * H > 65535)
+    return fail(ND_ERR_SHAPE, "%s: B*H = %lld exceeds 65535", fn, static_cast<long long>(B) * H);
+  if (B == 0 || H == 0) return ok();
+  if (!q || !k_cache || !v_cache || !out) return fail(ND_ERR_INVALID_ARG, "%s: null tensor pointer", fn);
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) ||
+      (k_new && (!aligned16(k_new) || !aligned16(v_new))))
+    return fail(ND_ERR_ALIGNMENT, "%s: tensors must be 16-byte aligned", fn);
+  int dev = 0;
+  int rc = check_current_device(&dev);
+  if (rc) return rc;
+  const size_t need = nd::kv_decode_workspace_bytes(B, H, L);
+  void* ws = workspace;
+  if (need > 0) {
+    if (ws == nullptr) {
+      rc = owned_workspace(dev, need, &ws);
+      if (rc) return rc;
+    } else if (workspace_bytes < need) {
+      return fail(ND_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu needed", fn, workspace_bytes, need);
+    } else if (!aligned16(ws)) {
+      return fail(ND_ERR_ALIGNMENT, "%s: workspace must be 16-byte aligned", fn);
+    }
+  }
+  cudaError_t e = nd::launch_kv_decode(
+      static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(q),
+      static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new),
+      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), out,
+      o_dtype == ND_F32, lse, B, H, L, L_max, scale, ws, qkv_ld);
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return ok();
+}
+
+
 
 extern "C" {
 
@@ -303,41 +353,37 @@ __attribute__((visibility("default"))) int nd_kv_decode_attn(
     void* stream, const void* q, const void* k_new, const void* v_new, void* k_cache,
     void* v_cache, void* out, int o_dtype, float* lse, int B, int H, int L, int L_max, int D,
     float scale, void* workspace, size_t workspace_bytes) {
-  if (B < 0 || H < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn: negative size");
-  if (D != 64) return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn: head_dim %d not supported (64 only)", D);
-  if (L < 1 || L > L_max)
-    return fail(ND_ERR_SHAPE, "nd_kv_decode_attn: need 1 <= L <= L_max (L=%d, L_max=%d)", L, L_max);
-  if (!valid_dtype(o_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn: bad o_dtype %d", o_dtype);
-  if ((k_new == nullptr) != (v_new == nullptr))
-    return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn: k_new and v_new must both be given or both NULL");
-  if (static_cast<long long>(B) * H > 65535)
-    return fail(ND_ERR_SHAPE, "nd_kv_decode_attn: B*H = %lld exceeds 65535", static_cast<long long>(B) * H);
+  return kv_decode_impl("nd_kv_decode_attn", stream, q, k_new, v_new, 0, k_cache, v_cache, out,
+                        o_dtype, lse, B, H, L, L_max, D, scale, workspace, workspace_bytes);
+}
+
+// Decode attention straight from a fused QKV projection: row b of qkv holds
+// q, then k_new, then v_new (H*D values each), rows qkv_ld elements apart.
+__attribute__((visibility("default"))) int nd_kv_decode_attn_qkv(
+    void* stream, const void* qkv, int64_t qkv_ld, void* k_cache, void* v_cache, void* out,
+    int o_dtype, float* lse, int B, int H, int L, int L_max, int D, float scale, void* workspace,
+    size_t workspace_bytes) {
+  if (B < 0 || H < 0) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn_qkv: negative size");
+  if (D != 64)
+    return fail(ND_ERR_UNSUPPORTED, "nd_kv_decode_attn_qkv: head_dim %d not supported (64 only)", D);
   if (B == 0 || H == 0) return ok();
-  if (!q || !k_cache || !v_cache || !out) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn: null tensor pointer");
-  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out) ||
-      (k_new && (!aligned16(k_new) || !aligned16(v_new))))
-    return fail(ND_ERR_ALIGNMENT, "nd_kv_decode_attn: tensors must be 16-byte aligned");
-  int dev = 0;
-  int rc = check_current_device(&dev);
-  if (rc) return rc;
-  const size_t need = nd::kv_decode_workspace_bytes(B, H, L);
-  void* ws = workspace;
-  if (need > 0) {
-    if (ws == nullptr) {
-      rc = owned_workspace(dev, need, &ws);
-      if (rc) return rc;
-    } else if (workspace_bytes < need) {
-      return fail(ND_ERR_WORKSPACE, "nd_kv_decode_attn: workspace %zu bytes < %zu needed", workspace_bytes, need);
-    } else if (!aligned16(ws)) {
-      return fail(ND_ERR_ALIGNMENT, "nd_kv_decode_attn: workspace must be 16-byte aligned");
-    }
-  }
-  cudaError_t e = nd::launch_kv_decode(
-      static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(q),
-      static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new),
-      static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), out,
-      o_dtype == ND_F32, lse, B, H, L, L_max, scale, ws);
-  if (e != cudaSuccess) return cuda_fail(e, "nd_kv_decode_attn");
+  if (qkv == nullptr) return fail(ND_ERR_INVALID_ARG, "nd_kv_decode_attn_qkv: qkv is NULL");
+  if (qkv_ld < 3LL * H * D || qkv_ld % 8 != 0)
+    return fail(ND_ERR_SHAPE,
+                "nd_kv_decode_attn_qkv: row stride %lld must be >= 3*H*D = %lld and a multiple of 8",
+                static_cast<long long>(qkv_ld), 3LL * H * D);
+  const char* base = static_cast<const char*>(qkv);
+  const size_t block = static_cast<size_t>(H) * D * sizeof(__nv_bfloat16);
+  return kv_decode_impl("nd_kv_decode_attn_qkv", stream, qkv, base + block, base + 2 * block,
+                        static_cast<long long>(qkv_ld), k_cache, v_cache, out, o_dtype, lse, B, H,
+                        L, L_max, D, scale, workspace, workspace_bytes);
+}
+
+// Programmatic dependent launch for this host thread's later launches of the
+// decode-step kernels (see launch.cuh for the rule those kernels follow).
+__attribute__((visibility("default"))) int nd_set_pdl(int enable, int* previous) {
+  if (previous != nullptr) *previous = nd::pdl_enabled() ? 1 : 0;
+  nd::set_pdl_enabled(enable != 0);
   return ok();
 }
 
@@ -439,6 +485,48 @@ __attribute__((visibility("default"))) int nd_gemm_bias_act(void* stream, const 
                                   static_cast<const __nv_bfloat16*>(W), bias, residual,
                                   residual_dtype == ND_F32, Y, y_dtype == ND_F32, M, N, K, act, &msg);
   if (e != cudaSuccess) return cuda_fail(e, "nd_gemm_bias_act", msg);
+  return ok();
+}
+
+// Few-row linear layer with the residual add and LayerNorm in its prologue.
+__attribute__((visibility("default"))) int nd_ln_gemm(void* stream, const void* x, const void* p,
+                                                      const float* p_bias, const float* gamma,
+                                                      const float* beta, float eps, void* s_out,
+                                                      const void* W, const float* bias, void* Y,
+                                                      int y_dtype, int M, int N, int K, int act) {
+  if (M < 0 || N < 0 || K < 0) return fail(ND_ERR_INVALID_ARG, "nd_ln_gemm: negative size");
+  if (act < ND_ACT_NONE || act > ND_ACT_GELU_ERF)
+    return fail(ND_ERR_UNSUPPORTED, "nd_ln_gemm: bad act %d", act);
+  if (!valid_dtype(y_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_ln_gemm: bad y dtype %d", y_dtype);
+  if (M > nd::kLnGemmMaxRows)
+    return fail(ND_ERR_SHAPE, "nd_ln_gemm: M = %d rows, at most %d", M, nd::kLnGemmMaxRows);
+  if (K == 0 || K % 32 != 0 || K > nd::kLnGemmMaxK)
+    return fail(ND_ERR_SHAPE, "nd_ln_gemm: K = %d must be a multiple of 32 in [32, %d]", K,
+                nd::kLnGemmMaxK);
+  if (M == 0 || N == 0) return ok();
+  if (!x || !W || !Y) return fail(ND_ERR_INVALID_ARG, "nd_ln_gemm: null tensor pointer");
+  if (!aligned16(x) || !aligned16(W) || !aligned16(Y) || (p && !aligned16(p)) ||
+      (s_out && !aligned16(s_out)) || (p_bias && !aligned16(p_bias)) ||
+      (gamma && !aligned16(gamma)) || (beta && !aligned16(beta)))
+    return fail(ND_ERR_ALIGNMENT, "nd_ln_gemm: tensors and parameter vectors must be 16-byte aligned");
+  if (s_out) {
+    // every CTA reads x and p while CTA 0 writes s_out
+    const size_t bytes = static_cast<size_t>(M) * K * 2;
+    auto overlaps = [&](const void* a) {
+      const uintptr_t u = reinterpret_cast<uintptr_t>(a), v = reinterpret_cast<uintptr_t>(s_out);
+      return a != nullptr && u < v + bytes && v < u + bytes;
+    };
+    if (overlaps(x) || overlaps(p))
+      return fail(ND_ERR_INVALID_ARG, "nd_ln_gemm: s_out must not overlap x or p");
+  }
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_ln_gemm(
+      static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x),
+      static_cast<const __nv_bfloat16*>(p), p_bias, gamma, beta, eps,
+      static_cast<__nv_bfloat16*>(s_out), static_cast<const __nv_bfloat16*>(W), bias, Y,
+      y_dtype == ND_F32, M, N, K, act);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_ln_gemm");
   return ok();
 }
 

@@ -21,7 +21,11 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <vector>
+
 #include "gemm.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "tma.h"
 
@@ -462,16 +466,25 @@ cudaError_t launch_bn(int BN, int act, cudaStream_t stream, const CUtensorMap& t
 
 // ---- skinny path: M <= 32 rows (decode-time activations) -------------------
 // A 128-row tensor-core tile would compute mostly padding and leave N/BN
-// CTAs streaming the weights; with M <= 32 the op is bound by reading W.
-// Here a CTA owns 8 rows of W and its 8 warps split K, so N/8 CTAs keep many
-// 16-byte loads of W in flight.  Each lane reads 16 bytes (8 k values) of
-// one W row and of each A row per 32-wide k chunk and feeds two
-// mma.m16n8k16 steps; the k values are assigned to fragment positions by
-// the same permutation for A and W, which leaves every dot product intact.
-// The warps' 16x8 (or 32x8) partial tiles are summed through shared memory
-// and the epilogue adds bias, activation and residual like the main path.
+// CTAs streaming the weights; with M <= 32 the op is bound by reading W, and
+// at decode sizes (a few MB of W) by the latency of that read.
+// A cluster of `ksplit` CTAs owns 8 rows of W; each CTA takes a contiguous
+// 1/ksplit of the K range and its 8 warps split that.  Each lane reads 16
+// bytes (8 k values) of one W row and of each A row per 32-wide k chunk and
+// feeds two mma.m16n8k16 steps; the k values are assigned to fragment
+// positions by the same permutation for A and W, which leaves every dot
+// product intact.  The warps' 16x8 (or 32x8) partial tiles are summed
+// through shared memory, the cluster's tiles by CTA rank 0 through
+// distributed shared memory (rank order, so the result does not depend on
+// timing), and the epilogue adds bias, activation and residual like the main
+// path.  ksplit is chosen so that a warp's loads for its whole share of K go
+// out together (one round trip to memory).
+// Under programmatic dependent launch the first batch of W loads is issued
+// before pdl_wait(): W is a constant operand; A and the residual are read
+// after it.
 constexpr int kSkinnyWarps = 8;
 constexpr int kSkinnyBatch = 4;  // k chunks whose loads are issued together
+constexpr int kSkinnyMaxSplit = 8;
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
@@ -494,9 +507,26 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32)
                        int residual_f32, void* __restrict__ Y, int M, int N, int K) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;  // fragment group (row / column) and slot
-  const int n0 = blockIdx.x * 8;
+  const int ksplit = static_cast<int>(cluster_nctarank());
+  const int kr = static_cast<int>(cluster_ctarank());
+  const int n0 = (blockIdx.x / ksplit) * 8;
   const bool w_ok = n0 + g < N;
   const __nv_bfloat16* wrow = W + static_cast<size_t>(w_ok ? n0 + g : 0) * K + t * 8;
+  const int n_chunks = K / 32;
+  const int per = (n_chunks + ksplit - 1) / ksplit;
+  const int cbeg = kr * per;
+  const int cend = min(n_chunks, cbeg + per);
+  constexpr int kStep = kSkinnyWarps * kSkinnyBatch;
+
+  uint4 wv[kSkinnyBatch];
+#pragma unroll
+  for (int u = 0; u < kSkinnyBatch; ++u) {
+    const int ch = cbeg + warp + u * kSkinnyWarps;
+    wv[u] = ldg16_or_zero(wrow + ch * 32, ch < cend && w_ok);
+  }
+  pdl_wait();
+  pdl_trigger();
+
   const __nv_bfloat16* arow[kMB][2];
   bool a_ok[kMB][2];
 #pragma unroll
@@ -512,14 +542,13 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32)
   for (int mb = 0; mb < kMB; ++mb)
 #pragma unroll
     for (int i = 0; i < 4; ++i) c[mb][i] = 0.f;
-  const int n_chunks = K / 32;
-  for (int c0 = warp; c0 < n_chunks; c0 += kSkinnyWarps * kSkinnyBatch) {
-    uint4 wv[kSkinnyBatch], av[kSkinnyBatch][kMB][2];
+  for (int c0 = cbeg + warp; c0 < cend; c0 += kStep) {
+    uint4 av[kSkinnyBatch][kMB][2];
 #pragma unroll
     for (int u = 0; u < kSkinnyBatch; ++u) {
       const int ch = c0 + u * kSkinnyWarps;
-      const bool in = ch < n_chunks;
-      wv[u] = ldg16_or_zero(wrow + ch * 32, in && w_ok);
+      const bool in = ch < cend;
+      if (c0 != cbeg + warp) wv[u] = ldg16_or_zero(wrow + ch * 32, in && w_ok);
 #pragma unroll
       for (int mb = 0; mb < kMB; ++mb)
 #pragma unroll
@@ -541,6 +570,7 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32)
   }
   // sum the warps' partial tiles: red[warp][m][n] for the 16·kMB x 8 tile
   __shared__ float red[kSkinnyWarps][kMB * 16][8];
+  __shared__ float part[kMB * 16 * 8];
 #pragma unroll
   for (int mb = 0; mb < kMB; ++mb) {
     red[warp][mb * 16 + g][2 * t] = c[mb][0];
@@ -550,34 +580,58 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32)
   }
   __syncthreads();
   for (int o = threadIdx.x; o < kMB * 16 * 8; o += blockDim.x) {
-    const int m = o >> 3, n = n0 + (o & 7);
-    if (m >= M || n >= N) continue;
     float z = 0.f;
 #pragma unroll
-    for (int w = 0; w < kSkinnyWarps; ++w) z += red[w][m][o & 7];
-    if (bias != nullptr) z += bias[n];
-    z = act1<kAct>(z);
-    const size_t idx = static_cast<size_t>(m) * N + n;
-    if constexpr (kRes)
-      z += residual_f32 ? static_cast<const float*>(residual)[idx]
-                        : __bfloat162float(static_cast<const __nv_bfloat16*>(residual)[idx]);
-    if constexpr (kOutF32) static_cast<float*>(Y)[idx] = z;
-    else static_cast<__nv_bfloat16*>(Y)[idx] = __float2bfloat16_rn(z);
+    for (int w = 0; w < kSkinnyWarps; ++w) z += red[w][o >> 3][o & 7];
+    part[o] = z;
   }
+  // every CTA of the cluster reaches both barriers (no early exit above)
+  if (ksplit > 1) cluster_sync();
+  else __syncthreads();
+  if (kr == 0) {
+    for (int o = threadIdx.x; o < kMB * 16 * 8; o += blockDim.x) {
+      const int m = o >> 3, n = n0 + (o & 7);
+      float z = part[o];
+      for (int r = 1; r < ksplit; ++r) z += ld_dsmem_f32(&part[o], static_cast<uint32_t>(r));
+      if (m >= M || n >= N) continue;
+      if (bias != nullptr) z += bias[n];
+      z = act1<kAct>(z);
+      const size_t idx = static_cast<size_t>(m) * N + n;
+      if constexpr (kRes)
+        z += residual_f32 ? static_cast<const float*>(residual)[idx]
+                          : __bfloat162float(static_cast<const __nv_bfloat16*>(residual)[idx]);
+      if constexpr (kOutF32) static_cast<float*>(Y)[idx] = z;
+      else static_cast<__nv_bfloat16*>(Y)[idx] = __float2bfloat16_rn(z);
+    }
+  }
+  // rank 0 has read every peer's tile before any CTA of the cluster exits
+  if (ksplit > 1) cluster_sync();
+}
+
+// K split across a cluster: enough CTAs that each warp's share of K is one
+// batch of loads, at most kSkinnyMaxSplit, and only while the grid has fewer
+// CTAs than two per SM (a larger grid already keeps every SM's loads busy).
+int skinny_ksplit(int N, int K) {
+  const int n_chunks = K / 32;
+  const int nblk = (N + 7) / 8;
+  int ks = (n_chunks + kSkinnyWarps * kSkinnyBatch - 1) / (kSkinnyWarps * kSkinnyBatch);
+  if (ks > kSkinnyMaxSplit) ks = kSkinnyMaxSplit;
+  if (ks < 1) ks = 1;
+  if (nblk >= 2 * 148) ks = 1;
+  return ks;
 }
 
 template <int kMB, bool kOutF32, int kAct>
 cudaError_t launch_skinny_act(cudaStream_t stream, const __nv_bfloat16* A, const __nv_bfloat16* W,
                               const float* bias, const void* residual, bool residual_f32, void* Y,
                               int M, int N, int K) {
-  const dim3 grid((N + 7) / 8);
+  const int ks = skinny_ksplit(N, K);
+  const dim3 grid(((N + 7) / 8) * ks);
   if (residual != nullptr)
-    skinny_gemm_kernel<kMB, kOutF32, kAct, true><<<grid, kSkinnyWarps * 32, 0, stream>>>(
-        A, W, bias, residual, residual_f32 ? 1 : 0, Y, M, N, K);
-  else
-    skinny_gemm_kernel<kMB, kOutF32, kAct, false><<<grid, kSkinnyWarps * 32, 0, stream>>>(
-        A, W, bias, residual, 0, Y, M, N, K);
-  return cudaGetLastError();
+    return launch_ex(skinny_gemm_kernel<kMB, kOutF32, kAct, true>, grid, dim3(kSkinnyWarps * 32), 0,
+                     stream, ks, true, A, W, bias, residual, residual_f32 ? 1 : 0, Y, M, N, K);
+  return launch_ex(skinny_gemm_kernel<kMB, kOutF32, kAct, false>, grid, dim3(kSkinnyWarps * 32), 0,
+                   stream, ks, true, A, W, bias, residual, 0, Y, M, N, K);
 }
 
 template <int kMB, bool kOutF32>
@@ -593,6 +647,321 @@ cudaError_t launch_skinny(int act, cudaStream_t stream, const __nv_bfloat16* A,
       return launch_skinny_act<kMB, kOutF32, ND_ACT_GELU_ERF>(stream, A, W, bias, residual, residual_f32, Y, M, N, K);
     default:
       return launch_skinny_act<kMB, kOutF32, ND_ACT_NONE>(stream, A, W, bias, residual, residual_f32, Y, M, N, K);
+  }
+}
+
+// ---- LayerNorm-prologue linear for few rows (decode steps) ----------------
+// Y = act(LN(x + p + p_bias) · Wᵀ + bias) for M <= 32 rows: the residual add,
+// the LayerNorm and the linear layer after it in one kernel, so a decode step
+// needs no separate residual + LayerNorm launch.  Persistent: each CTA
+//   1. issues the W loads of its first 8-row tile and copies p_bias, gamma and
+//      beta to shared memory (constant operands: before the previous kernel
+//      has finished, under programmatic dependent launch),
+//   2. forms s = x + (p + p_bias), rounded to bf16 as the residual stream
+//      (CTA 0 stores it to s_out), and LayerNorm(s) in the arithmetic of the
+//      separate residual + LayerNorm kernel (same per-lane order of the
+//      sums), into shared memory as the bf16 A operand; a warp per row, the
+//      row held in registers, all of its x / p loads in flight together (rows
+//      padded by 64 bytes so the 16-byte fragment loads of a quarter-warp hit
+//      distinct banks; rows >= M are zero),
+//   3. loops over 8-row tiles of W: 8 warps split K, mma.m16n8k16 with the k
+//      permutation of the skinny path, and the next tile's W loads issued
+//      before this tile's reduction and epilogue, so the latency of the weight
+//      stream overlaps them.
+constexpr int kLnGemmWarps = 8;
+constexpr int kLnGemmBatch = 4;   // k chunks of 32 per warp whose loads go out together
+constexpr int kLnGemmVecs = 4;    // 16-byte pieces of a row per lane loaded together
+
+__device__ __forceinline__ void bf16x8_to_f32_(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ uint4 pack8_bf16(const float (&v)[8]) {
+  uint4 r;
+  r.x = pack_bf16x2(v[0], v[1]);
+  r.y = pack_bf16x2(v[2], v[3]);
+  r.z = pack_bf16x2(v[4], v[5]);
+  r.w = pack_bf16x2(v[6], v[7]);
+  return r;
+}
+
+// shared memory: A rows [kMB*16][K + 32] bf16 | params [3][K] f32 | red [8][kMB*16][8] f32
+template <int kMB>
+__host__ __device__ constexpr size_t ln_gemm_par_offset(int K) {
+  return static_cast<size_t>(kMB) * 16 * (K + 32) * 2;
+}
+template <int kMB>
+__host__ __device__ constexpr size_t ln_gemm_red_offset(int K) {
+  return ln_gemm_par_offset<kMB>(K) + static_cast<size_t>(3) * K * 4;
+}
+template <int kMB>
+__host__ __device__ constexpr size_t ln_gemm_smem_bytes(int K) {
+  return ln_gemm_red_offset<kMB>(K) + static_cast<size_t>(kLnGemmWarps) * kMB * 16 * 8 * 4;
+}
+
+template <int kMB, bool kOutF32, int kAct>
+__global__ void __launch_bounds__(kLnGemmWarps * 32)
+    ln_gemm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ p,
+                   const float* __restrict__ p_bias, const float* __restrict__ gamma,
+                   const float* __restrict__ beta, float eps, __nv_bfloat16* __restrict__ s_out,
+                   const __nv_bfloat16* __restrict__ W, const float* __restrict__ bias,
+                   void* __restrict__ Y, int M, int N, int K) {
+  extern __shared__ __align__(128) unsigned char ln_smem[];
+  const int pitch = K + 32;  // bf16 elements per staged row
+  __nv_bfloat16* As = reinterpret_cast<__nv_bfloat16*>(ln_smem);
+  float* par = reinterpret_cast<float*>(ln_smem + ln_gemm_par_offset<kMB>(K));  // p_bias|gamma|beta
+  float* red = reinterpret_cast<float*>(ln_smem + ln_gemm_red_offset<kMB>(K));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int nblk = (N + 7) / 8;
+  const int n_chunks = K / 32;
+  constexpr int kStep = kLnGemmWarps * kLnGemmBatch;
+
+  auto load_w = [&](int tile, int c0, uint4 (&wv)[kLnGemmBatch]) {
+    const int n = tile * 8 + g;
+    const bool ok = n < N;
+    const __nv_bfloat16* wrow = W + static_cast<size_t>(ok ? n : 0) * K + t * 8;
+#pragma unroll
+    for (int u = 0; u < kLnGemmBatch; ++u) {
+      const int ch = c0 + u * kLnGemmWarps;
+      wv[u] = (ok && ch < n_chunks) ? __ldg(reinterpret_cast<const uint4*>(wrow + ch * 32))
+                                    : make_uint4(0, 0, 0, 0);
+    }
+  };
+
+  int tile = blockIdx.x;
+  uint4 wv[kLnGemmBatch];
+  if (tile < nblk) load_w(tile, warp, wv);
+  const int nvec = K >> 3;  // 16-byte pieces of a row (<= 32 * kLnGemmVecs)
+  {
+    // p_bias | gamma | beta to shared memory as par[(a * 8 + e) * nvec + c]
+    // (array a, element e of piece c): a lane reading its piece's element e
+    // and its neighbours' hits consecutive words.  All of a thread's float4
+    // loads are issued before the first store (16-byte aligned bases).
+    constexpr int kParLoads = (3 * kLnGemmMaxK / 4 + kLnGemmWarps * 32 - 1) / (kLnGemmWarps * 32);
+    const int per = K / 4;
+    float4 pv[kParLoads];
+#pragma unroll
+    for (int j = 0; j < kParLoads; ++j) {
+      const int i = threadIdx.x + j * kLnGemmWarps * 32;
+      const int a = i >= 2 * per ? 2 : (i >= per ? 1 : 0);
+      const float* src = a == 0 ? p_bias : (a == 1 ? gamma : beta);
+      const float dflt = a == 1 ? 1.f : 0.f;
+      pv[j] = (i < 3 * per && src) ? __ldg(reinterpret_cast<const float4*>(src) + (i - a * per))
+                                   : make_float4(dflt, dflt, dflt, dflt);
+    }
+#pragma unroll
+    for (int j = 0; j < kParLoads; ++j) {
+      const int i = threadIdx.x + j * kLnGemmWarps * 32;
+      if (i < 3 * per) {
+        const int a = i >= 2 * per ? 2 : (i >= per ? 1 : 0);
+        const int k = (i - a * per) * 4;  // element index within the array
+        const int c = k >> 3, e = k & 7;
+        float* d = par + (a * 8 + e) * nvec + c;
+        d[0] = pv[j].x;
+        d[nvec] = pv[j].y;
+        d[2 * nvec] = pv[j].z;
+        d[3 * nvec] = pv[j].w;
+      }
+    }
+  }
+  pdl_wait();  // x and p come from earlier kernels
+  pdl_trigger();
+  __syncthreads();  // params staged
+
+  // prologue: a warp per row, the row's pieces in registers through the
+  // three passes (sum, centred sum of squares, normalise), all of its x / p
+  // loads in flight together
+  for (int m = warp; m < kMB * 16; m += kLnGemmWarps) {
+    uint4* arow = reinterpret_cast<uint4*>(As + static_cast<size_t>(m) * pitch);
+    if (m >= M) {  // warp-uniform
+      for (int c = lane; c < nvec; c += 32) arow[c] = make_uint4(0, 0, 0, 0);
+      continue;
+    }
+    const size_t off = static_cast<size_t>(m) * K;
+    uint4 xv[kLnGemmVecs], qv[kLnGemmVecs];
+#pragma unroll
+    for (int i = 0; i < kLnGemmVecs; ++i) {
+      const int c = lane + 32 * i;
+      const bool ok = c < nvec;
+      xv[i] = ok ? *reinterpret_cast<const uint4*>(x + off + c * 8) : make_uint4(0, 0, 0, 0);
+      qv[i] = (ok && p) ? *reinterpret_cast<const uint4*>(p + off + c * 8) : make_uint4(0, 0, 0, 0);
+    }
+    float v[kLnGemmVecs][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLnGemmVecs; ++i) {
+      const int c = lane + 32 * i;
+      if (c >= nvec) continue;
+      float q[8];
+      bf16x8_to_f32_(xv[i], v[i]);
+      bf16x8_to_f32_(qv[i], q);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] += q[e] + par[e * nvec + c];
+      const uint4 packed = pack8_bf16(v[i]);
+      if (s_out != nullptr && blockIdx.x == 0)
+        reinterpret_cast<uint4*>(s_out + off)[c] = packed;
+      bf16x8_to_f32_(packed, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += v[i][e];
+    }
+    const float mu = warp_allsum(sum) / static_cast<float>(K);
+    float q2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLnGemmVecs; ++i) {
+      if (lane + 32 * i >= nvec) continue;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[i][e] - mu;
+        q2 += d * d;
+      }
+    }
+    const float rs = rsqrtf(warp_allsum(q2) / static_cast<float>(K) + eps);
+#pragma unroll
+    for (int i = 0; i < kLnGemmVecs; ++i) {
+      const int c = lane + 32 * i;
+      if (c >= nvec) continue;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        o[e] = (v[i][e] - mu) * rs * par[(8 + e) * nvec + c] + par[(16 + e) * nvec + c];
+      arow[c] = pack8_bf16(o);
+    }
+  }
+  __syncthreads();
+
+  for (; tile < nblk; tile += gridDim.x) {
+    const int n0 = tile * 8;
+    // this thread's epilogue bias, fetched before the tile's math
+    float bias_o[(kMB * 16 * 8 + kLnGemmWarps * 32 - 1) / (kLnGemmWarps * 32)];
+#pragma unroll
+    for (int j = 0; j < static_cast<int>(sizeof(bias_o) / sizeof(float)); ++j) {
+      const int n = n0 + ((threadIdx.x + j * kLnGemmWarps * 32) & 7);
+      bias_o[j] = (bias != nullptr && n < N) ? __ldg(bias + n) : 0.f;
+    }
+    float c[kMB][4];
+#pragma unroll
+    for (int mb = 0; mb < kMB; ++mb)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) c[mb][i] = 0.f;
+    for (int c0 = warp; c0 < n_chunks; c0 += kStep) {
+      if (c0 != warp) load_w(tile, c0, wv);
+#pragma unroll
+      for (int u = 0; u < kLnGemmBatch; ++u) {
+        const int ch = c0 + u * kLnGemmWarps;
+        if (ch >= n_chunks) break;  // warp-uniform
+        const uint32_t w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+        for (int mb = 0; mb < kMB; ++mb) {
+          const __nv_bfloat16* a0 = As + static_cast<size_t>(mb * 16 + g) * pitch + ch * 32 + t * 8;
+          const uint4 lo = *reinterpret_cast<const uint4*>(a0);
+          const uint4 hi = *reinterpret_cast<const uint4*>(a0 + 8 * pitch);
+          mma_bf16_16816(c[mb], lo.x, hi.x, lo.y, hi.y, w[0], w[1]);
+          mma_bf16_16816(c[mb], lo.z, hi.z, lo.w, hi.w, w[2], w[3]);
+        }
+      }
+    }
+    // the next tile's first W loads overlap this tile's reduction and epilogue
+    if (tile + static_cast<int>(gridDim.x) < nblk) load_w(tile + gridDim.x, warp, wv);
+    float* rw = red + warp * (kMB * 16 * 8);
+#pragma unroll
+    for (int mb = 0; mb < kMB; ++mb) {
+      rw[(mb * 16 + g) * 8 + 2 * t] = c[mb][0];
+      rw[(mb * 16 + g) * 8 + 2 * t + 1] = c[mb][1];
+      rw[(mb * 16 + g + 8) * 8 + 2 * t] = c[mb][2];
+      rw[(mb * 16 + g + 8) * 8 + 2 * t + 1] = c[mb][3];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < static_cast<int>(sizeof(bias_o) / sizeof(float)); ++j) {
+      const int o = threadIdx.x + j * kLnGemmWarps * 32;
+      if (o >= kMB * 16 * 8) break;
+      const int m = o >> 3, n = n0 + (o & 7);
+      if (m >= M || n >= N) continue;
+      float z = 0.f;
+#pragma unroll
+      for (int w = 0; w < kLnGemmWarps; ++w) z += red[w * (kMB * 16 * 8) + o];
+      z += bias_o[j];
+      z = act1<kAct>(z);
+      const size_t idx = static_cast<size_t>(m) * N + n;
+      if constexpr (kOutF32) static_cast<float*>(Y)[idx] = z;
+      else static_cast<__nv_bfloat16*>(Y)[idx] = __float2bfloat16_rn(z);
+    }
+    __syncthreads();  // red is rewritten by the next tile
+  }
+}
+
+template <int kMB, bool kOutF32, int kAct>
+cudaError_t launch_ln_gemm_act(cudaStream_t stream, const __nv_bfloat16* x,
+                               const __nv_bfloat16* p, const float* p_bias, const float* gamma,
+                               const float* beta, float eps, __nv_bfloat16* s_out,
+                               const __nv_bfloat16* W, const float* bias, void* Y, int M, int N,
+                               int K) {
+  auto kernel = ln_gemm_kernel<kMB, kOutF32, kAct>;
+  const size_t smem = ln_gemm_smem_bytes<kMB>(K);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  // per device: the kernel's shared-memory limit, SM count and occupancy at
+  // this size (resident CTAs per SM bound the persistent grid)
+  struct Entry {
+    int dev;
+    size_t smem;
+    int grid_per_sm, sms;
+  };
+  static std::mutex mu;
+  static std::vector<Entry> cache;
+  int per_sm = 0, sms = 0;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (const Entry& c : cache)
+      if (c.dev == dev && c.smem == smem) {
+        per_sm = c.grid_per_sm;
+        sms = c.sms;
+      }
+    if (per_sm == 0) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(ln_gemm_smem_bytes<kMB>(kLnGemmMaxK)));
+      if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kLnGemmWarps * 32, smem);
+      if (e != cudaSuccess) return e;
+      if (per_sm < 1) return cudaErrorInvalidConfiguration;
+      cache.push_back({dev, smem, per_sm, sms});
+    }
+  }
+  const int nblk = (N + 7) / 8;
+  const int grid = nblk < per_sm * sms ? nblk : per_sm * sms;
+  return launch_ex(kernel, dim3(grid), dim3(kLnGemmWarps * 32), smem, stream, 1, true, x, p, p_bias,
+                   gamma, beta, eps, s_out, W, bias, Y, M, N, K);
+}
+
+template <int kMB, bool kOutF32>
+cudaError_t launch_ln_gemm_mb(int act, cudaStream_t stream, const __nv_bfloat16* x,
+                              const __nv_bfloat16* p, const float* p_bias, const float* gamma,
+                              const float* beta, float eps, __nv_bfloat16* s_out,
+                              const __nv_bfloat16* W, const float* bias, void* Y, int M, int N,
+                              int K) {
+  switch (act) {
+    case ND_ACT_GELU_SIGMOID:
+      return launch_ln_gemm_act<kMB, kOutF32, ND_ACT_GELU_SIGMOID>(stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K);
+    case ND_ACT_GELU_TANH:
+      return launch_ln_gemm_act<kMB, kOutF32, ND_ACT_GELU_TANH>(stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K);
+    case ND_ACT_GELU_ERF:
+      return launch_ln_gemm_act<kMB, kOutF32, ND_ACT_GELU_ERF>(stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K);
+    default:
+      return launch_ln_gemm_act<kMB, kOutF32, ND_ACT_NONE>(stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K);
   }
 }
 
@@ -637,6 +1006,19 @@ cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_
   }
   return out_f32 ? launch_bn<true>(BN, act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
                  : launch_bn<false>(BN, act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+}
+
+cudaError_t launch_ln_gemm(cudaStream_t stream, const __nv_bfloat16* x, const __nv_bfloat16* p,
+                           const float* p_bias, const float* gamma, const float* beta, float eps,
+                           __nv_bfloat16* s_out, const __nv_bfloat16* W, const float* bias,
+                           void* Y, bool out_f32, int M, int N, int K, int act) {
+  if (M == 0 || N == 0) return cudaSuccess;
+  if (M > kLnGemmMaxRows || K <= 0 || K % 32 != 0 || K > kLnGemmMaxK) return cudaErrorInvalidValue;
+  if (M <= 16)
+    return out_f32 ? launch_ln_gemm_mb<1, true>(act, stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K)
+                   : launch_ln_gemm_mb<1, false>(act, stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K);
+  return out_f32 ? launch_ln_gemm_mb<2, true>(act, stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K)
+                 : launch_ln_gemm_mb<2, false>(act, stream, x, p, p_bias, gamma, beta, eps, s_out, W, bias, Y, M, N, K);
 }
 
 }  // namespace nd

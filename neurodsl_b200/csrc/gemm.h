@@ -14,4 +14,16 @@ cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_
                         const float* bias, const void* residual, bool residual_f32, void* Y,
                         bool out_f32, int M, int N, int K, int act, const char** err_msg);
 
+// Few-row linear layer with the residual add and LayerNorm in its prologue:
+//   s = bf16(x + (p + p_bias));  Y = act(LayerNorm(s; gamma, beta, eps) · Wᵀ + bias)
+// x, p, s_out [M][K] bf16 (p, p_bias, gamma, beta, s_out, bias may be null;
+// s_out, when given, receives s and must not overlap x or p); W [N][K] bf16;
+// Y [M][N] bf16 or fp32.  M <= kLnGemmMaxRows, K % 32 == 0, K <= kLnGemmMaxK.
+constexpr int kLnGemmMaxRows = 32;
+constexpr int kLnGemmMaxK = 1024;
+cudaError_t launch_ln_gemm(cudaStream_t stream, const __nv_bfloat16* x, const __nv_bfloat16* p,
+                           const float* p_bias, const float* gamma, const float* beta, float eps,
+                           __nv_bfloat16* s_out, const __nv_bfloat16* W, const float* bias,
+                           void* Y, bool out_f32, int M, int N, int K, int act);
+
 }  // namespace nd

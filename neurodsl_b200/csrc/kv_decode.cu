@@ -19,6 +19,7 @@
 #include <mutex>
 
 #include "kv_decode.h"
+#include "launch.cuh"
 
 namespace nd {
 
@@ -79,7 +80,8 @@ __global__ void __launch_bounds__(kThreads)
                      const __nv_bfloat16* __restrict__ v_new, __nv_bfloat16* __restrict__ k_cache,
                      __nv_bfloat16* __restrict__ v_cache, void* __restrict__ out,
                      float* __restrict__ lse, int L, int L_max, float scale_log2,
-                     ChunkPartial* __restrict__ partials, unsigned int* __restrict__ tickets) {
+                     ChunkPartial* __restrict__ partials, unsigned int* __restrict__ tickets,
+                     int H, long long qkv_ld) {
   const int chunk = blockIdx.x;
   const int nchunks = gridDim.x;
   const int bh = blockIdx.y;
@@ -93,7 +95,11 @@ __global__ void __launch_bounds__(kThreads)
   const uint4* vbase = reinterpret_cast<const uint4*>(v_cache + head_off);
   const int key0 = chunk * kChunk + warp * kKeysPerWarp + grp;
 
-  // Issue every K/V load of this thread before any arithmetic.
+  // Issue every K/V load of this thread before any arithmetic.  Under
+  // programmatic dependent launch they go out before the previous kernel (the
+  // one producing q, k_new and v_new) has finished: keys below L-1 were
+  // written by earlier, finished work, and the key at L-1, whose load may see
+  // an old value, is replaced by k_new / v_new below.
   uint4 kr[kIters], vr[kIters];
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
@@ -107,9 +113,14 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
 
+  pdl_wait();
+  pdl_trigger();
+
+  // q, k_new and v_new rows: batch b at b * qkv_ld, head h at h * 64
+  const size_t qoff = static_cast<size_t>(bh / H) * qkv_ld + static_cast<size_t>(bh % H) * kD;
   float qf[8];
   {
-    const uint4 qr = *reinterpret_cast<const uint4*>(q + static_cast<size_t>(bh) * kD + sub * 8);
+    const uint4 qr = *reinterpret_cast<const uint4*>(q + qoff + sub * 8);
     bf16x8_to_f32(qr, qf);
 #pragma unroll
     for (int i = 0; i < 8; ++i) qf[i] *= scale_log2;
@@ -121,10 +132,8 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
     for (int it = 0; it < kIters; ++it) {
       if (key0 + it * 4 == L - 1) {
-        const uint4 kn =
-            *reinterpret_cast<const uint4*>(k_new + static_cast<size_t>(bh) * kD + sub * 8);
-        const uint4 vn =
-            *reinterpret_cast<const uint4*>(v_new + static_cast<size_t>(bh) * kD + sub * 8);
+        const uint4 kn = *reinterpret_cast<const uint4*>(k_new + qoff + sub * 8);
+        const uint4 vn = *reinterpret_cast<const uint4*>(v_new + qoff + sub * 8);
         kr[it] = kn;
         vr[it] = vn;
         reinterpret_cast<uint4*>(k_cache + head_off)[static_cast<size_t>(L - 1) * (kD / 8) + sub] = kn;
@@ -303,7 +312,7 @@ cudaError_t launch_kv_decode(cudaStream_t stream, const __nv_bfloat16* q,
                              const __nv_bfloat16* k_new, const __nv_bfloat16* v_new,
                              __nv_bfloat16* k_cache, __nv_bfloat16* v_cache, void* out,
                              bool out_f32, float* lse, int B, int H, int L, int L_max, float scale,
-                             void* workspace) {
+                             void* workspace, long long qkv_ld) {
   const int nchunks = (L + kChunk - 1) / kChunk;
   dim3 grid(nchunks, B * H);
   ChunkPartial* partials = nullptr;
@@ -314,15 +323,14 @@ cudaError_t launch_kv_decode(cudaStream_t stream, const __nv_bfloat16* q,
                                                kv_decode_partials_offset());
   }
   const float scale_log2 = scale * kLog2e;
+  if (qkv_ld <= 0) qkv_ld = static_cast<long long>(H) * kD;
   if (out_f32)
-    kv_decode_kernel<true><<<grid, kThreads, 0, stream>>>(q, k_new, v_new, k_cache, v_cache, out,
-                                                          lse, L, L_max, scale_log2, partials,
-                                                          tickets);
-  else
-    kv_decode_kernel<false><<<grid, kThreads, 0, stream>>>(q, k_new, v_new, k_cache, v_cache, out,
-                                                           lse, L, L_max, scale_log2, partials,
-                                                           tickets);
-  return cudaGetLastError();
+    return launch_ex(kv_decode_kernel<true>, grid, dim3(kThreads), 0, stream, 1, true, q, k_new,
+                     v_new, k_cache, v_cache, out, lse, L, L_max, scale_log2, partials, tickets, H,
+                     qkv_ld);
+  return launch_ex(kv_decode_kernel<false>, grid, dim3(kThreads), 0, stream, 1, true, q, k_new,
+                   v_new, k_cache, v_cache, out, lse, L, L_max, scale_log2, partials, tickets, H,
+                   qkv_ld);
 }
 
 // Append one token's K/V rows at position `pos` of every (batch, head).

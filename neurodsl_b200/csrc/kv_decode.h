@@ -24,11 +24,13 @@ constexpr size_t kDecodeStaticScratchBytes = static_cast<size_t>(8) << 20;
 // the ticket region with cudaMemsetAsync on `stream`.  Allocates nothing.
 cudaError_t kv_decode_static_scratch(int device, cudaStream_t stream, void** ptr);
 
+// q, k_new and v_new hold one row of H*64 values per batch entry, rows
+// qkv_ld elements apart (0: H*64, i.e. [B][H][64] contiguous).
 cudaError_t launch_kv_decode(cudaStream_t stream, const __nv_bfloat16* q,
                              const __nv_bfloat16* k_new, const __nv_bfloat16* v_new,
                              __nv_bfloat16* k_cache, __nv_bfloat16* v_cache, void* out,
                              bool out_f32, float* lse, int B, int H, int L, int L_max, float scale,
-                             void* workspace);
+                             void* workspace, long long qkv_ld = 0);
 
 cudaError_t launch_kv_append(cudaStream_t stream, const __nv_bfloat16* k_new,
                              const __nv_bfloat16* v_new, __nv_bfloat16* k_cache,

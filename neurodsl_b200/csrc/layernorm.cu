@@ -13,6 +13,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "launch.cuh"
 #include "layernorm.h"
 
 namespace nd {
@@ -83,6 +84,8 @@ __global__ void __launch_bounds__(256)
                    float* __restrict__ rstd_out, int rows, int d, float eps) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  pdl_wait();  // x comes from the previous kernel
+  pdl_trigger();
   if (row >= rows) return;
   const int nvec = d >> 3;
   const TI* xr = x + static_cast<size_t>(row) * d;
@@ -203,13 +206,13 @@ cudaError_t launch_typed(cudaStream_t stream, const void* x, const float* gamma,
     const int grid = (rows + rows_per_block - 1) / rows_per_block;
     const int nvec = d / 8;
     if (nvec <= 32)
-      ln_warp_kernel<TI, TO, 1><<<grid, 256, 0, stream>>>(xi, gamma, beta, yo, mean, rstd, rows, d, eps);
+      return launch_ex(ln_warp_kernel<TI, TO, 1>, grid, dim3(256), 0, stream, 1, true, xi, gamma, beta, yo, mean, rstd, rows, d, eps);
     else if (nvec <= 64)
-      ln_warp_kernel<TI, TO, 2><<<grid, 256, 0, stream>>>(xi, gamma, beta, yo, mean, rstd, rows, d, eps);
+      return launch_ex(ln_warp_kernel<TI, TO, 2>, grid, dim3(256), 0, stream, 1, true, xi, gamma, beta, yo, mean, rstd, rows, d, eps);
     else if (nvec <= 128)
-      ln_warp_kernel<TI, TO, 4><<<grid, 256, 0, stream>>>(xi, gamma, beta, yo, mean, rstd, rows, d, eps);
+      return launch_ex(ln_warp_kernel<TI, TO, 4>, grid, dim3(256), 0, stream, 1, true, xi, gamma, beta, yo, mean, rstd, rows, d, eps);
     else
-      ln_warp_kernel<TI, TO, 8><<<grid, 256, 0, stream>>>(xi, gamma, beta, yo, mean, rstd, rows, d, eps);
+      return launch_ex(ln_warp_kernel<TI, TO, 8>, grid, dim3(256), 0, stream, 1, true, xi, gamma, beta, yo, mean, rstd, rows, d, eps);
   } else {
     const size_t smem = static_cast<size_t>(d) * sizeof(float);
     if (smem > 48 * 1024) {

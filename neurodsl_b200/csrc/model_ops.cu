@@ -15,7 +15,9 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "launch.cuh"
 #include "model_ops.h"
+#include "ptx.cuh"
 
 namespace nd {
 namespace {
@@ -54,6 +56,8 @@ __global__ void __launch_bounds__(256)
                  int* __restrict__ err_word) {
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  pdl_wait();  // the ids may come from the previous kernel (a greedy pick)
+  pdl_trigger();
   if (t >= T) return;
   const int id = ids[t];
   const int p = pos ? pos[t] : -1;
@@ -98,27 +102,39 @@ __device__ __forceinline__ void better(float& v, int& i, float v2, int i2) {
   }
 }
 
-constexpr int kArgmaxThreads = 1024;
-constexpr int kArgmaxUnroll = 8;  // independent loads in flight per thread
+constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxUnroll = 8;    // independent loads in flight per thread
+constexpr int kArgmaxCluster = 8;   // CTAs per row for long rows
 
+// A cluster of CTAs per row (one CTA for short rows): CTA rank r scans a
+// contiguous 1/cluster of the row, then rank 0 merges the CTAs' results from
+// distributed shared memory.  The merge keeps the first index among equal
+// maxima whatever the order, so the result is that of one sequential scan.
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads)
     argmax_kernel(const T* __restrict__ logits, long long ld, int V, int* __restrict__ idx,
                   float* __restrict__ val) {
-  const int row = blockIdx.x;
+  const int nc = static_cast<int>(cluster_nctarank());
+  const int cr = static_cast<int>(cluster_ctarank());
+  const int row = blockIdx.x / nc;
+  const int per = (V + nc - 1) / nc;
+  const int j_beg = cr * per;
+  const int j_end = min(V, j_beg + per);
+  pdl_wait();  // the logits come from the previous kernel
+  pdl_trigger();
   const T* r = logits + static_cast<size_t>(row) * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int j0 = threadIdx.x; j0 < V; j0 += kArgmaxThreads * kArgmaxUnroll) {
+  for (int j0 = j_beg + threadIdx.x; j0 < j_end; j0 += kArgmaxThreads * kArgmaxUnroll) {
     float v[kArgmaxUnroll];
 #pragma unroll
     for (int u = 0; u < kArgmaxUnroll; ++u) {
       const int j = j0 + u * kArgmaxThreads;
-      v[u] = j < V ? ld_f<T>(r + j) : -INFINITY;
+      v[u] = j < j_end ? ld_f<T>(r + j) : -INFINITY;
     }
 #pragma unroll
     for (int u = 0; u < kArgmaxUnroll; ++u)
-      if (j0 + u * kArgmaxThreads < V) better(bv, bi, v[u], j0 + u * kArgmaxThreads);
+      if (j0 + u * kArgmaxThreads < j_end) better(bv, bi, v[u], j0 + u * kArgmaxThreads);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -128,6 +144,8 @@ __global__ void __launch_bounds__(kArgmaxThreads)
   }
   __shared__ float sv[kArgmaxThreads / 32];
   __shared__ int si[kArgmaxThreads / 32];
+  __shared__ float cv;
+  __shared__ int ci;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
   if (lane == 0) {
     sv[w] = bv;
@@ -144,10 +162,24 @@ __global__ void __launch_bounds__(kArgmaxThreads)
       better(bv, bi, v2, i2);
     }
     if (lane == 0) {
-      idx[row] = bi == 0x7fffffff ? 0 : bi;
-      if (val) val[row] = bv;
+      cv = bv;
+      ci = bi;
     }
   }
+  // every CTA of the cluster reaches both barriers (no early exit above)
+  if (nc > 1) cluster_sync();
+  if (cr == 0 && threadIdx.x == 0) {
+    float v = cv;
+    int i = ci;
+    for (int q = 1; q < nc; ++q) {
+      const float v2 = ld_dsmem_f32(&cv, static_cast<uint32_t>(q));
+      const int i2 = __float_as_int(ld_dsmem_f32(&ci, static_cast<uint32_t>(q)));
+      better(v, i, v2, i2);
+    }
+    idx[row] = i == 0x7fffffff ? 0 : i;
+    if (val) val[row] = v;
+  }
+  if (nc > 1) cluster_sync();  // rank 0 has read every CTA's result
 }
 
 // ---------------------------------------------------------------- KV store
@@ -186,6 +218,8 @@ __global__ void __launch_bounds__(256)
                   __nv_bfloat16* __restrict__ y, int rows, int d, float eps) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  pdl_wait();  // x and p come from earlier kernels
+  pdl_trigger();
   if (row >= rows) return;
   const int nvec = d >> 3;
   const size_t off = static_cast<size_t>(row) * d;
@@ -248,17 +282,15 @@ cudaError_t launch_add_ln_typed(cudaStream_t stream, const __nv_bfloat16* x, con
                                 const float* bias, const float* gamma, const float* beta,
                                 __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d,
                                 float eps) {
-  const dim3 grid((rows + 7) / 8);
+  const dim3 grid((rows + 7) / 8), block(256);
   const TP* pp = static_cast<const TP*>(p);
   if (d <= 256)
-    add_ln_kernel<TP, 1><<<grid, 256, 0, stream>>>(x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  else if (d <= 512)
-    add_ln_kernel<TP, 2><<<grid, 256, 0, stream>>>(x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  else if (d <= 1024)
-    add_ln_kernel<TP, 4><<<grid, 256, 0, stream>>>(x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  else
-    add_ln_kernel<TP, 8><<<grid, 256, 0, stream>>>(x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  return cudaGetLastError();
+    return launch_ex(add_ln_kernel<TP, 1>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  if (d <= 512)
+    return launch_ex(add_ln_kernel<TP, 2>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  if (d <= 1024)
+    return launch_ex(add_ln_kernel<TP, 4>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  return launch_ex(add_ln_kernel<TP, 8>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
 }
 
 }  // namespace
@@ -267,19 +299,21 @@ cudaError_t launch_embed(cudaStream_t stream, const int* ids, const int* pos,
                          const __nv_bfloat16* wte, const __nv_bfloat16* wpe, __nv_bfloat16* y,
                          int T, int d, int vocab, int n_pos, int* err_word) {
   if (T == 0) return cudaSuccess;
-  embed_kernel<<<(T + 7) / 8, 256, 0, stream>>>(ids, pos, wte, wpe, y, T, d, vocab, n_pos, err_word);
-  return cudaGetLastError();
+  return launch_ex(embed_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, 1, true, ids, pos, wte,
+                   wpe, y, T, d, vocab, n_pos, err_word);
 }
 
 cudaError_t launch_argmax(cudaStream_t stream, const void* logits, bool f32, long long ld,
                           int rows, int V, int* idx, float* val) {
   if (rows == 0) return cudaSuccess;
+  // a few long rows (a decode batch's logits) spread over a cluster each
+  const int nc = (V >= 2 * kArgmaxCluster * kArgmaxThreads && rows < 148) ? kArgmaxCluster : 1;
+  const dim3 grid(static_cast<unsigned>(rows) * nc), block(kArgmaxThreads);
   if (f32)
-    argmax_kernel<float><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const float*>(logits), ld, V, idx, val);
-  else
-    argmax_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits),
-                                                           ld, V, idx, val);
-  return cudaGetLastError();
+    return launch_ex(argmax_kernel<float>, grid, block, 0, stream, nc, true,
+                     static_cast<const float*>(logits), ld, V, idx, val);
+  return launch_ex(argmax_kernel<__nv_bfloat16>, grid, block, 0, stream, nc, true,
+                   static_cast<const __nv_bfloat16*>(logits), ld, V, idx, val);
 }
 
 cudaError_t launch_kv_store(cudaStream_t stream, const __nv_bfloat16* src, long long ld, int k_col,

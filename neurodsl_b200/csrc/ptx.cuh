@@ -371,6 +371,33 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   return r;
 }
 
+// Thread-block clusters: this CTA's rank in its cluster, the cluster's size,
+// a full cluster barrier (release/acquire: shared-memory writes before it are
+// visible to the cluster's CTAs after it), and a load from the shared memory
+// of another CTA of the cluster at the address matching `p` in this CTA.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(const void* p, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
 // Hardware tanh approximation (the MUFU tanh instruction).
 __device__ __forceinline__ float tanh_approx(float x) {
   float y;

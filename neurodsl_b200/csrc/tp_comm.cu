@@ -24,6 +24,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "tp_comm.h"
 
@@ -83,6 +84,41 @@ __global__ void __launch_bounds__(256)
                             __nv_bfloat16* s_out, __nv_bfloat16* __restrict__ y, int rows, int d,
                             float eps, int* __restrict__ err_word) {
   __shared__ int s_ok;
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nvec = d >> 3;
+  const int row0 = blockIdx.x * warps + (threadIdx.x >> 5);
+  // This rank's inputs (x, bias, gamma, beta) come from earlier work on this
+  // stream, so the first row's loads go out before the peers' flags are
+  // awaited; only the partial sums in the slots wait for them.  bias, gamma
+  // and beta (the same for every row) are constant operands and go out even
+  // before the previous kernel has finished (programmatic dependent launch).
+  uint4 xr[kMaxVec];
+  float bs[kMaxVec][8], gm[kMaxVec][8], bt[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        bs[i][e] = bias ? __ldg(bias + c * 8 + e) : 0.f;
+        gm[i][e] = gamma ? __ldg(gamma + c * 8 + e) : 1.f;
+        bt[i][e] = beta ? __ldg(beta + c * 8 + e) : 0.f;
+      }
+    }
+  }
+  auto load_x = [&](int row) {
+    const size_t off = static_cast<size_t>(row) * d;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = lane + i * 32;
+      if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
+    }
+  };
+  pdl_wait();  // x and this rank's partial come from earlier kernels
+  pdl_trigger();
+  if (row0 < rows) load_x(row0);
+
   char* own = static_cast<char*>(regs.r[rank]);
   if (threadIdx.x == 0) {
     uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
@@ -115,10 +151,8 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   if (!s_ok) return;
 
-  const int warps = blockDim.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int nvec = d >> 3;
-  for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < rows; row += gridDim.x * warps) {
+  for (int row = row0; row < rows; row += gridDim.x * warps) {
+    if (row != row0) load_x(row);
     const size_t off = static_cast<size_t>(row) * d;
     float v[kMaxVec][8];
     float sum = 0.f;
@@ -126,7 +160,6 @@ __global__ void __launch_bounds__(256)
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + i * 32;
       if (c < nvec) {
-        const uint4 xv = reinterpret_cast<const uint4*>(x + off)[c];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
         // partial sums in rank order, then the residual and the bias
@@ -136,9 +169,9 @@ __global__ void __launch_bounds__(256)
           const char* slot = static_cast<const char*>(regs.r[p]) + slot_off;
           bf16x8_add(ld_cg16(slot + (off + c * 8) * 2), v[i]);
         }
-        bf16x8_add(xv, v[i]);
+        bf16x8_add(xr[i], v[i]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] += bias ? bias[c * 8 + e] : 0.f;
+        for (int e = 0; e < 8; ++e) v[i][e] += bs[i][e];
         const uint4 packed = f32_to_bf16x8(v[i]);
         reinterpret_cast<uint4*>(s_out + off)[c] = packed;
 #pragma unroll
@@ -167,11 +200,7 @@ __global__ void __launch_bounds__(256)
       if (c < nvec) {
         float o[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float g = gamma ? gamma[c * 8 + e] : 1.f;
-          const float b = beta ? beta[c * 8 + e] : 0.f;
-          o[e] = (v[i][e] - mu) * rs * g + b;
-        }
+        for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mu) * rs * gm[i][e] + bt[i][e];
         reinterpret_cast<uint4*>(y + off)[c] = f32_to_bf16x8(o);
       }
     }
@@ -205,13 +234,13 @@ cudaError_t launch_allreduce_add_layernorm(cudaStream_t stream, const CommRegion
   const dim3 grid(comm_grid(rows, sms));
   const size_t so = comm_slot_offset(slot, rows_max, d);
   if (d <= 256)
-    allreduce_add_ln_kernel<1><<<grid, 256, 0, stream>>>(regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    return launch_ex(allreduce_add_ln_kernel<1>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   else if (d <= 512)
-    allreduce_add_ln_kernel<2><<<grid, 256, 0, stream>>>(regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    return launch_ex(allreduce_add_ln_kernel<2>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   else if (d <= 1024)
-    allreduce_add_ln_kernel<4><<<grid, 256, 0, stream>>>(regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    return launch_ex(allreduce_add_ln_kernel<4>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   else
-    allreduce_add_ln_kernel<8><<<grid, 256, 0, stream>>>(regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    return launch_ex(allreduce_add_ln_kernel<8>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   return cudaGetLastError();
 }
 

@@ -11,11 +11,14 @@ in libneurodsl_b200.so:
 
   embedding             nd_embed
   LayerNorm             nd_layernorm, then nd_add_layernorm (residual add,
-                        bias and the next LayerNorm in one pass)
+                        bias and the next LayerNorm in one pass); one-GPU
+                        decode folds both into the next linear layer
+                        (nd_ln_gemm)
   QKV / out / MLP       nd_gemm_bias_act (bias and GELU in the epilogue)
   prefill attention     nd_flash_attn_fwd_strided on the fused QKV projection
                         (no per-head copies), K/V into the caches by nd_kv_store
-  decode attention      nd_kv_decode_attn with the new token appended in place
+  decode attention      nd_kv_decode_attn_qkv straight from the fused QKV
+                        projection, the new token appended in place
   greedy token          nd_argmax on the LM-head logits
 
 Tensor parallelism (Megatron layout): rank r of `tp` holds heads
@@ -30,6 +33,11 @@ partials over NVLink and applies the residual and LayerNorm itself
 local (max, index) per row that is all-gathered and reduced to the global
 first maximum.  Weights are generated from one seed on every rank and sliced,
 so any `tp` computes the same model.
+
+Decode steps run with programmatic dependent launch (nd_set_pdl): each
+kernel's weight loads, and the decode attention's cache reads, overlap the
+previous kernel, which matters because a decode step of a few rows is some
+ten kernels per layer of a few microseconds each.
 """
 import math
 from dataclasses import dataclass
@@ -71,10 +79,13 @@ class GPT:
     """Weights of one rank plus the buffers of one (batch, length) shape."""
 
     def __init__(self, cfg: GPTConfig, seed=0, device=None, tp=1, rank=0, group=None,
-                 weight_std=0.02, bias_std=0.0, nvlink_rows=0):
+                 weight_std=0.02, bias_std=0.0, nvlink_rows=0, pdl=True):
         if cfg.d_head != 64:
             raise ValueError("head_dim must be 64")
         self.cfg = cfg
+        # decode steps launch with programmatic dependent launch: their weights
+        # and earlier cache entries are written by no kernel of the step
+        self.pdl = pdl
         self.tp, self.rank, self.group = tp, rank, group
         self.device = torch.device(device or "cuda")
         dev = self.device
@@ -154,8 +165,9 @@ class GPT:
             "u": torch.empty(T, Fl, device=dev, dtype=bf),
             "last": torch.empty(B, d, device=dev, dtype=bf),
             "xd": torch.empty(B, d, device=dev, dtype=bf), "hd": torch.empty(B, d, device=dev, dtype=bf),
-            "qd": torch.empty(B, dl, device=dev, dtype=bf), "kd": torch.empty(B, dl, device=dev, dtype=bf),
-            "vd": torch.empty(B, dl, device=dev, dtype=bf), "ad": torch.empty(B, dl, device=dev, dtype=bf),
+            "xd2": torch.empty(B, d, device=dev, dtype=bf),
+            "qkvd": torch.empty(B, 3 * dl, device=dev, dtype=bf),
+            "ad": torch.empty(B, dl, device=dev, dtype=bf),
             "pd": torch.empty(B, d, device=dev, dtype=bf), "ud": torch.empty(B, Fl, device=dev, dtype=bf),
             "logits": torch.empty(B, self.v1 - self.v0, device=dev, dtype=torch.float32),
             "val": torch.empty(B, device=dev, dtype=torch.float32),
@@ -239,39 +251,71 @@ class GPT:
         B, S, steps = self._shape
         if not 0 <= t < steps:
             raise ValueError(f"step {t} outside [0, {steps})")
-        H, dl = self.n_head_local, self.d_local
+        H = self.n_head_local
         xd, hd = b["xd"], b["hd"]
-        ops.embed(b["ids"][t + 1], self.wte, self.wpe, b["pos_decode"][t], out=xd)
-        ops.layernorm(xd, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=hd,
-                      stats=False)
+        out_ids = b["ids"][t + 2] if t + 2 <= steps else b["idx"]
         Lc = S + t + 1
-        peer = self.comm is not None and B <= self.comm.rows_max
-        for i, L in enumerate(self.layers):
-            w, bb = L["w_qkv"], L["b_qkv"]
-            ops.linear(hd, w[:dl], bb[:dl], out=b["qd"])
-            ops.linear(hd, w[dl:2 * dl], bb[dl:2 * dl], out=b["kd"])
-            ops.linear(hd, w[2 * dl:], bb[2 * dl:], out=b["vd"])
-            ops.kv_decode_attn(b["qd"].view(B, H, 64), self.k_cache[i], self.v_cache[i], Lc,
-                               k_new=b["kd"].view(B, H, 64), v_new=b["vd"].view(B, H, 64),
-                               out=b["ad"].view(B, H, 64), workspace=b["ws"], want_lse=False)
-            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
-            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
-            if peer:
-                ops.linear(b["ad"], L["w_o"], out=self.comm.partial(B))
-                self.comm.add_layernorm(xd, L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, xd, hd)
+        with ops.pdl(self.pdl):
+            ops.embed(b["ids"][t + 1], self.wte, self.wpe, b["pos_decode"][t], out=xd)
+            if self.tp == 1:
+                self._decode_layers_fused(B, H, Lc, out_ids)
+                return b["logits"]
+            ops.layernorm(xd, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps,
+                          out=hd, stats=False)
+            peer = self.comm is not None and B <= self.comm.rows_max
+            for i, L in enumerate(self.layers):
+                ops.linear(hd, L["w_qkv"], L["b_qkv"], out=b["qkvd"])
+                ops.kv_decode_attn_qkv(b["qkvd"], self.k_cache[i], self.v_cache[i], Lc,
+                                       out=b["ad"].view(B, H, 64), workspace=b["ws"])
+                nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+                g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
+                if peer:
+                    ops.linear(b["ad"], L["w_o"], out=self.comm.partial(B))
+                    self.comm.add_layernorm(xd, L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, xd, hd)
+                    ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
+                    ops.linear(b["ud"], L["w_2"], out=self.comm.partial(B))
+                    self.comm.add_layernorm(xd, L["b_2"], g_, b_, cfg.eps, xd, hd)
+                    continue
+                ops.linear(b["ad"], L["w_o"], out=b["pd"])
+                self._all_reduce(b["pd"])
+                ops.add_layernorm(xd, b["pd"], L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=xd,
+                                  out=hd)
                 ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
-                ops.linear(b["ud"], L["w_2"], out=self.comm.partial(B))
-                self.comm.add_layernorm(xd, L["b_2"], g_, b_, cfg.eps, xd, hd)
-                continue
-            ops.linear(b["ad"], L["w_o"], out=b["pd"])
-            self._all_reduce(b["pd"])
-            ops.add_layernorm(xd, b["pd"], L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=xd, out=hd)
-            ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
-            ops.linear(b["ud"], L["w_2"], out=b["pd"])
-            self._all_reduce(b["pd"])
-            ops.add_layernorm(xd, b["pd"], L["b_2"], g_, b_, cfg.eps, s_out=xd, out=hd)
-        self._next_token(hd, b["ids"][t + 2] if t + 2 <= steps else b["idx"])
+                ops.linear(b["ud"], L["w_2"], out=b["pd"])
+                self._all_reduce(b["pd"])
+                ops.add_layernorm(xd, b["pd"], L["b_2"], g_, b_, cfg.eps, s_out=xd, out=hd)
+            self._next_token(hd, out_ids)
         return b["logits"]
+
+    def _decode_layers_fused(self, B, H, Lc, out_ids):
+        """One GPU: five launches per layer — residual + LN1 + QKV projection,
+        attention, output projection, residual + LN2 + up projection, down
+        projection (nd_ln_gemm folds each residual add and LayerNorm into the
+        linear layer after it) — then residual + final LN + LM head, argmax.
+        The residual stream alternates between two buffers: each fused launch
+        reads one and writes the updated stream to the other, since all its
+        CTAs read the old stream while one writes the new."""
+        cfg, b = self.cfg, self.buf
+        xa, xb = b["xd"], b["xd2"]
+        p = pb = None
+        for i, L in enumerate(self.layers):
+            ops.ln_linear(xa, L["w_qkv"], p=p, p_bias=pb, gamma=L["ln1_g"], beta=L["ln1_b"],
+                          eps=cfg.eps, s_out=None if p is None else xb, bias=L["b_qkv"],
+                          out=b["qkvd"])
+            if p is not None:
+                xa, xb = xb, xa
+            ops.kv_decode_attn_qkv(b["qkvd"], self.k_cache[i], self.v_cache[i], Lc,
+                                   out=b["ad"].view(B, H, 64), workspace=b["ws"])
+            ops.linear(b["ad"], L["w_o"], out=b["pd"])
+            ops.ln_linear(xa, L["w_1"], p=b["pd"], p_bias=L["b_o"], gamma=L["ln2_g"],
+                          beta=L["ln2_b"], eps=cfg.eps, s_out=xb, bias=L["b_1"], act=cfg.act,
+                          out=b["ud"])
+            xa, xb = xb, xa
+            ops.linear(b["ud"], L["w_2"], out=b["pd"])
+            p, pb = b["pd"], L["b_2"]
+        ops.ln_linear(xa, self.w_head, p=p, p_bias=pb, gamma=self.lnf_g, beta=self.lnf_b,
+                      eps=cfg.eps, out=b["logits"], out_dtype=torch.float32)
+        ops.argmax(b["logits"], idx=out_ids)
 
     def tokens(self):
         """Generated tokens so far: [B][steps] (prefill's token first)."""

@@ -128,6 +128,60 @@ def kv_decode_attn(q, k_cache, v_cache, L, k_new=None, v_new=None, scale=None, o
     return out, lse
 
 
+def kv_decode_attn_qkv(qkv, k_cache, v_cache, L, scale=None, out=None, out_dtype=torch.bfloat16,
+                       lse=None, workspace=None, want_lse=False, stream=None):
+    """Decode attention from a fused QKV projection qkv [B][3*H*64] (bf16,
+    unit column stride; rows may be padded): q, k_new and v_new are its three
+    column blocks, and k_new / v_new are appended at position L-1.
+    Returns (out [B][H][64], lse [B][H] or None)."""
+    if not isinstance(qkv, torch.Tensor) or qkv.dtype != torch.bfloat16 or qkv.dim() != 2:
+        raise ValueError("qkv must be a 2-D bf16 tensor")
+    if not qkv.is_cuda or qkv.stride(1) != 1:
+        raise ValueError("qkv must be a CUDA tensor with unit column stride")
+    _need(k_cache, "k_cache", torch.bfloat16, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, 4)
+    B = qkv.shape[0]
+    _, H, L_max, D = k_cache.shape
+    if k_cache.shape[0] != B or v_cache.shape != k_cache.shape or qkv.shape[1] != 3 * H * D:
+        raise ValueError("qkv / cache shape mismatch")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty((B, H, D), dtype=out_dtype, device=qkv.device)
+    if lse is None and want_lse:
+        lse = torch.empty((B, H), dtype=torch.float32, device=qkv.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(_lib.load().nd_kv_decode_attn_qkv(_stream(stream), _ptr(qkv), qkv.stride(0),
+                                            _ptr(k_cache), _ptr(v_cache), _ptr(out),
+                                            _DT[out.dtype], _ptr(lse), B, H, int(L), L_max, D,
+                                            float(scale), _ptr(workspace), ws_bytes))
+    return out, lse
+
+
+def set_pdl(enable):
+    """Programmatic dependent launch for this thread's decode-step kernels
+    (nd_set_pdl); returns the previous setting."""
+    prev = ctypes.c_int(0)
+    check(_lib.load().nd_set_pdl(1 if enable else 0, ctypes.byref(prev)))
+    return bool(prev.value)
+
+
+class pdl:
+    """Context manager: launches inside run with programmatic dependent
+    launch on (or off), restoring the previous setting on exit."""
+
+    def __init__(self, enable=True):
+        self.enable = enable
+
+    def __enter__(self):
+        self.prev = set_pdl(self.enable)
+        return self
+
+    def __exit__(self, *exc):
+        set_pdl(self.prev)
+        return False
+
+
 def kv_append(k_new, v_new, k_cache, v_cache, pos, stream=None):
     _need(k_new, "k_new", torch.bfloat16, 3)
     _need(v_new, "v_new", torch.bfloat16, 3)
@@ -166,6 +220,38 @@ def linear(A, W, bias=None, residual=None, act="none", out=None, out_dtype=torch
     check(_lib.load().nd_gemm_bias_act(_stream(stream), _ptr(A), _ptr(W), _ptr(bias),
                                        _ptr(residual), rdt, _ptr(out), _DT[out.dtype], M, N, K,
                                        ACT[act] if isinstance(act, str) else int(act)))
+    return out
+
+
+def ln_linear(x, W, p=None, p_bias=None, gamma=None, beta=None, eps=1e-5, s_out=None, bias=None,
+              act="none", out=None, out_dtype=torch.bfloat16, stream=None):
+    """Y = act(LayerNorm(x + p + p_bias)·Wᵀ + bias) for at most 32 rows, with
+    the residual sum s = bf16(x + p + p_bias) written to s_out if given
+    (nd_ln_gemm: residual :add + :layernorm + :linear in one launch)."""
+    _need(x, "x", torch.bfloat16, 2)
+    _need(W, "W", torch.bfloat16, 2)
+    M, K = x.shape
+    N = W.shape[0]
+    if W.shape[1] != K:
+        raise ValueError(f"x{tuple(x.shape)} and W{tuple(W.shape)} disagree on K")
+    for name, t in (("p", p), ("s_out", s_out)):
+        if t is not None:
+            _need(t, name, torch.bfloat16, 2)
+            if tuple(t.shape) != (M, K):
+                raise ValueError(f"{name} shape != x shape")
+    for name, t, n in (("p_bias", p_bias, K), ("gamma", gamma, K), ("beta", beta, K),
+                       ("bias", bias, N)):
+        if t is not None:
+            _need(t, name, torch.float32)
+            if t.numel() != n:
+                raise ValueError(f"{name} length != {n}")
+    if out is None:
+        out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    _need(out, "out", None, 2)
+    check(_lib.load().nd_ln_gemm(_stream(stream), _ptr(x), _ptr(p), _ptr(p_bias), _ptr(gamma),
+                                 _ptr(beta), float(eps), _ptr(s_out), _ptr(W), _ptr(bias),
+                                 _ptr(out), _DT[out.dtype], M, N, K,
+                                 ACT[act] if isinstance(act, str) else int(act)))
     return out
 
 

@@ -68,6 +68,28 @@ def test_argument_validation_runs_before_any_device_work():
     assert n.value > 64 * 12 * 9 * 256
 
 
+def test_pdl_switch_is_per_call_state_without_a_gpu():
+    """nd_set_pdl only records the launch mode (no device work): it returns
+    the previous setting, and the fused-QKV decode entry point checks its row
+    stride before touching the device."""
+    from neurodsl_b200 import _lib, ops
+    assert ops.set_pdl(True) is False
+    assert ops.set_pdl(False) is True
+    with ops.pdl(True):
+        assert ops.set_pdl(True) is True
+    assert ops.set_pdl(False) is False
+    lib = _lib.load()
+    rc = lib.nd_kv_decode_attn_qkv(None, 16, 3 * 2 * 64 - 8, None, None, None, 1, None, 2, 2, 4,
+                                   16, 64, 0.125, None, 0)
+    assert rc == _lib.ND_ERR_SHAPE
+    assert b"row stride" in lib.nd_last_error_string()
+    # nd_ln_gemm: K must be a multiple of 32 up to 1024, at most 32 rows
+    for M, K in ((4, 80), (4, 2048), (33, 64)):
+        rc = lib.nd_ln_gemm(None, None, None, None, None, None, 1e-5, None, None, None, None, 1,
+                            M, 8, K, 0)
+        assert rc == _lib.ND_ERR_SHAPE, (M, K)
+
+
 def test_missing_library_raises(tmp_path):
     from neurodsl_b200 import _lib
     with pytest.raises(ImportError):

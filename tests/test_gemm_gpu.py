@@ -60,15 +60,22 @@ def test_shapes_vs_torch(M, N, K, act):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 768, 768), (7, 300, 96), (16, 2304, 768),
-                                   (17, 50257, 768), (32, 1024, 4096), (30, 8, 32)])
+                                   (17, 50257, 768), (32, 1024, 4096), (30, 8, 32),
+                                   (16, 768, 3072), (3, 40, 1056), (9, 96, 16384)])
 @pytest.mark.parametrize("act,res", [("none", False), ("tanh", True), ("sigmoid", False)])
 def test_few_rows_vs_oracle(M, N, K, act, res):
     """M <= 32 takes the weight-streaming path; compared with the oracle on
-    bf16-rounded inputs, bf16 and fp32 outputs, with and without residual."""
+    bf16-rounded inputs, bf16 and fp32 outputs, with and without residual.
+    The shapes cover K split over clusters of 1, 2, 3, 4 and 8 CTAs (K/32
+    chunks of 32 per CTA batch, uneven last share at K = 1056) and warps that
+    loop over more than one batch (K = 16384)."""
     ops = _ops()
     rng = np.random.default_rng(M * 7 + N + K)
     A = oracle.bf16_round(rng.standard_normal((M, K), dtype=np.float32))
-    W = oracle.bf16_round((0.03 * rng.standard_normal((N, K))).astype(np.float32))
+    # outputs of order one at every K, so the absolute tolerance stays above
+    # half a bf16 ulp of the output
+    w_std = min(0.03, 2.0 / np.sqrt(K))
+    W = oracle.bf16_round((w_std * rng.standard_normal((N, K))).astype(np.float32))
     b = (0.1 * rng.standard_normal(N)).astype(np.float32)
     R = oracle.bf16_round(rng.standard_normal((M, N), dtype=np.float32)) if res else None
     ref = oracle.linear(A, W, b, residual=R, act=act)
