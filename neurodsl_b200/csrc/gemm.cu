@@ -37,15 +37,23 @@ constexpr int kBK = 64;
 constexpr int kThreads = 384;
 constexpr uint32_t kATileBytes = kBM * kBK * 2;  // 16 KB
 
+constexpr int kEpiWarps = 8;
+constexpr uint32_t kStagePitch = 80;  // bytes per staged 32-column bf16 row (64 + 16 pad)
+constexpr uint32_t kStageWarpBytes = 32 * kStagePitch;
+constexpr uint32_t kBiasWarpBytes = 4 * 32 * 4;  // a warp's bias: up to 4 chunks of 32
+
 template <int BN>
 struct GemmCfg {
-  // 4 x 48 KB (BN 256), 7 x 32 KB (BN 128) or 9 x 24 KB (BN 64) stages plus
-  // barriers, within the 232,448-byte per-block limit.
-  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 7 : 9);
+  // 4 x 48 KB (BN 256), 6 x 32 KB (BN 128) or 8 x 24 KB (BN 64) stages, then
+  // barriers, the epilogue warps' store staging and their bias slices, within
+  // the 232,448-byte per-block limit.
+  static constexpr int kStages = BN >= 256 ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr uint32_t kBTileBytes = BN * kBK * 2;
   static constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
   static constexpr uint32_t kOffBar = kStages * kStageBytes;
-  static constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;
+  static constexpr uint32_t kOffStaging = kOffBar + 256;
+  static constexpr uint32_t kOffBias = kOffStaging + kEpiWarps * kStageWarpBytes;
+  static constexpr uint32_t kSmemBytes = kOffBias + kEpiWarps * kBiasWarpBytes + 1024;
   static_assert(kSmemBytes <= 232448, "dynamic shared memory per block");
   static constexpr uint32_t kTmemCols = 2 * BN;   // two accumulators (power of two)
   static constexpr uint32_t kIdesc = idesc_bf16_f32(kBM, BN, false, false);
@@ -208,6 +216,66 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const uint6
   }
 }
 
+// One 32-column chunk of the bf16 output for a warp's 32 rows (thread = row),
+// y = act(acc + bias): the bias comes from the tile's copy in shared memory
+// (bias_s, a broadcast read) and the rows go out through the warp's staging
+// buffer, so that each store instruction writes 8 whole 64-byte row segments
+// (16 full sectors) instead of 32 half sectors.  Needs the 16-byte path
+// (vec, col0 + 32 <= N).
+template <int kAct>
+__device__ __forceinline__ void store_chunk_staged(const uint32_t (&r)[32], uint32_t bias_s,
+                                                   bool has_bias, uint32_t stg,
+                                                   __nv_bfloat16* __restrict__ Y, int m_base,
+                                                   int lane, int M, int col0, int N) {
+  uint64_t z[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) z[q] = f2_pack(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+  if (has_bias) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 bb;
+      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(bb.x), "=f"(bb.y), "=f"(bb.z), "=f"(bb.w)
+                   : "r"(bias_s + q * 16));
+      z[2 * q] = f2_add(z[2 * q], f2_pack(bb.x, bb.y));
+      z[2 * q + 1] = f2_add(z[2 * q + 1], f2_pack(bb.z, bb.w));
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 16; ++q) z[q] = act2<kAct>(z[q]);
+  const uint32_t row_s = stg + static_cast<uint32_t>(lane) * kStagePitch;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      float lo, hi;
+      f2_unpack(z[4 * q + h], lo, hi);
+      w[h] = pack_bf16x2(lo, hi);
+    }
+    st_shared_v4(row_s + q * 16, w[0], w[1], w[2], w[3]);
+  }
+  __syncwarp();
+  // read back 8 rows x 4 pieces per instruction, consecutive lanes along a
+  // row, so each global store instruction writes 8 whole 64-byte segments.
+  // (The 80-byte pitch makes the writes conflict-free and costs the reads
+  // one 2-way conflict per quarter-warp; measured faster than a conflict-free
+  // XOR swizzle and than reading 8 rows at one piece per quarter-warp.)
+  const int piece = lane & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int row = j * 8 + (lane >> 2);
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(stg + row * kStagePitch + piece * 16));
+    const int m = m_base + row;
+    if (m < M)
+      *reinterpret_cast<uint4*>(Y + static_cast<size_t>(m) * N + col0 + piece * 8) = v;
+  }
+  __syncwarp();  // the buffer is rewritten by the next chunk
+}
+
 // Tile t of the persistent walk: N fastest within groups of 8 row blocks, so
 // CTAs running at the same time share A rows and W columns in L2.
 __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int& m_blk,
@@ -350,6 +418,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if constexpr (kRes)
       if (static_cast<int>(blockIdx.x) < n_tiles_total) prefetch_residual(blockIdx.x);
+    // bf16 path without residual: lane's float4 of the bias for tile t, chunk
+    // half + 2 * (lane >> 3), columns (lane & 7) * 4 .. + 3 of that chunk
+    auto load_bias4 = [&](int t) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (kRes || kOutF32 || bias == nullptr || !vec || t >= n_tiles_total) return v;
+      int m2, n2;
+      tile_coords(t, m_tiles, n_tiles, m2, n2);
+      const int col = n2 * BN + (half + 2 * (lane >> 3)) * 32 + (lane & 7) * 4;
+      if (col + 4 <= N && (half + 2 * (lane >> 3)) * 32 < BN)
+        v = __ldg(reinterpret_cast<const float4*>(bias + col));
+      return v;
+    };
+    float4 bias_cur = load_bias4(blockIdx.x);
+    float4 bias_next = load_bias4(blockIdx.x + gridDim.x);
     for (int t = blockIdx.x; t < n_tiles_total; t += gridDim.x, ++lt) {
       int m_blk, n_blk;
       tile_coords(t, m_tiles, n_tiles, m_blk, n_blk);
@@ -380,6 +462,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t no_res[16] = {};
         uint32_t r[2][32];
         if (half < n_chunks) tmem_ld32(acc + half * 32, r[0]);
+        // bf16 output: this warp's bias for the tile (its chunks c = half + 2j,
+        // 32 values each) into its own shared-memory slice, one float4 per
+        // lane, the next tile's float4 already loaded; no other warp reads it
+        const uint32_t wbias = smem_u32(smem + Cfg::kOffBias) + (warp - 4) * kBiasWarpBytes;
+        if constexpr (!kOutF32) {
+          st_shared_v4(wbias + lane * 16, __float_as_uint(bias_cur.x), __float_as_uint(bias_cur.y),
+                       __float_as_uint(bias_cur.z), __float_as_uint(bias_cur.w));
+          bias_cur = bias_next;
+          bias_next = load_bias4(t + 2 * static_cast<int>(gridDim.x));
+          __syncwarp();
+        }
+        const uint32_t stg = smem_u32(smem + Cfg::kOffStaging) + (warp - 4) * kStageWarpBytes;
+        const int m_base = m_blk * kBM + quarter * 32;
 #pragma unroll 1
         for (int c = half, k = 0; c < n_chunks; c += 2, ++k) {
           const int col0 = n_blk * BN + c * 32;
@@ -389,8 +484,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #define ND_EPILOGUE_CHUNK(CUR, NXT)                                                        \
           {                                                                               \
             if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);                  \
-            store_chunk<kOutF32, kAct, false>(r[CUR], no_res, bias, residual, residual_f32, Y, \
-                                              m, M, col0, N, vec);                        \
+            if (!kOutF32 && vec && col0 + 32 <= N)                                        \
+              store_chunk_staged<kAct>(r[CUR], wbias + k * 128, bias != nullptr, stg,     \
+                                       static_cast<__nv_bfloat16*>(Y), m_base, lane, M,   \
+                                       col0, N);                                          \
+            else                                                                          \
+              store_chunk<kOutF32, kAct, false>(r[CUR], no_res, bias, residual, residual_f32, \
+                                                Y, m, M, col0, N, vec);                   \
           }
           if (k & 1) ND_EPILOGUE_CHUNK(1, 0) else ND_EPILOGUE_CHUNK(0, 1)
 #undef ND_EPILOGUE_CHUNK
