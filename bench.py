@@ -214,8 +214,8 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
     ids = torch.randint(0, cfg.vocab, (B, S), device=dev, dtype=torch.int32, generator=gen)
     graphs = True
     try:
-        model.generate(ids, steps, graph_chunk=chunk)
-    except Exception:  # collectives that cannot be captured: decode eagerly
+        model.generate(ids, steps, graph_chunk=chunk, graph_prefill=True)
+    except Exception:  # collectives that cannot be captured: run eagerly
         graphs = False
         model.release_graphs()
         torch.cuda.synchronize()
@@ -227,7 +227,10 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
         barrier()
         torch.cuda.synchronize()
         ev[0].record()
-        model.prefill(ids, steps)
+        if graphs:
+            model.prefill_graphed(ids, steps)
+        else:
+            model.prefill(ids, steps)
         ev[1].record()
         if graphs:
             for g in model._graphs:
@@ -260,6 +263,7 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
                       "with residual + LayerNorm") if tp > 1 else None,
         "scaling": "strong" if tp > 1 else "weak",
         "prefill": {"value": replicas * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
+                    "launch": "one CUDA graph" if graphs else "eager launches",
                     "roofline": {"bound": "tensor", "achieved": p_tflops / world,
                                  "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
                                  "frac": p_tflops / world / peaks["bf16_tflops"]}},

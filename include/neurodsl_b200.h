@@ -34,6 +34,9 @@
  *                       cell 15 (rule name src/compiler_config.jl:154-158)
  *   nd_ln_gemm          residual :add src/dispatch.jl:386-417 + :layernorm +
  *                       :linear :363-384 for a decode step's few rows
+ *   nd_gelu, nd_scale_mask, nd_softmax  the unfused :gelu (notebook/compiler.ipynb
+ *                       cell 15 form), :scale_mask src/dispatch.jl:464-474 and
+ *                       :softmax src/kernels.jl:269-287 ops
  *   nd_layernorm        the :layernorm rule symbol src/compiler_config.jl:168-172
  *                       (the reference ships only RMSNorm, rmsnorm_fwd!
  *                       src/kernels.jl:48-64,104-131, used by :rmsnorm
@@ -228,6 +231,20 @@ int nd_gemm_bias_act(void *stream, const void *A, const void *W, const float *bi
 int nd_ln_gemm(void *stream, const void *x, const void *p, const float *p_bias,
                const float *gamma, const float *beta, float eps, void *s_out, const void *W,
                const float *bias, void *Y, int y_dtype, int M, int N, int K, int act);
+
+/*
+ * Unfused graph ops, fp32 in and out (the operator graph's Float32 values);
+ * the compiler's rewrite rules replace them by the fused entry points, and
+ * they run here when a graph is executed without rewriting.
+ *   nd_gelu        y[i] = GELU(x[i]), i < n; act = ND_ACT_GELU_*   (:gelu)
+ *   nd_scale_mask  y = x / sqrt(d_head), -Inf where col > row, for one
+ *                  [rows][cols] score block  (:scale_mask with its causal mask)
+ *   nd_softmax     row softmax of [rows][cols]; a row of -Inf gives zeros
+ *                  (:softmax)
+ */
+int nd_gelu(void *stream, const float *x, float *y, int64_t n, int act);
+int nd_scale_mask(void *stream, const float *x, float *y, int rows, int cols, int d_head);
+int nd_softmax(void *stream, const float *x, float *y, int rows, int cols);
 
 /*
  * LayerNorm over the last dimension of x [rows][d]:

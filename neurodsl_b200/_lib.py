@@ -56,6 +56,9 @@ SIGNATURES = {
     "nd_kv_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
     "nd_ln_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
+    "nd_gelu": (_i, [_vp, _vp, _vp, ctypes.c_int64, _i]),
+    "nd_scale_mask": (_i, [_vp, _vp, _vp, _i, _i, _i]),
+    "nd_softmax": (_i, [_vp, _vp, _vp, _i, _i]),
     "nd_layernorm": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _f]),
     "nd_convert_2d": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i]),
     "nd_embed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),

@@ -22,7 +22,7 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libneurodsl_b200.so")
 SOURCES = ["abi.cu", "tma.cu", "flash_fwd.cu", "kv_decode.cu", "gemm.cu", "layernorm.cu", "model_ops.cu",
-           "tp_comm.cu"]
+           "tp_comm.cu", "elementwise.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",

@@ -1,0 +1,228 @@
+"""NeuroDSL's rewrite-rule compiler, restated over the operator-API mirror, with
+rules that map unfused transformer graphs onto the B200 fused operators.
+
+  reference (Julia)                               here
+  ---------------------------------------------   ---------------------------------
+  RewriteRule  src/compiler_config.jl:75-97       RewriteRule (+ optional `attrs`)
+  CompilerConfig  src/compiler_config.jl:349-359  CompilerConfig
+  op_of / single_consumer                         op_of / single_consumer
+    src/compiler_rules.jl:56-72
+  _is_fuseable_chain  src/compiler_rules.jl:121   _is_fuseable_chain
+  scan_graph  src/compiler_rules.jl:575-623       scan_graph
+  _apply_fusion!  src/compiler.jl:16-66           _apply_fusion
+  compile  src/compiler.jl:70-124                 compile -> CompiledPlan
+  _flash_condition  src/compiler_config.jl:107    _flash_condition
+
+Matching follows the reference: for each rule, every node produced by the
+pattern's first op starts a chain that follows single consumers through the
+pattern; intermediate nodes must have exactly one consumer; the optional
+condition must hold; matches apply in decreasing `cost_delta`.  A fusion
+merges the chain's attrs, takes the chain's external inputs in rule order,
+deletes the intermediate nodes and re-registers the last node's output
+with the fused op.  As in the reference, `training=True` refuses a fusion
+into an op without a backward rule; the B200 operators are inference-only,
+so inference graphs compile with `CompilerConfig(training=False)`.
+
+B200 extension: a rule may carry `attrs` merged into the fused rule (the
+:linear weight is (out, in), so a :linear chain sets `trans_b=True` for ops
+that take a :matmul-style weight), and a condition receives the graph, the
+chain and the namespace like the reference's.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Callable, Dict, List, Optional, Tuple
+
+from . import graph as G
+
+
+@dataclass
+class RewriteRule:
+    name: str
+    pattern: Tuple[str, ...]
+    result: str
+    condition: Optional[Callable] = None
+    cost_delta: float = 1.0
+    verified: bool = False
+    attrs: Dict[str, Any] = field(default_factory=dict)
+
+
+@dataclass
+class RuleMatch:
+    rule: RewriteRule
+    nodes: List[str]
+    namespace: str
+    score: float
+
+
+def producer(g, sym, ns):
+    return g.rules[ns].get(sym)
+
+
+def op_of(g, sym, ns) -> Optional[str]:
+    r = producer(g, sym, ns)
+    return None if r is None else r.op
+
+
+def consumers(g, sym, ns) -> List[str]:
+    return [out for out, r in g.rules[ns].items() if sym in r.inputs]
+
+
+def single_consumer(g, sym, ns) -> Optional[str]:
+    c = consumers(g, sym, ns)
+    return c[0] if len(c) == 1 else None
+
+
+def _is_fuseable_chain(g, chain, ns) -> bool:
+    if len(chain) < 2:
+        return False
+    return all(single_consumer(g, s, ns) is not None for s in chain[:-1])
+
+
+# ------------------------------------------------------------- conditions ---
+
+def _flash_condition(g, chain, ns) -> bool:
+    """The reference's condition on :flash_attention: the first node's value
+    has at least 2 dims and more than 512 rows (src/compiler_config.jl:107-112)."""
+    nd = g.nodes[ns].get(chain[0])
+    v = None if nd is None else nd.value
+    return v is not None and v.dim() >= 2 and v.shape[0] > 512
+
+
+def _naive_attention_condition(g, chain, ns) -> bool:
+    """matmul(Q, K; trans_b=true) -> scale_mask -> softmax -> matmul(P, V): the
+    per-head naive attention of MultiHeadAttention (src/layers.jl:62-72),
+    which is causal softmax(Q·Kᵀ/√d_head)·V — the :flash_attn op.  The last
+    matmul must take the probabilities as its first operand, without
+    transposition."""
+    qk = producer(g, chain[0], ns)
+    pv = producer(g, chain[3], ns)
+    return (bool(qk.attrs.get("trans_b", False)) and len(qk.inputs) == 2
+            and len(pv.inputs) == 2 and pv.inputs[0] == chain[2]
+            and not pv.attrs.get("trans_b", False))
+
+
+def _three_input_layernorm(g, chain, ns) -> bool:
+    """:layernorm with [x, gamma, beta], so the fused op's inputs are
+    [x, gamma, beta, W(, b)]."""
+    return len(producer(g, chain[0], ns).inputs) == 3
+
+
+# ------------------------------------------------------------------ rules ---
+
+B200_RULES: List[RewriteRule] = [
+    RewriteRule("naive_attention_to_flash", ("matmul", "scale_mask", "softmax", "matmul"),
+                "flash_attn", condition=_naive_attention_condition, cost_delta=0.70,
+                attrs={"causal": True}),
+    RewriteRule("layernorm_linear_fusion", ("layernorm", "linear"), "fused_layernorm_linear",
+                condition=_three_input_layernorm, cost_delta=0.40, attrs={"trans_b": True}),
+    RewriteRule("layernorm_matmul_fusion", ("layernorm", "matmul"), "fused_layernorm_linear",
+                condition=_three_input_layernorm, cost_delta=0.40),
+    RewriteRule("linear_gelu_fusion", ("linear", "gelu"), "fused_linear_gelu", cost_delta=0.35,
+                attrs={"trans_b": True}),
+    RewriteRule("matmul_gelu_fusion", ("matmul", "gelu"), "fused_linear_gelu", cost_delta=0.35),
+    RewriteRule("linear_residual_fusion", ("linear", "add"), "fused_linear_residual",
+                cost_delta=0.30),
+]
+
+# fused ops with a backward rule (none of the B200 operators has one)
+BACKWARD_SUPPORT = {"identity"}
+
+
+@dataclass
+class CompilerConfig:
+    rules: List[RewriteRule] = field(default_factory=lambda: list(B200_RULES))
+    training: bool = True
+
+
+@dataclass
+class CompiledPlan:
+    namespace: str
+    order: List[str]
+    fused_ops: Dict[str, str]
+    config: CompilerConfig
+
+    def __call__(self, g, output_sym, ctx_store=None):
+        """Run the compiled graph up to `output_sym` (the reference's
+        plan(g, output_sym), src/compiler.jl:204)."""
+        return G.demand(g, output_sym, ctx_store=ctx_store, namespace=self.namespace)
+
+
+def scan_graph(g, rules=None, namespace=None) -> List[RuleMatch]:
+    ns = namespace or g.active_ns
+    rules = B200_RULES if rules is None else rules
+    if ns not in g.rules:
+        return []
+    matches: List[RuleMatch] = []
+    for rule in rules:
+        if not rule.pattern:
+            continue
+        for sym, r in list(g.rules[ns].items()):
+            if r.op != rule.pattern[0]:
+                continue
+            chain = [sym]
+            ok = True
+            for expected in rule.pattern[1:]:
+                nxt = single_consumer(g, chain[-1], ns)
+                if nxt is None or op_of(g, nxt, ns) != expected:
+                    ok = False
+                    break
+                chain.append(nxt)
+            if not ok:
+                continue
+            if len(chain) > 1 and not _is_fuseable_chain(g, chain, ns):
+                continue
+            if rule.condition is not None:
+                try:
+                    if not rule.condition(g, chain, ns):
+                        continue
+                except Exception:   # a failing condition makes the rule inapplicable
+                    continue
+            matches.append(RuleMatch(rule, chain, ns, rule.cost_delta))
+    matches.sort(key=lambda m: -m.score)
+    return matches
+
+
+def _apply_fusion(g, ns, chain, rule: RewriteRule, training=True) -> bool:
+    fused_op = rule.result
+    if training and fused_op != "identity" and fused_op not in BACKWARD_SUPPORT:
+        return False
+    if any(s not in g.rules[ns] or g.rules[ns][s].op != op
+           for s, op in zip(chain, rule.pattern)):
+        return False       # an earlier fusion took or rewrote part of this chain
+    for a, b in zip(chain[:-1], chain[1:]):
+        users = consumers(g, a, ns)
+        if len(users) != 1 or users[0] != b:
+            return False
+    rules = [g.rules[ns][s] for s in chain]
+    merged: Dict[str, Any] = {}
+    for r in rules:
+        merged.update(r.attrs)
+    merged.update(rule.attrs)
+    intermediate = {r.output for r in rules[:-1]}
+    fused_inputs: List[str] = []
+    for r in rules:
+        for inp in r.inputs:
+            if inp not in intermediate and inp not in fused_inputs:
+                fused_inputs.append(inp)
+    out = rules[-1].output
+    for s in chain[:-1]:
+        del g.rules[ns][s]
+        del g.nodes[ns][s]
+    del g.rules[ns][chain[-1]]
+    G.addrule(g, G.GraphRule(out, fused_inputs, fused_op, attrs=merged, namespace=ns))
+    G._invalidate_downstream(g, out, ns)
+    return True
+
+
+def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> CompiledPlan:
+    """Scan, apply the matches in decreasing score, recompute the order."""
+    config = config or CompilerConfig()
+    ns = namespace or g.active_ns
+    fused_ops: Dict[str, str] = {}
+    for m in scan_graph(g, config.rules, ns):
+        if _apply_fusion(g, ns, m.nodes, m.rule, training=config.training):
+            fused_ops[m.nodes[-1]] = m.rule.result
+    g._topo_cache[ns] = None
+    order = G.topo_order(g, ns)
+    return CompiledPlan(ns, order, fused_ops, config)

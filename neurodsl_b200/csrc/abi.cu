@@ -7,6 +7,7 @@
 // the host wrappers turn a non-zero status back into an exception.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdarg.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -19,6 +20,7 @@
 #include "gemm.h"
 #include "kv_decode.h"
 #include "launch.cuh"
+#include "elementwise.h"
 #include "layernorm.h"
 #include "model_ops.h"
 #include "tp_comm.h"
@@ -527,6 +529,47 @@ __attribute__((visibility("default"))) int nd_ln_gemm(void* stream, const void* 
       static_cast<__nv_bfloat16*>(s_out), static_cast<const __nv_bfloat16*>(W), bias, Y,
       y_dtype == ND_F32, M, N, K, act);
   if (e != cudaSuccess) return cuda_fail(e, "nd_ln_gemm");
+  return ok();
+}
+
+// Unfused graph ops (fp32): :gelu, :scale_mask (causal), :softmax.
+__attribute__((visibility("default"))) int nd_gelu(void* stream, const float* x, float* y,
+                                                   int64_t n, int act) {
+  if (n < 0) return fail(ND_ERR_INVALID_ARG, "nd_gelu: negative size");
+  if (act < ND_ACT_GELU_SIGMOID || act > ND_ACT_GELU_ERF)
+    return fail(ND_ERR_UNSUPPORTED, "nd_gelu: act %d is not a GELU form", act);
+  if (n == 0) return ok();
+  if (!x || !y) return fail(ND_ERR_INVALID_ARG, "nd_gelu: null pointer");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_gelu(static_cast<cudaStream_t>(stream), x, y, n, act);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_gelu");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_scale_mask(void* stream, const float* x, float* y,
+                                                         int rows, int cols, int d_head) {
+  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_scale_mask: negative size");
+  if (d_head <= 0) return fail(ND_ERR_INVALID_ARG, "nd_scale_mask: d_head = %d", d_head);
+  if (static_cast<long long>(rows) * cols == 0) return ok();
+  if (!x || !y) return fail(ND_ERR_INVALID_ARG, "nd_scale_mask: null pointer");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_scale_mask(static_cast<cudaStream_t>(stream), x, y, rows, cols,
+                                        1.f / sqrtf(static_cast<float>(d_head)));
+  if (e != cudaSuccess) return cuda_fail(e, "nd_scale_mask");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_softmax(void* stream, const float* x, float* y,
+                                                      int rows, int cols) {
+  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_softmax: negative size");
+  if (static_cast<long long>(rows) * cols == 0) return ok();
+  if (!x || !y) return fail(ND_ERR_INVALID_ARG, "nd_softmax: null pointer");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_softmax(static_cast<cudaStream_t>(stream), x, y, rows, cols);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_softmax");
   return ok();
 }
 

@@ -234,16 +234,20 @@ def _infer_output_shape(op: str, inputs, attrs):
         A, B = inputs[0], inputs[1]
         tb = attrs.get("trans_b", False)
         return (A.shape[0], B.shape[0] if tb else B.shape[1])
-    if op in ("linear", "fused_linear_residual", "fused_layernorm_linear"):
+    if op in ("linear", "fused_linear_residual"):
         X, W = inputs[0], inputs[1]
         return (X.shape[0], W.shape[0])
+    if op == "fused_layernorm_linear":                       # [x, gamma, beta, W(, b)]
+        W = inputs[3]
+        return (inputs[0].shape[0], W.shape[0] if attrs.get("trans_b", False) else W.shape[1])
     if op == "hcat_heads":
         return (inputs[0].shape[0], sum(x.shape[1] for x in inputs))
     if op == "slice_cols":
         return (inputs[0].shape[0], attrs["end_col"] - attrs["start_col"] + 1)
     if op == "flash_attention" and len(inputs) == 1:
         return (inputs[0].shape[0], inputs[0].shape[1] // 3)   # fused (S, 3d) projection
-    if op in ("add", "identity", "flash_attn", "flash_attention", "layernorm", "gelu"):
+    if op in ("add", "identity", "flash_attn", "flash_attention", "layernorm", "gelu",
+              "scale_mask", "softmax"):
         return tuple(inputs[0].shape)
     if op == "kv_decode_attn":
         return tuple(inputs[0].shape)
@@ -516,9 +520,13 @@ def _dispatch_fused_linear_gelu(dev, output_buffer, inputs, attrs, out_sym, out_
 
 def _dispatch_fused_linear_residual(dev, output_buffer, inputs, attrs, out_sym, out_node,
                                     ctx_store):
-    """:fused_linear_residual — X·Wᵀ + b + R: the :linear rule followed by the
-    residual :add (src/dispatch.jl:363-417) in one GEMM epilogue."""
-    X, W, b, R = inputs[0], inputs[1], inputs[2], inputs[3]
+    """:fused_linear_residual — X·Wᵀ (+ b) + R, inputs [X, W, (b,) R]: the
+    :linear rule followed by the residual :add (src/dispatch.jl:363-417) in
+    one GEMM epilogue."""
+    if len(inputs) == 4:
+        X, W, b, R = inputs
+    else:                                   # a :linear without bias, then the :add
+        (X, W, R), b = inputs, None
     res = R if R.is_contiguous() else R.contiguous()
     _gemm_into(output_buffer, X, _bf16_rows(W), bias=b, residual=res)
     _store_ctx(ctx_store, out_sym, {"X": X, "W": W, "n_inputs": 4})
@@ -554,6 +562,66 @@ def _dispatch_add(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_stor
     return output_buffer
 
 
+def _f32(x):
+    return x if x.dtype == torch.float32 and x.is_contiguous() else x.float().contiguous()
+
+
+def _dispatch_gelu(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:gelu — elementwise GELU in the form of attr :approx (default :sigmoid,
+    the z·σ(1.702 z) of the reference's fused_linear_gelu notebook op); the
+    compiler fuses a :matmul / :linear followed by it into
+    :fused_linear_gelu."""
+    approx = _GELU_APPROX[str(attrs.get("approx", "sigmoid")).lstrip(":")]
+    ops.gelu(_f32(inputs[0]), act=approx, out=output_buffer)
+    _store_ctx(ctx_store, out_sym, {"x": inputs[0], "approx": approx})
+    return output_buffer
+
+
+def _dispatch_scale_mask(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:scale_mask — scores / sqrt(d_head) plus the causal mask
+    (src/dispatch.jl:464-474); ctx {scale}."""
+    scores = inputs[0]
+    d_head = int(attrs.get("d_head", scores.shape[1]))
+    ops.scale_mask(_f32(scores), d_head, out=output_buffer)
+    _store_ctx(ctx_store, out_sym, {"scale": 1.0 / math.sqrt(d_head)})
+    return output_buffer
+
+
+def _dispatch_softmax(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
+    """:softmax — row softmax (src/kernels.jl:269-287); ctx {output}."""
+    ops.softmax(_f32(inputs[0]), out=output_buffer)
+    _store_ctx(ctx_store, out_sym, {"output": output_buffer})
+    return output_buffer
+
+
+def _dispatch_fused_layernorm_linear(dev, output_buffer, inputs, attrs, out_sym, out_node,
+                                     ctx_store):
+    """:fused_layernorm_linear — LayerNorm(x; gamma, beta, :eps) · W (+ b),
+    inputs [x, gamma, beta, W(, b)], attr :trans_b (true for a :linear weight
+    (out, in)).  At most 32 bf16 rows with K % 32 == 0 and K <= 1024 take
+    nd_ln_gemm (one launch, the LayerNorm in the GEMM prologue); otherwise the
+    LayerNorm goes to a bf16 buffer (aux_data[:_ln_buf]) read by the GEMM."""
+    x, gamma, beta, W = inputs[:4]
+    b = inputs[4] if len(inputs) > 4 else None
+    eps = float(attrs.get("eps", 1e-5))
+    Wnk = _weight_nk(W, attrs.get("trans_b", False))
+    g = gamma.reshape(-1).float().contiguous()
+    bt = beta.reshape(-1).float().contiguous()
+    rows, K = x.shape
+    if x.dtype == torch.bfloat16 and rows <= 32 and K % 32 == 0 and K <= 1024:
+        ops.ln_linear(x.contiguous(), Wnk, gamma=g, beta=bt, eps=eps, bias=_bias_vec(b),
+                      out=output_buffer)
+    else:
+        h = out_node.aux_data.get("_ln_buf")
+        if h is None or tuple(h.shape) != (rows, K):
+            h = torch.empty((rows, K), dtype=torch.bfloat16, device=dev.torch_device)
+            out_node.aux_data["_ln_buf"] = h
+        ops.layernorm(x.contiguous(), g, bt, eps=eps, out=h, stats=False)
+        ops.linear(h, Wnk, _bias_vec(b), out=output_buffer)
+    _store_ctx(ctx_store, out_sym, {"x": x, "gamma": gamma, "beta": beta, "W": W})
+    return output_buffer
+
+
 def register_b200_ops():
     """Register the B200 operators (the @defop / register_op! plugin form)."""
     register_op("flash_attn", _dispatch_flash_attn)
@@ -563,6 +631,10 @@ def register_b200_ops():
     register_op("fused_linear_residual", _dispatch_fused_linear_residual)
     register_op("layernorm", _dispatch_layernorm)
     register_op("add", _dispatch_add)
+    register_op("gelu", _dispatch_gelu)
+    register_op("scale_mask", _dispatch_scale_mask)
+    register_op("softmax", _dispatch_softmax)
+    register_op("fused_layernorm_linear", _dispatch_fused_layernorm_linear)
 
 
 register_b200_ops()

@@ -321,11 +321,37 @@ class GPT:
         """Generated tokens so far: [B][steps] (prefill's token first)."""
         return self.buf["ids"][1:].t()
 
-    def generate(self, ids, steps, graph_chunk=0):
+    def prefill_graphed(self, ids, steps=0):
+        """prefill(ids, steps) replayed from a CUDA graph captured on the first
+        call for this (prompt shape, steps): the prompt is copied into a static
+        buffer and the ~10 launches per layer replay without host work in
+        between.  Returns the logits like prefill."""
+        key = (tuple(ids.shape), max(steps, 1))
+        if getattr(self, "_prefill_key", None) != key:
+            self._prefill_graph = None
+            self._prefill_ids = torch.empty_like(ids)
+            self._prefill_ids.copy_(ids)
+            self.prefill(self._prefill_ids, steps)   # buffers allocated outside the capture
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self.prefill(self._prefill_ids, steps)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            self._prefill_graph, self._prefill_key = g, key
+        self._prefill_ids.copy_(ids)
+        self._prefill_graph.replay()
+        return self.buf["logits"]
+
+    def generate(self, ids, steps, graph_chunk=0, graph_prefill=False):
         """Greedy generation of `steps` tokens after the prompt ids [B][S].
         graph_chunk > 0 captures that many decode steps per CUDA graph (the
-        graphs are kept and replayed by later calls of the same shape)."""
-        self.prefill(ids, steps)
+        graphs are kept and replayed by later calls of the same shape);
+        graph_prefill replays the prefill from a CUDA graph too."""
+        if graph_prefill:
+            self.prefill_graphed(ids, steps)
+        else:
+            self.prefill(ids, steps)
         n_dec = steps - 1
         if graph_chunk <= 0:
             for t in range(n_dec):
@@ -353,6 +379,8 @@ class GPT:
         process group is destroyed)."""
         self._graphs = []
         self._graphs_key = None
+        self._prefill_graph = None
+        self._prefill_key = None
 
     def close(self):
         """Release graphs and the NVLink reduction regions (collective when

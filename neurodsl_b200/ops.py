@@ -255,6 +255,39 @@ def ln_linear(x, W, p=None, p_bias=None, gamma=None, beta=None, eps=1e-5, s_out=
     return out
 
 
+def gelu(x, act="sigmoid", out=None, stream=None):
+    """Elementwise GELU of a float32 tensor (nd_gelu, the unfused :gelu op)."""
+    _need(x, "x", torch.float32)
+    if out is None:
+        out = torch.empty_like(x)
+    _need(out, "out", torch.float32)
+    check(_lib.load().nd_gelu(_stream(stream), _ptr(x), _ptr(out), x.numel(),
+                              ACT[act] if isinstance(act, str) else int(act)))
+    return out
+
+
+def scale_mask(scores, d_head, out=None, stream=None):
+    """scores / sqrt(d_head) with the causal mask (-Inf above the diagonal) of
+    one float32 [rows][cols] block (nd_scale_mask, the :scale_mask op)."""
+    _need(scores, "scores", torch.float32, 2)
+    if out is None:
+        out = torch.empty_like(scores)
+    _need(out, "out", torch.float32, 2)
+    check(_lib.load().nd_scale_mask(_stream(stream), _ptr(scores), _ptr(out), scores.shape[0],
+                                    scores.shape[1], int(d_head)))
+    return out
+
+
+def softmax(x, out=None, stream=None):
+    """Row softmax of a float32 [rows][cols] matrix (nd_softmax, the :softmax op)."""
+    _need(x, "x", torch.float32, 2)
+    if out is None:
+        out = torch.empty_like(x)
+    _need(out, "out", torch.float32, 2)
+    check(_lib.load().nd_softmax(_stream(stream), _ptr(x), _ptr(out), x.shape[0], x.shape[1]))
+    return out
+
+
 def layernorm(x, gamma=None, beta=None, eps=1e-5, out=None, out_dtype=None, mean=None,
               rstd=None, stats=True, stream=None):
     """Row LayerNorm of x [rows][d]; returns (y, mean, rstd).  With

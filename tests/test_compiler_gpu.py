@@ -1,0 +1,152 @@
+"""GPU checks of graphs compiled by the rewrite rules: each graph runs once as
+written (unfused ops, each a library kernel) and once compiled onto the fused
+operators; both are compared with the oracle (bf16-operand tolerance:
+max-abs 2e-2, rel-L2 1e-2) and with each other."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import oracle  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_L2 = 2e-2, 1e-2
+
+
+def _mods():
+    from neurodsl_b200 import compiler as C
+    from neurodsl_b200 import graph as G
+    return C, G
+
+
+def check(out, ref, max_abs=MAX_ABS, rel_l2=REL_L2):
+    out = np.asarray(out, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = float(np.abs(out - ref).max())
+    rel = float(np.linalg.norm(out - ref) / max(np.linalg.norm(ref), 1e-30))
+    assert err <= max_abs and rel <= rel_l2, (err, rel)
+
+
+def _run(build, compiled, out):
+    C, G = _mods()
+    g = G.NeuroGraph()
+    build(G, g)
+    fused = {}
+    if compiled:
+        fused = C.compile(g, C.CompilerConfig(training=False)).fused_ops
+    y = G.demand(g, out)
+    torch.cuda.synchronize()
+    return y.float().cpu().numpy(), fused, g
+
+
+def test_unfused_elementwise_ops_match_oracle():
+    _, G = _mods()
+    rng = np.random.default_rng(0)
+    s = rng.standard_normal((96, 96)).astype(np.float32) * 4
+    x = rng.standard_normal((37, 50)).astype(np.float32)
+    g = G.NeuroGraph()
+    G.set_(g, "s", s)
+    G.set_(g, "x", x)
+    G.addrule(g, G.GraphRule("sm", ["s"], "scale_mask", attrs={"d_head": 64}))
+    G.addrule(g, G.GraphRule("p", ["sm"], "softmax"))
+    G.addrule(g, G.GraphRule("ge", ["x"], "gelu", attrs={"approx": "tanh"}))
+    p = G.demand(g, "p").cpu().numpy()
+    ge = G.demand(g, "ge").cpu().numpy()
+    np.testing.assert_allclose(p, oracle.softmax(oracle.scale_mask(s, 64)), atol=1e-6, rtol=1e-5)
+    np.testing.assert_allclose(np.triu(p, 1), 0.0)
+    # the oracle's GELU through an identity matrix (x·I is exact in fp32)
+    ge_ref = oracle.linear(x, np.eye(x.shape[1], dtype=np.float32), act="tanh")
+    np.testing.assert_allclose(ge, ge_ref, atol=1e-5, rtol=1e-5)
+
+
+def test_matmul_gelu_compiles_to_the_fused_gemm():
+    rng = np.random.default_rng(1)
+    x = oracle.bf16_round(rng.standard_normal((128, 256)).astype(np.float32))
+    W = oracle.bf16_round((0.05 * rng.standard_normal((256, 384))).astype(np.float32))
+
+    def build(G, g):
+        G.set_(g, "x", x)
+        G.set_(g, "W", W, is_param=True)
+        G.addrule(g, G.GraphRule("u", ["x", "W"], "matmul", attrs={"trans_b": False}))
+        G.addrule(g, G.GraphRule("v", ["u"], "gelu", attrs={"approx": "sigmoid"}))
+    y0, _, _ = _run(build, False, "v")
+    y1, fused, g = _run(build, True, "v")
+    assert fused == {"v": "fused_linear_gelu"} and "u" not in g.nodes["default"]
+    ref = oracle.linear(x, W, trans_w=False, act="sigmoid")
+    check(y0, ref)
+    check(y1, ref)
+
+
+@pytest.mark.parametrize("rows,dtype", [(64, torch.float32), (16, torch.bfloat16)])
+def test_layernorm_linear_compiles_to_the_fused_op(rows, dtype):
+    rng = np.random.default_rng(rows)
+    d, n = 512, 384
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    gm = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    bt = (0.1 * rng.standard_normal(d)).astype(np.float32)
+    W = oracle.bf16_round((0.05 * rng.standard_normal((n, d))).astype(np.float32))
+    b = (0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    def build(G, g):
+        G.set_(g, "x", torch.from_numpy(x).to(dtype))
+        G.set_(g, "g", gm, is_param=True)
+        G.set_(g, "b", bt, is_param=True)
+        G.set_(g, "W", W, is_param=True)
+        G.set_(g, "bw", b, is_param=True)
+        G.addrule(g, G.GraphRule("h", ["x", "g", "b"], "layernorm", attrs={"eps": 1e-5}))
+        G.addrule(g, G.GraphRule("y", ["h", "W", "bw"], "linear"))
+    y0, _, _ = _run(build, False, "y")
+    y1, fused, _ = _run(build, True, "y")
+    assert fused == {"y": "fused_layernorm_linear"}
+    xin = torch.from_numpy(x).to(dtype).float().numpy()
+    h, _, _ = oracle.layernorm(xin, gm, bt, 1e-5)
+    ref = oracle.linear(oracle.bf16_round(h), W, b)
+    check(y0, ref)
+    check(y1, ref)
+    if dtype == torch.float32:
+        # the fused op's LayerNorm writes bf16 directly, the same values the
+        # unfused :linear gets by converting the fp32 LayerNorm output
+        np.testing.assert_array_equal(y0, y1)
+
+
+def test_naive_attention_compiles_to_flash_attn():
+    rng = np.random.default_rng(3)
+    S, D = 256, 64
+    q, k, v = (oracle.bf16_round(rng.standard_normal((S, D)).astype(np.float32)) for _ in range(3))
+
+    def build(G, g):
+        for name, a in (("q", q), ("k", k), ("v", v)):
+            G.set_(g, name, a)
+        G.addrule(g, G.GraphRule("sc", ["q", "k"], "matmul", attrs={"trans_b": True}))
+        G.addrule(g, G.GraphRule("sk", ["sc"], "scale_mask", attrs={"d_head": D}))
+        G.addrule(g, G.GraphRule("pr", ["sk"], "softmax"))
+        G.addrule(g, G.GraphRule("ao", ["pr", "v"], "matmul"))
+    y0, _, _ = _run(build, False, "ao")
+    y1, fused, g = _run(build, True, "ao")
+    assert fused == {"ao": "flash_attn"} and set(g.rules["default"]) == {"ao"}
+    ref, _, _ = oracle.attn_simple(q, k, v, D, causal=True)
+    check(y0, ref)
+    check(y1, ref)
+
+
+def test_linear_add_compiles_to_the_residual_gemm():
+    rng = np.random.default_rng(4)
+    x = oracle.bf16_round(rng.standard_normal((96, 256)).astype(np.float32))
+    W = oracle.bf16_round((0.05 * rng.standard_normal((128, 256))).astype(np.float32))
+    b = (0.1 * rng.standard_normal(128)).astype(np.float32)
+    r = rng.standard_normal((96, 128)).astype(np.float32)
+
+    def build(G, g):
+        G.set_(g, "x", x)
+        G.set_(g, "W", W, is_param=True)
+        G.set_(g, "b", b, is_param=True)
+        G.set_(g, "r", r)
+        G.addrule(g, G.GraphRule("y", ["x", "W", "b"], "linear"))
+        G.addrule(g, G.GraphRule("z", ["r", "y"], "add"))
+    y0, _, _ = _run(build, False, "z")
+    y1, fused, _ = _run(build, True, "z")
+    assert fused == {"z": "fused_linear_residual"}
+    ref = oracle.linear(x, W, b, residual=r)
+    check(y0, ref)
+    check(y1, ref)

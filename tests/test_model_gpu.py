@@ -67,3 +67,22 @@ def test_rejects_sequences_past_the_position_table():
     model, cfg = _model()
     with pytest.raises(ValueError):
         model.prefill(torch.zeros((1, 60), dtype=torch.int32, device="cuda"), steps=10)
+
+
+def test_graphed_prefill_matches_eager():
+    """prefill_graphed (a captured CUDA graph, replayed with a new prompt
+    copied into its static buffer) gives the eager prefill's logits and first
+    token, on a second prompt too."""
+    from neurodsl_b200.model import GPT, GPTConfig
+    cfg = GPTConfig(n_layer=2, d_model=256, n_head=4, d_ff=1024, vocab=3001, n_pos=256)
+    m = GPT(cfg, seed=3)
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    for _ in range(2):
+        ids = torch.randint(0, cfg.vocab, (3, 48), device="cuda", dtype=torch.int32, generator=gen)
+        eager = m.prefill(ids, 4).clone()
+        first = m.buf["ids"][1].clone()
+        graphed = m.prefill_graphed(ids, 4).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(eager, graphed)
+        assert torch.equal(first, m.buf["ids"][1])
+    m.release_graphs()
