@@ -36,12 +36,16 @@ namespace {
 constexpr size_t kFlagsBytes = sizeof(uint32_t) * kCommMaxRanks * kCommMaxCtas;
 constexpr size_t kCountersOff = kFlagsBytes;
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Flags use the fence / relaxed-access form of release and acquire: one
+// system-scope fence before the stores to every peer (a st.release per peer
+// would wait for each earlier remote store to complete before the next), and
+// relaxed polls followed by one fence once every peer's flag is seen.
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 // 16 bytes, cached in L2 only (a slot is rewritten every other call)
@@ -123,12 +127,12 @@ __global__ void __launch_bounds__(256)
   if (threadIdx.x == 0) {
     uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
     const uint32_t seq = counters[blockIdx.x] + 1;
-    __threadfence_system();
+    __threadfence_system();  // release: this rank's slot before the flags
 #pragma unroll
     for (int p = 0; p < kCommMaxRanks; ++p) {
       if (p >= tp || p == rank) continue;
       uint32_t* flags = reinterpret_cast<uint32_t*>(regs.r[p]);
-      st_release_sys(flags + rank * kCommMaxCtas + blockIdx.x, seq);
+      st_relaxed_sys(flags + rank * kCommMaxCtas + blockIdx.x, seq);
     }
     int ok = 1;
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(own);
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(256)
       if (p == rank) continue;
       const uint32_t* f = mine + p * kCommMaxCtas + blockIdx.x;
       uint32_t it = 0;
-      while (static_cast<int32_t>(ld_acquire_sys(f) - seq) < 0) {
+      while (static_cast<int32_t>(ld_relaxed_sys(f) - seq) < 0) {
         if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
           ok = 0;
           if (err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
@@ -145,6 +149,7 @@ __global__ void __launch_bounds__(256)
         }
       }
     }
+    __threadfence_system();  // acquire: the peers' slots after their flags
     counters[blockIdx.x] = seq;
     s_ok = ok;
   }
