@@ -83,6 +83,12 @@ def test_pdl_switch_is_per_call_state_without_a_gpu():
                                    16, 64, 0.125, None, 0)
     assert rc == _lib.ND_ERR_SHAPE
     assert b"row stride" in lib.nd_last_error_string()
+    # the unfused graph ops refuse bad arguments before touching the device
+    assert lib.nd_gelu(None, None, None, 16, 0) == _lib.ND_ERR_UNSUPPORTED      # not a GELU form
+    assert lib.nd_gelu(None, None, None, -1, 1) == _lib.ND_ERR_INVALID_ARG
+    assert lib.nd_scale_mask(None, None, None, 4, 4, 0) == _lib.ND_ERR_INVALID_ARG  # d_head 0
+    assert lib.nd_softmax(None, None, None, -2, 4) == _lib.ND_ERR_INVALID_ARG
+    assert lib.nd_gelu(None, None, None, 0, 1) == _lib.ND_OK                     # empty
     # nd_ln_gemm: K must be a multiple of 32 up to 1024, at most 32 rows
     for M, K in ((4, 80), (4, 2048), (33, 64)):
         rc = lib.nd_ln_gemm(None, None, None, None, None, None, 1e-5, None, None, None, None, 1,
