@@ -8,10 +8,13 @@ library's prefill kernel over all 128 (batch, head) pairs.  Metric: attention
 TFLOP/s with the algorithmic causal count 4·B·H·D·S(S+1)/2 per step.  The same
 JSON line carries the KV-cache decode workload (batch 64, 12 heads, head_dim
 64, cache 1024 -> 1152 over 128 appending steps) as tokens/s, each with its
-roofline against the measured B200 peaks, and two whole decoders assembled
-from the library (prefill tokens/s and greedy-decode tokens/s): GPT-2 small
+roofline against the measured B200 peaks, the fused GEMM + bias + GELU and
+LayerNorm kernels on their own shapes, and two whole decoders assembled from
+the library (prefill tokens/s and greedy-decode tokens/s): GPT-2 small
 (batch 16, prompt 512, 256 tokens; one replica per GPU) and a 24-layer d=1024
 model (batch 32, prompt 2048, 512 tokens; tensor-parallel over all GPUs).
+The decoders' prefill is replayed from one CUDA graph and their decode steps
+from graphs of several steps each; token ids stay on the device throughout.
 
 Multi-GPU: one process per GPU (torchrun); every rank runs its own full
 workload (independent batches, no collective on the data path) and the job
