@@ -12,6 +12,7 @@ rules that map unfused transformer graphs onto the B200 fused operators.
   _apply_fusion!  src/compiler.jl:16-66           _apply_fusion
   compile  src/compiler.jl:70-124                 compile -> CompiledPlan
   _flash_condition  src/compiler_config.jl:107    _flash_condition
+  memory plan + BufferPool (liveness.jl)          neurodsl_b200/liveness.py
 
 Matching follows the reference: for each rule, every node produced by the
 pattern's first op starts a chain that follows single consumers through the
@@ -34,6 +35,7 @@ from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, List, Optional, Tuple
 
 from . import graph as G
+from . import liveness as L
 
 
 @dataclass
@@ -133,6 +135,7 @@ BACKWARD_SUPPORT = {"identity"}
 class CompilerConfig:
     rules: List[RewriteRule] = field(default_factory=lambda: list(B200_RULES))
     training: bool = True
+    pooled: bool = True      # run with the memory plan's buffer pool
 
 
 @dataclass
@@ -141,10 +144,18 @@ class CompiledPlan:
     order: List[str]
     fused_ops: Dict[str, str]
     config: CompilerConfig
+    memory_plan: Optional[L.MemoryPlan] = None
+    pool: Optional[L.BufferPool] = None
 
     def __call__(self, g, output_sym, ctx_store=None):
         """Run the compiled graph up to `output_sym` (the reference's
-        plan(g, output_sym), src/compiler.jl:204)."""
+        plan(g, output_sym), src/compiler.jl:204): with the buffer pool, every
+        intermediate's buffer returns to the pool when its liveness interval
+        ends and later nodes reuse it (a CtxStore then holds buffers that later
+        nodes overwrite: keep it for unpooled runs)."""
+        if self.config.pooled and self.memory_plan is not None:
+            return L.run_planned(g, self.memory_plan, self.pool, output_sym, self.namespace,
+                                 ctx_store)
         return G.demand(g, output_sym, ctx_store=ctx_store, namespace=self.namespace)
 
 
@@ -225,4 +236,5 @@ def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> Compi
             fused_ops[m.nodes[-1]] = m.rule.result
     g._topo_cache[ns] = None
     order = G.topo_order(g, ns)
-    return CompiledPlan(ns, order, fused_ops, config)
+    memory_plan = L.plan_memory(g, ns)
+    return CompiledPlan(ns, order, fused_ops, config, memory_plan, L.BufferPool(g.device))

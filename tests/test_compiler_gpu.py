@@ -150,3 +150,45 @@ def test_linear_add_compiles_to_the_residual_gemm():
     ref = oracle.linear(x, W, b, residual=r)
     check(y0, ref)
     check(y1, ref)
+
+
+def test_pooled_plan_reuses_buffers_and_matches_demand():
+    """A compiled plan run with its buffer pool gives the bits of an unpooled
+    demand; intermediates return their buffers (value None, invalid), the
+    output stays, and a second run takes every buffer from the pool."""
+    C, G = _mods()
+    rng = np.random.default_rng(6)
+    x = rng.standard_normal((64, 256)).astype(np.float32)
+    gm = np.ones(256, np.float32)
+    bt = np.zeros(256, np.float32)
+    W1 = (0.05 * rng.standard_normal((512, 256))).astype(np.float32)
+    W2 = (0.05 * rng.standard_normal((256, 512))).astype(np.float32)
+
+    def build(G, g):
+        G.set_(g, "x", x)
+        for name, a in (("g", gm), ("b", bt), ("W1", W1), ("W2", W2)):
+            G.set_(g, name, a, is_param=True)
+        G.addrule(g, G.GraphRule("h", ["x", "g", "b"], "layernorm"))
+        G.addrule(g, G.GraphRule("u", ["h", "W1"], "linear"))
+        G.addrule(g, G.GraphRule("v", ["u"], "gelu", attrs={"approx": "tanh"}))
+        G.addrule(g, G.GraphRule("y", ["v", "W2"], "linear"))
+        G.addrule(g, G.GraphRule("z", ["y", "x"], "add"))
+    ref, _, _ = _run(build, True, "z")           # compiled, unpooled demand
+    g = G.NeuroGraph()
+    build(G, g)
+    plan = C.compile(g, C.CompilerConfig(training=False))
+    assert plan.fused_ops == {"u": "fused_layernorm_linear", "z": "fused_linear_residual"}
+    out = plan(g, "z").cpu().numpy()
+    np.testing.assert_array_equal(out, ref)
+    ns = g.nodes["default"]
+    computed = [s for s in plan.memory_plan.order if s in g.rules["default"] and s != "z"]
+    assert computed and all(ns[s].value is None and not ns[s].valid for s in computed)
+    assert ns["z"].valid and ns["x"].value is not None
+    st = plan.pool.stats()
+    G.set_(g, "x", x)                               # invalidates everything downstream
+    out2 = plan(g, "z").cpu().numpy()
+    np.testing.assert_array_equal(out2, ref)
+    st2 = plan.pool.stats()
+    # the intermediates' buffers come back from the pool; the kept output's
+    # own buffer is reused in place
+    assert st2["allocs"] == st["allocs"] and st2["hits"] == st["hits"] + len(computed)

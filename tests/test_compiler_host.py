@@ -123,3 +123,52 @@ def test_failing_condition_makes_rule_inapplicable():
     _rule(g, "u", ["x", "W"], "matmul")
     _rule(g, "v", ["u"], "gelu")
     assert C.scan_graph(g, [rule]) == []
+
+
+# ------------------------------------------------------------ memory plan ---
+
+def test_liveness_and_slots_of_a_chain():
+    """x -> a -> b -> c, plus d = f(a, c): a lives until d; b's slot is free
+    again when c starts only if b's last use is before c's first step."""
+    from neurodsl_b200 import liveness as L
+    g = _graph(["x", "W"])
+    _rule(g, "a", ["x", "W"], "matmul")
+    _rule(g, "b", ["a"], "gelu")
+    _rule(g, "c", ["b"], "gelu")
+    _rule(g, "d", ["a", "c"], "add")
+    order = G.topo_order(g)
+    live = L.compute_liveness(g)
+    pos = {s: i + 1 for i, s in enumerate(order)}
+    assert live["a"] == L.LivenessInterval(pos["a"], pos["d"])
+    assert live["b"] == L.LivenessInterval(pos["b"], pos["c"])
+    assert live["W"].last_use == len(order)          # parameter: to the end
+    slot = L.greedy_interval_coloring(live, order)
+    # nodes alive at the same step never share a slot
+    for s in order:
+        for t in order:
+            if s < t and slot[s] == slot[t]:
+                a, b = live[s], live[t]
+                assert a.last_use < b.first_use or b.last_use < a.first_use
+    plan = L.plan_memory(g)
+    assert plan.n_slots == max(slot.values()) and plan.order == order
+
+
+def test_buffer_pool_buckets_by_shape_and_dtype():
+    import torch
+    from neurodsl_b200 import liveness as L
+    pool = L.BufferPool(torch.device("cpu"))
+    a = pool.acquire((4, 8))
+    pool.release(a)
+    assert pool.acquire((4, 8)) is a                 # reused
+    b = pool.acquire((4, 8), torch.bfloat16)         # other dtype: a new buffer
+    assert b is not a and b.dtype == torch.bfloat16
+    assert pool.stats() == {"allocs": 2, "hits": 1, "hit_rate_pct": 33.3}
+
+
+def test_compile_attaches_a_memory_plan():
+    g = _graph(["x", "W"])
+    _rule(g, "u", ["x", "W"], "matmul", trans_b=True)
+    _rule(g, "v", ["u"], "gelu")
+    plan = C.compile(g, C.CompilerConfig(training=False))
+    assert plan.memory_plan is not None and plan.pool is not None
+    assert set(plan.memory_plan.order) == {"x", "W", "v"}
