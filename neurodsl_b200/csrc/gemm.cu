@@ -1085,10 +1085,24 @@ cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  // Widest tile that still gives every SM at least one tile.
+  // Tile width: fewest waves of tiles over the SMs, a wave of 128- or 64-wide
+  // tiles counting half or a quarter of a 256-wide one, with a penalty for
+  // the narrower tiles (each A tile is reused over fewer columns); ties keep
+  // the wider tile.  M = 8192, N = 768 takes 128 (384 tiles in 3 waves of
+  // half-width tiles instead of 192 tiles in 2 full-width waves).
   const int m_tiles = (M + kBM - 1) / kBM;
   int BN = 256;
-  while (BN > 64 && static_cast<long long>(m_tiles) * ((N + BN - 1) / BN) < sms) BN >>= 1;
+  double best_cost = 0.0;
+  for (int bn = 256; bn >= 64; bn >>= 1) {
+    const long long tiles = static_cast<long long>(m_tiles) * ((N + bn - 1) / bn);
+    const long long waves = (tiles + sms - 1) / sms;
+    const double penalty = bn == 256 ? 1.0 : (bn == 128 ? 1.1 : 1.25);
+    const double cost = static_cast<double>(waves) * (bn / 256.0) * penalty;
+    if (bn == 256 || cost < best_cost * 0.999) {
+      best_cost = cost;
+      BN = bn;
+    }
+  }
   CUtensorMap ta, tw;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
