@@ -47,6 +47,7 @@
  *   nd_argmax           the greedy argmax over LM-head logits (:matmul trans_b
  *                       src/dispatch.jl:213-243 feeds it)
  *   nd_kv_store         no reference counterpart (prefill fills the decode cache)
+ *   nd_gemm_qkv_cache   the QKV :linear (src/dispatch.jl:363-384) with that cache fill
  *   nd_add_layernorm    residual :add src/dispatch.jl:386-417 + :layernorm
  *   nd_comm_*, nd_allreduce_add_layernorm  no reference counterpart (multi-GPU
  *                       tensor-parallel reduction fused with :add + :layernorm)
@@ -217,6 +218,18 @@ int nd_kv_append(void *stream, const void *k_new, const void *v_new, void *k_cac
 int nd_gemm_bias_act(void *stream, const void *A, const void *W, const float *bias,
                      const void *residual, int residual_dtype, void *Y, int y_dtype, int M, int N,
                      int K, int act);
+
+/*
+ * The QKV projection of a prefill, filling the decode caches in the same
+ * launch: Y[M][3*H*64] = A[M][K] · W[3*H*64][K]ᵀ + bias (bf16 Y, as
+ * nd_gemm_bias_act), and the K and V column blocks of row m (token
+ * s = m % S of sequence b = m / S, M = B*S) also go to position pos0 + s of
+ * k_cache, v_cache [B][H][L_max][64] bf16 — what nd_kv_store would copy
+ * afterwards, without reading the projection back.
+ */
+int nd_gemm_qkv_cache(void *stream, const void *A, const void *W, const float *bias, void *Y,
+                      int M, int K, void *k_cache, void *v_cache, int B, int S, int H, int L_max,
+                      int pos0);
 
 /*
  * Few-row linear layer with the residual add and LayerNorm in its prologue

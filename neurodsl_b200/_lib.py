@@ -55,6 +55,7 @@ SIGNATURES = {
     "nd_set_pdl": (_i, [_i, ctypes.POINTER(_i)]),
     "nd_kv_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
+    "nd_gemm_qkv_cache": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_ln_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gelu": (_i, [_vp, _vp, _vp, ctypes.c_int64, _i]),
     "nd_scale_mask": (_i, [_vp, _vp, _vp, _i, _i, _i]),

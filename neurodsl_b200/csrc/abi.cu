@@ -490,6 +490,61 @@ __attribute__((visibility("default"))) int nd_gemm_bias_act(void* stream, const 
   return ok();
 }
 
+// QKV projection of a prefill that also fills the decode caches.
+__attribute__((visibility("default"))) int nd_gemm_qkv_cache(
+    void* stream, const void* A, const void* W, const float* bias, void* Y, int M, int K,
+    void* k_cache, void* v_cache, int B, int S, int H, int L_max, int pos0) {
+  if (M < 0 || K < 0 || B < 0 || S < 0 || H < 0 || pos0 < 0)
+    return fail(ND_ERR_INVALID_ARG, "nd_gemm_qkv_cache: negative size");
+  if (static_cast<long long>(B) * S != M)
+    return fail(ND_ERR_SHAPE, "nd_gemm_qkv_cache: M = %d rows but B*S = %lld", M,
+                static_cast<long long>(B) * S);
+  if (pos0 + S > L_max)
+    return fail(ND_ERR_SHAPE, "nd_gemm_qkv_cache: positions [%d, %d) exceed L_max %d", pos0,
+                pos0 + S, L_max);
+  if (M == 0 || H == 0) return ok();
+  if (K == 0 || K % 8) return fail(ND_ERR_SHAPE, "nd_gemm_qkv_cache: K = %d must be a positive multiple of 8", K);
+  if (!A || !W || !Y || !k_cache || !v_cache)
+    return fail(ND_ERR_INVALID_ARG, "nd_gemm_qkv_cache: null tensor pointer");
+  if (!aligned16(A) || !aligned16(W) || !aligned16(Y) || !aligned16(k_cache) ||
+      !aligned16(v_cache))
+    return fail(ND_ERR_ALIGNMENT, "nd_gemm_qkv_cache: tensors must be 16-byte aligned");
+  if (static_cast<long long>(B) * H > 65535)
+    return fail(ND_ERR_SHAPE, "nd_gemm_qkv_cache: B*H exceeds 65535");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  const int dl = H * 64, N = 3 * dl;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const char* msg = nullptr;
+  auto* kc = static_cast<__nv_bfloat16*>(k_cache);
+  auto* vc = static_cast<__nv_bfloat16*>(v_cache);
+  cudaError_t e;
+  if (M > 32 && aligned16(bias)) {
+    // the tensor-core path's bf16 staged epilogue writes the cache rows too
+    nd::KvOut kv;
+    kv.k = kc;
+    kv.v = vc;
+    kv.S = S;
+    kv.H = H;
+    kv.L_max = L_max;
+    kv.pos0 = pos0;
+    kv.dl = dl;
+    e = nd::launch_gemm(st, static_cast<const __nv_bfloat16*>(A),
+                        static_cast<const __nv_bfloat16*>(W), bias, nullptr, false, Y, false, M,
+                        N, K, ND_ACT_NONE, &msg, kv);
+  } else {
+    // few rows (the weight-streaming path) or an unaligned bias: GEMM, then copy
+    e = nd::launch_gemm(st, static_cast<const __nv_bfloat16*>(A),
+                        static_cast<const __nv_bfloat16*>(W), bias, nullptr, false, Y, false, M,
+                        N, K, ND_ACT_NONE, &msg);
+    if (e == cudaSuccess)
+      e = nd::launch_kv_store(st, static_cast<const __nv_bfloat16*>(Y), N, dl, 2 * dl, kc, vc, B,
+                              S, H, L_max, pos0);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "nd_gemm_qkv_cache", msg);
+  return ok();
+}
+
 // Few-row linear layer with the residual add and LayerNorm in its prologue.
 __attribute__((visibility("default"))) int nd_ln_gemm(void* stream, const void* x, const void* p,
                                                       const float* p_bias, const float* gamma,

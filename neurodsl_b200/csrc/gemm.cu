@@ -222,11 +222,12 @@ __device__ __forceinline__ void store_chunk(const uint32_t (&r)[32], const uint6
 // buffer, so that each store instruction writes 8 whole 64-byte row segments
 // (16 full sectors) instead of 32 half sectors.  Needs the 16-byte path
 // (vec, col0 + 32 <= N).
-template <int kAct>
+template <int kAct, bool kKv>
 __device__ __forceinline__ void store_chunk_staged(const uint32_t (&r)[32], uint32_t bias_s,
                                                    bool has_bias, uint32_t stg,
                                                    __nv_bfloat16* __restrict__ Y, int m_base,
-                                                   int lane, int M, int col0, int N) {
+                                                   int lane, int M, int col0, int N,
+                                                   const KvOut& kv) {
   uint64_t z[16];
 #pragma unroll
   for (int q = 0; q < 16; ++q) z[q] = f2_pack(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
@@ -270,8 +271,21 @@ __device__ __forceinline__ void store_chunk_staged(const uint32_t (&r)[32], uint
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                  : "r"(stg + row * kStagePitch + piece * 16));
     const int m = m_base + row;
-    if (m < M)
+    if (m < M) {
       *reinterpret_cast<uint4*>(Y + static_cast<size_t>(m) * N + col0 + piece * 8) = v;
+      if (kKv && col0 >= kv.dl) {
+        // a K or V column block: the same 16 bytes into the head-major cache
+        // at token (b, s) = (m / S, m % S), head and dims of the column
+        const int c = col0 - kv.dl;
+        const int is_v = c >= kv.dl ? 1 : 0;
+        const int hc = c - is_v * kv.dl;
+        const int b = m / kv.S, s = m - b * kv.S;
+        const size_t idx =
+            (static_cast<size_t>(b * kv.H + (hc >> 6)) * kv.L_max + kv.pos0 + s) * 64 + (hc & 63) +
+            piece * 8;
+        *reinterpret_cast<uint4*>((is_v ? kv.v : kv.k) + idx) = v;
+      }
+    }
   }
   __syncwarp();  // the buffer is rewritten by the next chunk
 }
@@ -290,12 +304,12 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   n_blk = r / rows;
 }
 
-template <int BN, bool kOutF32, int kAct, bool kRes>
+template <int BN, bool kOutF32, int kAct, bool kRes, bool kKv>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_w,
                 const float* __restrict__ bias, const void* __restrict__ residual,
                 int residual_f32, void* __restrict__ Y, int M, int N, int K, int vec,
-                int* __restrict__ err_word) {
+                int* __restrict__ err_word, KvOut kv) {
   using Cfg = GemmCfg<BN>;
   constexpr int kStages = Cfg::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -485,9 +499,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           {                                                                               \
             if (c + 2 < n_chunks) tmem_ld32(acc + (c + 2) * 32, r[NXT]);                  \
             if (!kOutF32 && vec && col0 + 32 <= N)                                        \
-              store_chunk_staged<kAct>(r[CUR], wbias + k * 128, bias != nullptr, stg,     \
+              store_chunk_staged<kAct, kKv>(r[CUR], wbias + k * 128, bias != nullptr, stg, \
                                        static_cast<__nv_bfloat16*>(Y), m_base, lane, M,   \
-                                       col0, N);                                          \
+                                       col0, N, kv);                                      \
             else                                                                          \
               store_chunk<kOutF32, kAct, false>(r[CUR], no_res, bias, residual, residual_f32, \
                                                 Y, m, M, col0, N, vec);                   \
@@ -511,12 +525,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool kOutF32, int kAct, bool kRes>
+template <int BN, bool kOutF32, int kAct, bool kRes, bool kKv = false>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tw,
                          const float* bias, const void* residual, bool residual_f32, void* Y,
-                         int M, int N, int K, int sms) {
+                         int M, int N, int K, int sms, const KvOut& kv) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_kernel<BN, kOutF32, kAct, kRes>;
+  auto kern = gemm_kernel<BN, kOutF32, kAct, kRes, kKv>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -525,43 +539,46 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& ta, const CUten
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const int vec = (N % 8 == 0) && al16(Y) && al16(residual) && al16(bias) ? 1 : 0;
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tw, bias, residual, residual_f32 ? 1 : 0,
-                                                    Y, M, N, K, vec, device_error_word());
+                                                    Y, M, N, K, vec, device_error_word(), kv);
   return cudaGetLastError();
 }
 
 template <int BN, bool kOutF32>
 cudaError_t launch_act(int act, cudaStream_t stream, const CUtensorMap& ta, const CUtensorMap& tw,
                        const float* bias, const void* residual, bool residual_f32, void* Y, int M,
-                       int N, int K, int sms) {
+                       int N, int K, int sms, const KvOut& kv) {
   switch (act) {
     case ND_ACT_GELU_SIGMOID:
       return residual != nullptr
-                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
-                 : launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv)
+                 : launch_typed<BN, kOutF32, ND_ACT_GELU_SIGMOID, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
     case ND_ACT_GELU_TANH:
       return residual != nullptr
-                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_TANH, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
-                 : launch_typed<BN, kOutF32, ND_ACT_GELU_TANH, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_TANH, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv)
+                 : launch_typed<BN, kOutF32, ND_ACT_GELU_TANH, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
     case ND_ACT_GELU_ERF:
       return residual != nullptr
-                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_ERF, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
-                 : launch_typed<BN, kOutF32, ND_ACT_GELU_ERF, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+                 ? launch_typed<BN, kOutF32, ND_ACT_GELU_ERF, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv)
+                 : launch_typed<BN, kOutF32, ND_ACT_GELU_ERF, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
     default:
-      return residual != nullptr
-                 ? launch_typed<BN, kOutF32, ND_ACT_NONE, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
-                 : launch_typed<BN, kOutF32, ND_ACT_NONE, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+      if (residual != nullptr)
+        return launch_typed<BN, kOutF32, ND_ACT_NONE, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
+      if constexpr (!kOutF32)
+        if (kv.k != nullptr)  // the QKV projection that also fills the caches
+          return launch_typed<BN, false, ND_ACT_NONE, false, true>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
+      return launch_typed<BN, kOutF32, ND_ACT_NONE, false>(stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
   }
 }
 
 template <bool kOutF32>
 cudaError_t launch_bn(int BN, int act, cudaStream_t stream, const CUtensorMap& ta,
                       const CUtensorMap& tw, const float* bias, const void* residual,
-                      bool residual_f32, void* Y, int M, int N, int K, int sms) {
+                      bool residual_f32, void* Y, int M, int N, int K, int sms, const KvOut& kv) {
   if (BN == 256)
-    return launch_act<256, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+    return launch_act<256, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
   if (BN == 128)
-    return launch_act<128, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
-  return launch_act<64, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+    return launch_act<128, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
+  return launch_act<64, kOutF32>(act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
 }
 
 // ---- skinny path: M <= 32 rows (decode-time activations) -------------------
@@ -1069,7 +1086,8 @@ cudaError_t launch_ln_gemm_mb(int act, cudaStream_t stream, const __nv_bfloat16*
 
 cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_bfloat16* W,
                         const float* bias, const void* residual, bool residual_f32, void* Y,
-                        bool out_f32, int M, int N, int K, int act, const char** err_msg) {
+                        bool out_f32, int M, int N, int K, int act, const char** err_msg,
+                        const KvOut& kv) {
   if (M == 0 || N == 0) return cudaSuccess;
   if (K == 0) return cudaErrorInvalidValue;
   if (M <= 32 && K % 32 == 0) {
@@ -1118,8 +1136,8 @@ cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_
     e = make_tmap_bf16_sw128(&tw, W, 2, dims, strides, box, err_msg);
     if (e != cudaSuccess) return e;
   }
-  return out_f32 ? launch_bn<true>(BN, act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms)
-                 : launch_bn<false>(BN, act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms);
+  return out_f32 ? launch_bn<true>(BN, act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv)
+                 : launch_bn<false>(BN, act, stream, ta, tw, bias, residual, residual_f32, Y, M, N, K, sms, kv);
 }
 
 cudaError_t launch_ln_gemm(cudaStream_t stream, const __nv_bfloat16* x, const __nv_bfloat16* p,

@@ -16,7 +16,8 @@ in libneurodsl_b200.so:
                         (nd_ln_gemm)
   QKV / out / MLP       nd_gemm_bias_act (bias and GELU in the epilogue)
   prefill attention     nd_flash_attn_fwd_strided on the fused QKV projection
-                        (no per-head copies), K/V into the caches by nd_kv_store
+                        (no per-head copies); the projection's epilogue also
+                        writes K/V into the caches (nd_gemm_qkv_cache)
   decode attention      nd_kv_decode_attn_qkv straight from the fused QKV
                         projection, the new token appended in place
   greedy token          nd_argmax on the LM-head logits
@@ -225,8 +226,8 @@ class GPT:
         parts = b["qkv"].view(B, S, 3, H, 64).permute(2, 0, 3, 1, 4)   # [3][B][H][S][64]
         o4 = b["attn"].view(B, S, H, 64).permute(0, 2, 1, 3)
         for i, L in enumerate(self.layers):
-            ops.linear(h, L["w_qkv"], L["b_qkv"], out=b["qkv"])
-            ops.kv_store(b["qkv"], dl, 2 * dl, self.k_cache[i], self.v_cache[i], B, S, 0)
+            ops.linear_qkv_cache(h, L["w_qkv"], L["b_qkv"], b["qkv"], self.k_cache[i],
+                                 self.v_cache[i], B, S)
             ops.flash_attn_fwd(parts[0], parts[1], parts[2], causal=True, out=o4)
             ops.linear(b["attn"], L["w_o"], out=b["part"])
             self._all_reduce(b["part"])

@@ -223,6 +223,29 @@ def linear(A, W, bias=None, residual=None, act="none", out=None, out_dtype=torch
     return out
 
 
+def linear_qkv_cache(A, W, bias, out, k_cache, v_cache, B, S, pos0=0, stream=None):
+    """The QKV projection out = A·Wᵀ + bias (A [B*S][K], W [3*H*64][K], bf16
+    out) that also writes its K and V column blocks into the head-major
+    caches [B][H][L_max][64] at positions pos0.. (nd_gemm_qkv_cache)."""
+    _need(A, "A", torch.bfloat16, 2)
+    _need(W, "W", torch.bfloat16, 2)
+    _need(out, "out", torch.bfloat16, 2)
+    _need(k_cache, "k_cache", torch.bfloat16, 4)
+    _need(v_cache, "v_cache", torch.bfloat16, 4)
+    M, K = A.shape
+    _, H, L_max, D = k_cache.shape
+    if D != 64 or W.shape != (3 * H * 64, K) or tuple(out.shape) != (M, 3 * H * 64):
+        raise ValueError("QKV projection / cache shape mismatch")
+    if v_cache.shape != k_cache.shape or k_cache.shape[0] != B:
+        raise ValueError("cache shape mismatch")
+    if bias is not None:
+        _need(bias, "bias", torch.float32)
+    check(_lib.load().nd_gemm_qkv_cache(_stream(stream), _ptr(A), _ptr(W), _ptr(bias), _ptr(out),
+                                        M, K, _ptr(k_cache), _ptr(v_cache), int(B), int(S), H,
+                                        L_max, int(pos0)))
+    return out
+
+
 def ln_linear(x, W, p=None, p_bias=None, gamma=None, beta=None, eps=1e-5, s_out=None, bias=None,
               act="none", out=None, out_dtype=torch.bfloat16, stream=None):
     """Y = act(LayerNorm(x + p + p_bias)·Wᵀ + bias) for at most 32 rows, with

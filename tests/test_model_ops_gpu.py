@@ -119,3 +119,30 @@ def test_add_layernorm_rejects_bad_width():
     x = torch.zeros((4, 12), device="cuda", dtype=torch.bfloat16)
     with pytest.raises(NeuroDSLError):
         ops.add_layernorm(x, x)
+
+
+@pytest.mark.parametrize("B,S,H,K,pos0,bias_off", [(2, 100, 3, 192, 0, 0), (3, 77, 2, 128, 5, 0),
+                                                    (2, 9, 3, 192, 0, 0), (2, 100, 3, 192, 0, 1)])
+def test_qkv_projection_fills_the_caches(B, S, H, K, pos0, bias_off):
+    """nd_gemm_qkv_cache gives the projection and cache rows of
+    nd_gemm_bias_act followed by nd_kv_store, bit for bit: the tensor-core
+    epilogue path (M > 32), the few-row path (M = 18) and an unaligned bias
+    (which takes the two-launch form)."""
+    ops = _ops()
+    gen = torch.Generator(device="cuda").manual_seed(B * S + K)
+    bf = torch.bfloat16
+    M, N, L_max = B * S, 3 * H * 64, S + pos0 + 3
+    A = torch.randn(M, K, device="cuda", generator=gen).to(bf)
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=gen)).to(bf)
+    bias = torch.randn(N + bias_off, device="cuda", generator=gen)[bias_off:]
+    kc0 = torch.randn(B, H, L_max, 64, device="cuda", generator=gen).to(bf)
+    vc0 = torch.randn(B, H, L_max, 64, device="cuda", generator=gen).to(bf)
+    y_ref = ops.linear(A, W, bias)
+    kc_ref, vc_ref = kc0.clone(), vc0.clone()
+    ops.kv_store(y_ref, H * 64, 2 * H * 64, kc_ref, vc_ref, B, S, pos0)
+    y = torch.empty_like(y_ref)
+    kc, vc = kc0.clone(), vc0.clone()
+    ops.linear_qkv_cache(A, W, bias, y, kc, vc, B, S, pos0)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    assert torch.equal(kc, kc_ref) and torch.equal(vc, vc_ref)
