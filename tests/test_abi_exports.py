@@ -105,3 +105,31 @@ def test_missing_library_raises(tmp_path):
             _lib.load(str(tmp_path / "nope.so"))
         finally:
             _lib._lib = old
+
+
+def test_empty_inputs_are_accepted_without_a_device():
+    """Zero-size shapes (an empty batch, no rows, no tokens) return ND_OK
+    before any pointer is touched or the device is queried, so a caller's
+    ragged batch that happens to be empty needs no special case."""
+    from neurodsl_b200 import _lib
+    lib = _lib.load()
+    N = None
+    calls = {
+        "nd_flash_attn_fwd": lambda: lib.nd_flash_attn_fwd(N, N, N, N, N, 0, N, N, 0, 4, 128, 128,
+                                                           64, 0.125, 1),
+        "nd_kv_decode_attn": lambda: lib.nd_kv_decode_attn(N, N, N, N, N, N, N, 0, N, 0, 4, 5, 8,
+                                                           64, 0.125, N, 0),
+        "nd_kv_decode_attn_qkv": lambda: lib.nd_kv_decode_attn_qkv(N, N, 0, N, N, N, 0, N, 0, 4,
+                                                                   5, 8, 64, 0.125, N, 0),
+        "nd_gemm_bias_act": lambda: lib.nd_gemm_bias_act(N, N, N, N, N, 0, N, 0, 0, 64, 64, 0),
+        "nd_gemm_qkv_cache": lambda: lib.nd_gemm_qkv_cache(N, N, N, N, N, 0, 64, N, N, 0, 7, 2,
+                                                           16, 0),
+        "nd_ln_gemm": lambda: lib.nd_ln_gemm(N, N, N, N, N, N, 1e-5, N, N, N, N, 1, 0, 64, 64, 0),
+        "nd_layernorm": lambda: lib.nd_layernorm(N, N, 0, N, N, N, 0, N, N, 0, 64, 1e-5),
+        "nd_add_layernorm": lambda: lib.nd_add_layernorm(N, N, N, 1, N, N, N, N, N, 0, 64, 1e-5),
+        "nd_softmax": lambda: lib.nd_softmax(N, N, N, 0, 16),
+        "nd_scale_mask": lambda: lib.nd_scale_mask(N, N, N, 0, 16, 64),
+        "nd_argmax": lambda: lib.nd_argmax(N, N, 0, 64, 0, 64, N, N),
+    }
+    for name, call in calls.items():
+        assert call() == _lib.ND_OK, (name, lib.nd_last_error_string())
