@@ -7,7 +7,7 @@
  * checker or the timed CPU baseline, never as a product code path.
  *
  * Parity status: UNPINNED against reference outputs.  The reference is Julia
- * (not installed here or on the GPU box) and its test suite holds no golden
+ * (no Julia toolchain is installed where this builds or runs) and its test suite holds no golden
  * vectors; its only equivalence test for this path compares its tiled and
  * simple CPU attention with each other (test/test_runtime_optimizations.jl:55-69).
  * The same equivalence is re-asserted against this restatement in
