@@ -34,6 +34,7 @@
  *                       cell 15 (rule name src/compiler_config.jl:154-158)
  *   nd_ln_gemm          residual :add src/dispatch.jl:386-417 + :layernorm +
  *                       :linear :363-384 for a decode step's few rows
+ *   nd_add              :add with its vector broadcasts, src/dispatch.jl:386-417
  *   nd_gelu, nd_scale_mask, nd_softmax  the unfused :gelu (notebook/compiler.ipynb
  *                       cell 15 form), :scale_mask src/dispatch.jl:464-474 and
  *                       :softmax src/kernels.jl:269-287 ops
@@ -258,6 +259,14 @@ int nd_ln_gemm(void *stream, const void *x, const void *p, const float *p_bias,
 int nd_gelu(void *stream, const float *x, float *y, int64_t n, int act);
 int nd_scale_mask(void *stream, const float *x, float *y, int rows, int cols, int d_head);
 int nd_softmax(void *stream, const float *x, float *y, int rows, int cols);
+
+/*
+ * The residual :add of the operator graph, fp32: y = a + b over
+ * [rows][cols], with b the same shape (b_mode 0), one value per column
+ * (b_mode 1, length cols) or one per row (b_mode 2, length rows) — the
+ * reference's matrix + vector broadcasts.
+ */
+int nd_add(void *stream, const float *a, const float *b, float *y, int rows, int cols, int b_mode);
 
 /*
  * LayerNorm over the last dimension of x [rows][d]:

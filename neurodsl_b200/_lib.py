@@ -60,6 +60,7 @@ SIGNATURES = {
     "nd_gelu": (_i, [_vp, _vp, _vp, ctypes.c_int64, _i]),
     "nd_scale_mask": (_i, [_vp, _vp, _vp, _i, _i, _i]),
     "nd_softmax": (_i, [_vp, _vp, _vp, _i, _i]),
+    "nd_add": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i]),
     "nd_layernorm": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _f]),
     "nd_convert_2d": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i]),
     "nd_embed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),

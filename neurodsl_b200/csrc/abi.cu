@@ -616,6 +616,19 @@ __attribute__((visibility("default"))) int nd_scale_mask(void* stream, const flo
   return ok();
 }
 
+__attribute__((visibility("default"))) int nd_add(void* stream, const float* a, const float* b,
+                                                  float* y, int rows, int cols, int b_mode) {
+  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_add: negative size");
+  if (b_mode < 0 || b_mode > 2) return fail(ND_ERR_INVALID_ARG, "nd_add: b_mode %d", b_mode);
+  if (static_cast<long long>(rows) * cols == 0) return ok();
+  if (!a || !b || !y) return fail(ND_ERR_INVALID_ARG, "nd_add: null pointer");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_add(static_cast<cudaStream_t>(stream), a, b, y, rows, cols, b_mode);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_add");
+  return ok();
+}
+
 __attribute__((visibility("default"))) int nd_softmax(void* stream, const float* x, float* y,
                                                       int rows, int cols) {
   if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_softmax: negative size");

@@ -1,4 +1,5 @@
-// elementwise.cu — the unfused graph ops that rewrite rules fuse away:
+// elementwise.cu — the unfused graph ops (those rewrite rules fuse away, and
+// the residual :add):
 //   gelu_kernel        y = GELU(x) elementwise (the :gelu op; sigmoid, tanh or
 //                      erf form, the same forms as the GEMM epilogue)
 //   scale_mask_kernel  y = x / sqrt(d_head) + causal mask (the :scale_mask op,
@@ -6,6 +7,8 @@
 //                      causal_mask, src/kernels.jl:425-430: -Inf above the
 //                      diagonal of each [rows][cols] score block)
 //   softmax_kernel     row softmax (the :softmax op, src/kernels.jl:269-287)
+//   add_kernel         the :add op with its vector broadcasts
+//                      (src/dispatch.jl:386-417)
 // fp32 rows in and out (the graph's Float32 node values).  HBM-bound; a warp
 // per row for the softmax with 16-byte loads where the row allows.
 #include <cuda_bf16.h>
@@ -41,6 +44,19 @@ __global__ void scale_mask_kernel(const float* __restrict__ x, float* __restrict
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int r = static_cast<int>(i / cols), c = static_cast<int>(i - static_cast<long long>(r) * cols);
     y[i] = c > r ? -INFINITY : x[i] * scale;
+  }
+}
+
+// y = a + b over [rows][cols] fp32; b is the same shape (mode 0), one value
+// per column (mode 1) or one per row (mode 2): the :add op with its bias
+// broadcasts (src/dispatch.jl:386-417).
+__global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                           float* __restrict__ y, int rows, int cols, int mode) {
+  const long long n = static_cast<long long>(rows) * cols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long bi = mode == 0 ? i : (mode == 1 ? i % cols : i / cols);
+    y[i] = a[i] + b[bi];
   }
 }
 
@@ -94,6 +110,14 @@ cudaError_t launch_scale_mask(cudaStream_t stream, const float* x, float* y, int
   const long long n = static_cast<long long>(rows) * cols;
   if (n == 0) return cudaSuccess;
   scale_mask_kernel<<<grid_for(n, 256), 256, 0, stream>>>(x, y, rows, cols, scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_add(cudaStream_t stream, const float* a, const float* b, float* y, int rows,
+                       int cols, int mode) {
+  const long long n = static_cast<long long>(rows) * cols;
+  if (n == 0) return cudaSuccess;
+  add_kernel<<<grid_for(n, 256), 256, 0, stream>>>(a, b, y, rows, cols, mode);
   return cudaGetLastError();
 }
 

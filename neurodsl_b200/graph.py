@@ -246,7 +246,10 @@ def _infer_output_shape(op: str, inputs, attrs):
         return (inputs[0].shape[0], attrs["end_col"] - attrs["start_col"] + 1)
     if op == "flash_attention" and len(inputs) == 1:
         return (inputs[0].shape[0], inputs[0].shape[1] // 3)   # fused (S, 3d) projection
-    if op in ("add", "identity", "flash_attn", "flash_attention", "layernorm", "gelu",
+    if op == "add":
+        a, b = inputs[0], inputs[1]
+        return tuple(b.shape) if (a.dim() == 1 and b.dim() == 2) else tuple(a.shape)
+    if op in ("identity", "flash_attn", "flash_attention", "layernorm", "gelu",
               "scale_mask", "softmax"):
         return tuple(inputs[0].shape)
     if op == "kv_decode_attn":
@@ -557,8 +560,13 @@ def _dispatch_layernorm(dev, output_buffer, inputs, attrs, out_sym, out_node, ct
 
 
 def _dispatch_add(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
-    """:add residual (src/dispatch.jl:386-417) as a graph-glue device op."""
-    torch.add(inputs[0], inputs[1], out=output_buffer)
+    """:add (src/dispatch.jl:386-417): same shapes, or a matrix and a vector
+    broadcast per column (preferred when the lengths match, as in the
+    reference) or per row, in either operand order (nd_add)."""
+    a, b = _f32(inputs[0]), _f32(inputs[1])
+    if a.dim() == 1 and b.dim() == 2:
+        a, b = b, a
+    ops.add(a, b, out=output_buffer)
     return output_buffer
 
 

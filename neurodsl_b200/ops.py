@@ -301,6 +301,27 @@ def scale_mask(scores, d_head, out=None, stream=None):
     return out
 
 
+def add(a, b, out=None, stream=None):
+    """a + b for float32 tensors (nd_add, the :add op): b of a's shape, or a
+    vector of one value per column or per row of a 2-D a."""
+    _need(a, "a", torch.float32)
+    _need(b, "b", torch.float32)
+    rows, cols = (a.shape[0], a.shape[1]) if a.dim() == 2 else (1, a.numel())
+    if tuple(b.shape) == tuple(a.shape):
+        mode = 0
+    elif a.dim() == 2 and b.dim() == 1 and b.numel() == cols:
+        mode = 1
+    elif a.dim() == 2 and b.dim() == 1 and b.numel() == rows:
+        mode = 2
+    else:
+        raise ValueError(f"add: shapes {tuple(a.shape)} and {tuple(b.shape)} do not broadcast")
+    if out is None:
+        out = torch.empty_like(a)
+    _need(out, "out", torch.float32)
+    check(_lib.load().nd_add(_stream(stream), _ptr(a), _ptr(b), _ptr(out), rows, cols, mode))
+    return out
+
+
 def softmax(x, out=None, stream=None):
     """Row softmax of a float32 [rows][cols] matrix (nd_softmax, the :softmax op)."""
     _need(x, "x", torch.float32, 2)

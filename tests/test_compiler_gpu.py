@@ -192,3 +192,34 @@ def test_pooled_plan_reuses_buffers_and_matches_demand():
     # the intermediates' buffers come back from the pool; the kept output's
     # own buffer is reused in place
     assert st2["allocs"] == st["allocs"] and st2["hits"] == st["hits"] + len(computed)
+
+
+def test_add_op_broadcasts_like_the_reference():
+    """:add on the library kernel: same shapes, a vector per column
+    (preferred when both lengths match), a vector per row, and the vector
+    first — each the fp32 sums NumPy gives, bit for bit."""
+    _, G = _mods()
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((6, 9)).astype(np.float32)
+    sq = rng.standard_normal((5, 5)).astype(np.float32)
+    cases = {
+        "same": (a, rng.standard_normal((6, 9)).astype(np.float32)),
+        "per_col": (a, rng.standard_normal(9).astype(np.float32)),
+        "per_row": (a, rng.standard_normal(6).astype(np.float32)),
+        "square_prefers_cols": (sq, rng.standard_normal(5).astype(np.float32)),
+    }
+    for name, (x, y) in cases.items():
+        for first, second in ((x, y), (y, x)):
+            g = G.NeuroGraph()
+            G.set_(g, "p", first)
+            G.set_(g, "q", second)
+            G.addrule(g, G.GraphRule("z", ["p", "q"], "add"))
+            z = G.demand(g, "z").cpu().numpy()
+            m, v = (first, second) if first.ndim == 2 else (second, first)
+            if v.ndim == 1 and v.shape[0] == m.shape[1]:
+                ref = m + v.reshape(1, -1)
+            elif v.ndim == 1:
+                ref = m + v.reshape(-1, 1)
+            else:
+                ref = m + v
+            np.testing.assert_array_equal(z, ref, err_msg=name)
