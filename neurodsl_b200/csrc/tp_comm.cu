@@ -80,9 +80,14 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-template <int kMaxVec>
+// kTP is the rank count: a compile-time count lets every rank's slot load of
+// a row issue before the first one is used (a runtime count leaves each load
+// behind its own branch, so the NVLink reads of a row go out one at a time).
+// `own` is this rank's region (regs.r[rank]), passed on its own so that no
+// dynamic index into the region array puts that array in local memory.
+template <int kMaxVec, int kTP>
 __global__ void __launch_bounds__(256)
-    allreduce_add_ln_kernel(CommRegions regs, int tp, int rank, size_t slot_off,
+    allreduce_add_ln_kernel(CommRegions regs, char* own, int rank, size_t slot_off,
                             const __nv_bfloat16* x, const float* __restrict__ bias,
                             const float* __restrict__ gamma, const float* __restrict__ beta,
                             __nv_bfloat16* s_out, __nv_bfloat16* __restrict__ y, int rows, int d,
@@ -111,33 +116,30 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
-  auto load_x = [&](int row) {
-    const size_t off = static_cast<size_t>(row) * d;
+  pdl_wait();  // x and this rank's partial come from earlier kernels
+  pdl_trigger();
+  if (row0 < rows) {
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + i * 32;
-      if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
+      if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row0) * d)[c];
     }
-  };
-  pdl_wait();  // x and this rank's partial come from earlier kernels
-  pdl_trigger();
-  if (row0 < rows) load_x(row0);
+  }
 
-  char* own = static_cast<char*>(regs.r[rank]);
   if (threadIdx.x == 0) {
     uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
     const uint32_t seq = counters[blockIdx.x] + 1;
     __threadfence_system();  // release: this rank's slot before the flags
 #pragma unroll
-    for (int p = 0; p < kCommMaxRanks; ++p) {
-      if (p >= tp || p == rank) continue;
+    for (int p = 0; p < kTP; ++p) {
+      if (p == rank) continue;
       uint32_t* flags = reinterpret_cast<uint32_t*>(regs.r[p]);
       st_relaxed_sys(flags + rank * kCommMaxCtas + blockIdx.x, seq);
     }
     int ok = 1;
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(own);
     const uint64_t t0 = globaltimer();
-    for (int p = 0; p < tp && ok; ++p) {
+    for (int p = 0; p < kTP && ok; ++p) {
       if (p == rank) continue;
       const uint32_t* f = mine + p * kCommMaxCtas + blockIdx.x;
       uint32_t it = 0;
@@ -157,23 +159,30 @@ __global__ void __launch_bounds__(256)
   if (!s_ok) return;
 
   for (int row = row0; row < rows; row += gridDim.x * warps) {
-    if (row != row0) load_x(row);
     const size_t off = static_cast<size_t>(row) * d;
+    if (row != row0) {
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + i * 32;
+        if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
+      }
+    }
     float v[kMaxVec][8];
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + i * 32;
       if (c < nvec) {
+        // every rank's 16 bytes in flight together, then the partial sums in
+        // rank order, the residual and the bias
+        uint4 pv[kTP];
+#pragma unroll
+        for (int p = 0; p < kTP; ++p)
+          pv[p] = ld_cg16(static_cast<const char*>(regs.r[p]) + slot_off + (off + c * 8) * 2);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
-        // partial sums in rank order, then the residual and the bias
 #pragma unroll
-        for (int p = 0; p < kCommMaxRanks; ++p) {
-          if (p >= tp) break;
-          const char* slot = static_cast<const char*>(regs.r[p]) + slot_off;
-          bf16x8_add(ld_cg16(slot + (off + c * 8) * 2), v[i]);
-        }
+        for (int p = 0; p < kTP; ++p) bf16x8_add(pv[p], v[i]);
         bf16x8_add(xr[i], v[i]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] += bs[i][e];
@@ -212,6 +221,33 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+template <int kMaxVec, int kTP>
+cudaError_t launch_one(dim3 grid, cudaStream_t stream, const CommRegions& regs, int rank,
+                       size_t so, const __nv_bfloat16* x, const float* bias, const float* gamma,
+                       const float* beta, __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d,
+                       float eps, int* err_word) {
+  return launch_ex(allreduce_add_ln_kernel<kMaxVec, kTP>, grid, dim3(256), 0, stream, 1, true,
+                   regs, static_cast<char*>(regs.r[rank]), rank, so, x, bias, gamma, beta, s_out,
+                   y, rows, d, eps, err_word);
+}
+
+template <int kMaxVec>
+cudaError_t launch_tp(int tp, dim3 grid, cudaStream_t stream, const CommRegions& regs, int rank,
+                      size_t so, const __nv_bfloat16* x, const float* bias, const float* gamma,
+                      const float* beta, __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d,
+                      float eps, int* err_word) {
+  switch (tp) {
+#define ND_TP_CASE(n) \
+  case n:             \
+    return launch_one<kMaxVec, n>(grid, stream, regs, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    ND_TP_CASE(1) ND_TP_CASE(2) ND_TP_CASE(3) ND_TP_CASE(4)
+    ND_TP_CASE(5) ND_TP_CASE(6) ND_TP_CASE(7) ND_TP_CASE(8)
+#undef ND_TP_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
 
 size_t comm_region_bytes(int rows_max, int d) {
@@ -236,17 +272,16 @@ cudaError_t launch_allreduce_add_layernorm(cudaStream_t stream, const CommRegion
                                            const float* gamma, const float* beta,
                                            __nv_bfloat16* s_out, __nv_bfloat16* y, int rows,
                                            int d, float eps, int sms, int* err_word) {
+  if (tp < 1 || tp > kCommMaxRanks || rank < 0 || rank >= tp) return cudaErrorInvalidValue;
   const dim3 grid(comm_grid(rows, sms));
   const size_t so = comm_slot_offset(slot, rows_max, d);
   if (d <= 256)
-    return launch_ex(allreduce_add_ln_kernel<1>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    return launch_tp<1>(tp, grid, stream, regs, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   else if (d <= 512)
-    return launch_ex(allreduce_add_ln_kernel<2>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+    return launch_tp<2>(tp, grid, stream, regs, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   else if (d <= 1024)
-    return launch_ex(allreduce_add_ln_kernel<4>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
-  else
-    return launch_ex(allreduce_add_ln_kernel<8>, grid, dim3(256), 0, stream, 1, true, regs, tp, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
-  return cudaGetLastError();
+    return launch_tp<4>(tp, grid, stream, regs, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
+  return launch_tp<8>(tp, grid, stream, regs, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
 }
 
 }  // namespace nd
