@@ -33,15 +33,20 @@ __device__ int g_device_error = 0;
 
 namespace nd {
 int* device_error_word() {
+  // Several host threads may resolve the same device's address at once; they
+  // all obtain the same value, so atomic loads and stores keep the cache
+  // race-free without a lock.
   static int* cached[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (cached[dev] == nullptr) {
+  int* w = __atomic_load_n(&cached[dev], __ATOMIC_ACQUIRE);
+  if (w == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-    cached[dev] = static_cast<int*>(p);
+    w = static_cast<int*>(p);
+    __atomic_store_n(&cached[dev], w, __ATOMIC_RELEASE);
   }
-  return cached[dev];
+  return w;
 }
 namespace {
 thread_local bool t_pdl = false;
