@@ -117,7 +117,32 @@ def test_shape_inference_for_b200_ops():
         assert G._infer_output_shape("no_such_op", [X], {}) == (128, 1024)
 
 
+def test_shape_inference_for_unfused_and_compiled_ops():
+    """The unfused ops keep their input's shape; :add takes the matrix's shape
+    whichever operand the vector is; the compiled LayerNorm + linear takes the
+    weight's output dimension in either orientation; a fused (S, 3d) QKV
+    projection gives (S, d)."""
+    X = torch.zeros(64, 512)
+    for op in ("gelu", "scale_mask", "softmax", "identity"):
+        assert G._infer_output_shape(op, [X], {}) == (64, 512)
+    v = torch.zeros(512)
+    assert G._infer_output_shape("add", [X, v], {}) == (64, 512)
+    assert G._infer_output_shape("add", [v, X], {}) == (64, 512)
+    assert G._infer_output_shape("add", [X, X], {}) == (64, 512)
+    g, b = torch.zeros(512), torch.zeros(512)
+    W = torch.zeros(384, 512)
+    assert G._infer_output_shape("fused_layernorm_linear", [X, g, b, W],
+                                 {"trans_b": True}) == (64, 384)
+    assert G._infer_output_shape("fused_layernorm_linear", [X, g, b, W.T], {}) == (64, 384)
+    assert G._infer_output_shape("flash_attention", [torch.zeros(128, 3 * 512)],
+                                 {"n_heads": 8}) == (128, 512)
+    assert G._infer_output_shape("slice_cols", [X], {"start_col": 65, "end_col": 128}) == (64, 64)
+    assert G._infer_output_shape("matmul", [X, W], {"trans_b": True}) == (64, 384)
+    assert G._infer_output_shape("matmul", [X, W.T], {}) == (64, 384)
+
+
 def test_b200_ops_registered():
     for op in ("flash_attn", "flash_attention", "kv_decode_attn", "fused_linear_gelu",
-               "fused_linear_residual", "layernorm"):
+               "fused_linear_residual", "layernorm", "add", "gelu", "scale_mask", "softmax",
+               "fused_layernorm_linear"):
         assert op in G.CUSTOM_OPS
