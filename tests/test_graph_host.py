@@ -146,3 +146,23 @@ def test_b200_ops_registered():
                "fused_linear_residual", "layernorm", "add", "gelu", "scale_mask", "softmax",
                "fused_layernorm_linear"):
         assert op in G.CUSTOM_OPS
+
+
+def test_aliased_output_goes_through_a_kept_side_buffer():
+    """An output buffer that is also an input (the buffer pool can hand out
+    such a pair) is redirected to aux_data[:_alias_buf], kept for the next
+    call of the same shape and dtype and replaced when either changes
+    (src/dispatch.jl:220-231)."""
+    node = G.GraphNode("y", None)
+    x = torch.zeros(4, 8)
+    other = torch.zeros(4, 8)
+    buf, aliased = G._alias_safe(other, node, [x])
+    assert buf is other and not aliased and "_alias_buf" not in node.aux_data
+    buf, aliased = G._alias_safe(x, node, [x, other])
+    assert aliased and buf is not x and buf.shape == x.shape
+    assert buf.data_ptr() != x.data_ptr()
+    again, _ = G._alias_safe(x, node, [x])
+    assert again is buf                                   # reused
+    xb = torch.zeros(4, 8, dtype=torch.bfloat16)
+    third, aliased = G._alias_safe(xb, node, [xb])
+    assert aliased and third is not buf and third.dtype == torch.bfloat16
