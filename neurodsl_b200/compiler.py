@@ -11,6 +11,10 @@ rules that map unfused transformer graphs onto the B200 fused operators.
   scan_graph  src/compiler_rules.jl:575-623       scan_graph
   _apply_fusion!  src/compiler.jl:16-66           _apply_fusion
   compile  src/compiler.jl:70-124                 compile -> CompiledPlan
+  dirty tracking / recompile!  src/compiler.jl:126-191
+                                                  _register_dirty_tracking,
+                                                  is_dirty, recompile
+  plan(g, out)  src/compiler.jl:204-240           CompiledPlan.__call__
   _flash_condition  src/compiler_config.jl:107    _flash_condition
   memory plan + BufferPool (liveness.jl)          neurodsl_b200/liveness.py
 
@@ -31,8 +35,9 @@ chain and the namespace like the reference's.
 """
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass, field
-from typing import Any, Callable, Dict, List, Optional, Tuple
+from typing import Any, Callable, Dict, List, Optional, Set, Tuple
 
 from . import graph as G
 from . import liveness as L
@@ -146,16 +151,27 @@ class CompiledPlan:
     config: CompilerConfig
     memory_plan: Optional[L.MemoryPlan] = None
     pool: Optional[L.BufferPool] = None
+    dirty_nodes: Set[str] = field(default_factory=set)
+    n_recompiles: int = 0
+    compiled_at: float = 0.0
+
+    def is_dirty(self) -> bool:
+        return bool(self.dirty_nodes)
 
     def __call__(self, g, output_sym, ctx_store=None):
         """Run the compiled graph up to `output_sym` (the reference's
-        plan(g, output_sym), src/compiler.jl:204): with the buffer pool, every
-        intermediate's buffer returns to the pool when its liveness interval
-        ends and later nodes reuse it (a CtxStore then holds buffers that later
-        nodes overwrite: keep it for unpooled runs)."""
+        plan(g, output_sym), src/compiler.jl:204-240), recompiling first when
+        a set_ since the last compilation invalidated one of its nodes.  With
+        the buffer pool, every intermediate's buffer returns to the pool when
+        its liveness interval ends and later nodes reuse it — except, with
+        `training=True`, a backpropagable (Quantom) node, whose forward value
+        a backward pass needs (a CtxStore holds buffers that later nodes
+        overwrite: keep it for unpooled runs)."""
+        if self.is_dirty():
+            recompile(self, g)
         if self.config.pooled and self.memory_plan is not None:
             return L.run_planned(g, self.memory_plan, self.pool, output_sym, self.namespace,
-                                 ctx_store)
+                                 ctx_store, training=self.config.training)
         return G.demand(g, output_sym, ctx_store=ctx_store, namespace=self.namespace)
 
 
@@ -237,4 +253,60 @@ def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> Compi
     g._topo_cache[ns] = None
     order = G.topo_order(g, ns)
     memory_plan = L.plan_memory(g, ns)
-    return CompiledPlan(ns, order, fused_ops, config, memory_plan, L.BufferPool(g.device))
+    plan = CompiledPlan(ns, order, fused_ops, config, memory_plan, L.BufferPool(g.device),
+                        compiled_at=time.time())
+    _register_dirty_tracking(plan, g, ns)
+    return plan
+
+
+def _register_dirty_tracking(plan: CompiledPlan, g, ns):
+    """Every node of the plan reports its invalidation (a set_ upstream) into
+    plan.dirty_nodes (src/compiler.jl:126-131)."""
+    def mark(sym, plan=plan):
+        plan.dirty_nodes.add(sym)
+    for sym in plan.order:
+        nd = g.nodes[ns].get(sym)
+        if nd is not None:
+            nd.on_change = mark
+
+
+def is_dirty(plan: CompiledPlan) -> bool:
+    return plan.is_dirty()
+
+
+def recompile(plan: CompiledPlan, g) -> CompiledPlan:
+    """recompile!(plan, g) (src/compiler.jl:142-191): a no-op for a clean
+    plan; otherwise the rules are applied again, but only to matches that
+    touch the region downstream of the dirty nodes, and the order and memory
+    plan are recomputed.  A graph that gained nodes since the last
+    compilation is compiled afresh."""
+    if not plan.is_dirty():
+        return plan
+    ns = plan.namespace
+    if len(g.nodes[ns]) != len(plan.order):
+        fresh = compile(g, plan.config, namespace=ns)
+        plan.order, plan.memory_plan = fresh.order, fresh.memory_plan
+        plan.pool, plan.fused_ops = fresh.pool, fresh.fused_ops
+        _register_dirty_tracking(plan, g, ns)
+    else:
+        affected: Set[str] = set()
+        queue = list(plan.dirty_nodes)
+        while queue:
+            sym = queue.pop()
+            if sym in affected:
+                continue
+            affected.add(sym)
+            queue.extend(consumers(g, sym, ns))
+        for m in scan_graph(g, plan.config.rules, ns):
+            if not affected.intersection(m.nodes):
+                continue
+            if _apply_fusion(g, ns, m.nodes, m.rule, training=plan.config.training):
+                plan.fused_ops[m.nodes[-1]] = m.rule.result
+        g._topo_cache[ns] = None
+        plan.order = G.topo_order(g, ns)
+        plan.memory_plan = L.plan_memory(g, ns)
+        _register_dirty_tracking(plan, g, ns)
+    plan.dirty_nodes.clear()
+    plan.n_recompiles += 1
+    plan.compiled_at = time.time()
+    return plan

@@ -141,19 +141,22 @@ def execute_rule_pooled(g, rule, pool: BufferPool, ctx_store=None):
 
 
 def run_planned(g, plan: MemoryPlan, pool: BufferPool, output_sym, namespace=None,
-                ctx_store=None):
+                ctx_store=None, training=False):
     """Run the graph in plan order up to `output_sym` with pooled outputs and
     return every computed node's buffer to the pool once its interval has
     ended (the reference's CompiledPlan call, src/compiler.jl:204-240).  The
     requested output stays; nodes without a rule (inputs, parameters) are
-    never released, since their values belong to the caller."""
+    never released, since their values belong to the caller; with
+    `training`, neither is a backpropagable (Quantom) node, whose forward
+    value a backward pass reads (src/compiler.jl:233)."""
     ns = namespace or g.active_ns
     held: List[str] = []
     for step, sym in enumerate(plan.order, start=1):
         nd = g.nodes[ns][sym]
         if not (nd.valid and nd.value is not None) and sym in g.rules[ns]:
             execute_rule_pooled(g, g.rules[ns][sym], pool, ctx_store)
-            held.append(sym)
+            if not (training and issubclass(nd.atom_type, G.Quantom)):
+                held.append(sym)
         for prev in list(held):
             if prev == output_sym:
                 continue

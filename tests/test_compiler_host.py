@@ -1,7 +1,8 @@
-"""Host tests of the rewrite-rule compiler (no GPU: graphs carry no values,
-only rules).  The matching and application logic follows the reference's
-scan_graph / _apply_fusion! (src/compiler_rules.jl:575-623,
-src/compiler.jl:16-66)."""
+"""Host tests of the rewrite-rule compiler (no GPU): rule matching on graphs
+that carry no values, and recompilation and pooling on graphs whose ops the
+test registers on a CPU device tag.  The logic follows the reference's
+scan_graph / _apply_fusion! / recompile! / plan call
+(src/compiler_rules.jl:575-623, src/compiler.jl:16-240)."""
 import pytest
 
 pytest.importorskip("torch")
@@ -172,3 +173,174 @@ def test_compile_attaches_a_memory_plan():
     plan = C.compile(g, C.CompilerConfig(training=False))
     assert plan.memory_plan is not None and plan.pool is not None
     assert set(plan.memory_plan.order) == {"x", "W", "v"}
+
+
+# ------------------------------------- recompilation and pooling semantics ---
+# Restatements of the reference's compiler tests (test/test_compiler.jl:147-292)
+# on the host: the ops are registered by the test on a CPU device tag, under
+# names of its own, so the executor runs without a kernel.
+
+import torch  # noqa: E402
+
+
+class _HostDevice:
+    torch_device = torch.device("cpu")
+
+
+@pytest.fixture
+def cpu_ops():
+    saved = dict(G.CUSTOM_OPS)
+
+    def mm(dev, out, ins, attrs, sym, node, ctx):
+        out.copy_(ins[0] @ ins[1])
+
+    def addb(dev, out, ins, attrs, sym, node, ctx):
+        out.copy_(ins[0] + ins[1])
+
+    def relu(dev, out, ins, attrs, sym, node, ctx):
+        out.copy_(torch.relu(ins[0]))
+
+    def mm_add_relu(dev, out, ins, attrs, sym, node, ctx):
+        out.copy_(torch.relu(ins[0] @ ins[1] + ins[2]))
+
+    for name, fn in (("t_mm", mm), ("t_addb", addb), ("t_relu", relu),
+                     ("t_mm_add_relu", mm_add_relu)):
+        G.register_op(name, fn)
+    yield
+    G.CUSTOM_OPS.clear()
+    G.CUSTOM_OPS.update(saved)
+
+
+def _chain(seed=0):
+    """x·W + b, then relu (the reference's build_chain with square operands,
+    since the test ops get the first input's shape)."""
+    gen = torch.Generator().manual_seed(seed)
+    g = G.NeuroGraph(device=_HostDevice())
+    G.set_(g, "x", torch.randn(4, 4, generator=gen), is_param=True)
+    G.set_(g, "W", torch.randn(4, 4, generator=gen))
+    G.set_(g, "b", torch.randn(1, 4, generator=gen))
+    _rule(g, "h", ["x", "W"], "t_mm")
+    _rule(g, "y", ["h", "b"], "t_addb")
+    _rule(g, "z", ["y"], "t_relu")
+    return g
+
+
+def _fusion():
+    return C.RewriteRule("t_mar", ("t_mm", "t_addb", "t_relu"), "t_mm_add_relu", cost_delta=0.5)
+
+
+_quiet_shapes = pytest.mark.filterwarnings("ignore:Shape inference")
+
+
+@_quiet_shapes
+def test_plan_starts_clean_and_set_marks_it_dirty(cpu_ops):
+    g = _chain()
+    plan = C.compile(g, C.CompilerConfig(rules=[_fusion()], training=False))
+    assert g.rules["default"]["z"].op == "t_mm_add_relu"
+    assert not C.is_dirty(plan) and plan.n_recompiles == 0
+    G.set_(g, "x", torch.randn(4, 4), is_param=True)
+    assert C.is_dirty(plan)
+
+
+@_quiet_shapes
+def test_recompile_is_a_no_op_on_a_clean_plan(cpu_ops):
+    g = _chain()
+    plan = C.compile(g, C.CompilerConfig(rules=[_fusion()], training=False))
+    C.recompile(plan, g)
+    C.recompile(plan, g)
+    assert plan.n_recompiles == 0
+
+
+@_quiet_shapes
+def test_calling_a_dirty_plan_recompiles_and_recomputes(cpu_ops):
+    g = _chain()
+    plan = C.compile(g, C.CompilerConfig(rules=[_fusion()], training=False))
+    plan(g, "z")
+    assert plan.n_recompiles == 0
+    x_new = torch.randn(4, 4, generator=torch.Generator().manual_seed(9))
+    G.set_(g, "x", x_new, is_param=True)
+    assert C.is_dirty(plan)
+    out = plan(g, "z").clone()
+    assert plan.n_recompiles == 1 and not C.is_dirty(plan)
+    ref = G.NeuroGraph(device=_HostDevice())
+    G.set_(ref, "x", x_new)
+    G.set_(ref, "W", g.nodes["default"]["W"].value)
+    G.set_(ref, "b", g.nodes["default"]["b"].value)
+    _rule(ref, "h", ["x", "W"], "t_mm")
+    _rule(ref, "y", ["h", "b"], "t_addb")
+    _rule(ref, "z", ["y"], "t_relu")
+    torch.testing.assert_close(out, G.demand(ref, "z", ctx_store=G.CtxStore()), atol=1e-5,
+                               rtol=0)
+
+
+@_quiet_shapes
+def test_recompile_picks_up_a_rule_added_after_compilation(cpu_ops):
+    """A graph that gained nodes since the last compilation is compiled
+    afresh on the next call (src/compiler.jl:146-158)."""
+    g = _chain()
+    plan = C.compile(g, C.CompilerConfig(rules=[_fusion()], training=False))
+    _rule(g, "w", ["z"], "t_relu")
+    plan.dirty_nodes.add("z")
+    out = plan(g, "w")
+    assert plan.n_recompiles == 1 and "w" in plan.order
+    ns = g.nodes["default"]
+    x, W, b = ns["x"].value, ns["W"].value, ns["b"].value
+    torch.testing.assert_close(out, torch.relu(x @ W + b), atol=1e-5, rtol=0)
+
+
+def _mlp(atom):
+    gen = torch.Generator().manual_seed(3)
+    g = G.NeuroGraph(device=_HostDevice())
+    G.set_(g, "x", torch.randn(6, 6, generator=gen), is_param=True)
+    for w in ("W1", "W2", "W3"):
+        G.set_(g, w, torch.randn(6, 6, generator=gen), is_param=True)
+    for out, ins, op in (("h1", ["x", "W1"], "t_mm"), ("h2", ["h1"], "t_relu"),
+                         ("h3", ["h2", "W2"], "t_mm"), ("h4", ["h3"], "t_relu"),
+                         ("out", ["h4", "W3"], "t_mm")):
+        G.addrule(g, G.GraphRule(out, ins, op, atom_type=atom))
+    return g
+
+
+@_quiet_shapes
+def test_inference_pooling_recycles_intermediates(cpu_ops):
+    g = _mlp(G.Datom)
+    plan = C.compile(g, C.CompilerConfig(rules=[], training=False))
+    plan(g, "out")
+    st = plan.pool.stats()
+    assert st["allocs"] + st["hits"] > 0
+    assert g.nodes["default"]["h1"].value is None
+
+
+@_quiet_shapes
+def test_training_pooling_keeps_backpropagable_intermediates(cpu_ops):
+    g = _mlp(G.Quantom)
+    plan = C.compile(g, C.CompilerConfig(rules=[], training=True))
+    plan(g, "out")
+    assert all(g.nodes["default"][s].value is not None for s in ("h1", "h2", "h3", "h4"))
+
+
+@_quiet_shapes
+def test_params_and_requested_output_never_recycled(cpu_ops):
+    for atom, training in ((G.Datom, False), (G.Quantom, True)):
+        g = _mlp(atom)
+        plan = C.compile(g, C.CompilerConfig(rules=[], training=training))
+        plan(g, "out")
+        for s in ("W1", "W2", "W3", "out"):
+            assert g.nodes["default"][s].value is not None, (s, training)
+
+
+def test_training_guard_refuses_then_allows_a_made_up_op():
+    """test/test_compiler.jl:147-167: a rule into an op without a backward
+    rule is refused by default and applied with training=False."""
+    made_up = C.RewriteRule("made_up_fusion", ("matmul", "gelu"), "made_up_op_no_grad",
+                            cost_delta=0.9)
+    g = _graph(["x", "W"])
+    _rule(g, "h", ["x", "W"], "matmul")
+    _rule(g, "z", ["h"], "gelu")
+    C.compile(g, C.CompilerConfig(rules=[made_up]))
+    assert g.rules["default"]["z"].op == "gelu"
+    g2 = _graph(["x", "W"])
+    _rule(g2, "h", ["x", "W"], "matmul")
+    _rule(g2, "z", ["h"], "gelu")
+    C.compile(g2, C.CompilerConfig(rules=[made_up], training=False))
+    assert g2.rules["default"]["z"].op == "made_up_op_no_grad"
