@@ -15,6 +15,10 @@ rules that map unfused transformer graphs onto the B200 fused operators.
                                                   _register_dirty_tracking,
                                                   is_dirty, recompile
   plan(g, out)  src/compiler.jl:204-240           CompiledPlan.__call__
+  symbolic_cost / default_cost                    symbolic_cost / default_cost
+    src/compiler_config.jl:230-283
+  _choose_cheapest_alternative                    choose_cheapest_alternative
+    src/compiler_rules.jl:696-750
   _flash_condition  src/compiler_config.jl:107    _flash_condition
   memory plan + BufferPool (liveness.jl)          neurodsl_b200/liveness.py
 
@@ -136,11 +140,72 @@ B200_RULES: List[RewriteRule] = [
 BACKWARD_SUPPORT = {"identity"}
 
 
+# ------------------------------------------------------------------- cost ---
+
+_GEMM_OPS = {"matmul", "fused_matmul_relu", "fused_linear_gelu", "fused_matmul_sigmoid",
+             "scaled_matmul", "fused_rmsnorm_linear", "fused_layernorm_linear",
+             "fused_matmul_add", "fused_linear_residual", "linear"}
+_ELEMENTWISE_OPS = {"relu", "gelu", "sigmoid", "tanh", "softmax", "scale", "add", "wsum", "nsum",
+                    "scale_add", "scale_mask"}
+_ATTENTION_OPS = {"softmax_attn", "flash_attention", "flash_attn"}
+
+
+def _numel(shape) -> int:
+    n = 1
+    for x in shape:
+        n *= int(x)
+    return n
+
+
+def symbolic_cost(op: str, shapes) -> float:
+    """A size-based cost of `op` on inputs of the given shapes, in the units of
+    the reference's symbolic model (src/compiler_config.jl:230-267): GEMMs
+    M·K·N / 1e9 from the first two operands, elementwise ops volume / 1e8,
+    norms volume / 5e7, attention S²·d / 1e9, pure restructuring 0, anything
+    else volume / 5e7.  The B200 ops are placed in the matching class."""
+    shapes = [tuple(s) for s in shapes]
+    if not shapes:
+        return 0.0
+    if op in _GEMM_OPS:
+        if len(shapes) < 2:
+            return 0.0
+        a, b = shapes[0], shapes[1]
+        M = a[0] if len(a) >= 1 else 1
+        K = a[1] if len(a) >= 2 else 1
+        N = b[1] if len(b) >= 2 else (b[0] if len(b) >= 1 else 1)
+        return M * K * N / 1e9
+    if op in _ELEMENTWISE_OPS:
+        return _numel(shapes[0]) / 1e8
+    if op in ("layernorm", "rmsnorm"):
+        return _numel(shapes[0]) / 5e7
+    if op in _ATTENTION_OPS:
+        s = shapes[0]
+        seq = s[0] if len(s) >= 1 else 1
+        d = s[1] if len(s) >= 2 else 1
+        return seq * seq * d / 1e9
+    if op in ("transpose", "identity", "double_transpose_elim"):
+        return 0.0
+    return _numel(shapes[0]) / 5e7
+
+
+def default_cost(op: str, shapes, rule_cost_delta: float = 0.0) -> float:
+    """symbolic_cost less the rule's declared saving, never below zero
+    (src/compiler_config.jl:278-283)."""
+    return max(0.0, symbolic_cost(op, shapes) - rule_cost_delta)
+
+
+# Rule pairs that rewrite the same pattern instance into alternative ops; when
+# both match at the same root node only the cheaper survives
+# (src/compiler_rules.jl:696).
+ALTERNATIVE_RULE_PAIRS: List[Tuple[str, str]] = [("sdpa_fusion", "flash_attention")]
+
+
 @dataclass
 class CompilerConfig:
     rules: List[RewriteRule] = field(default_factory=lambda: list(B200_RULES))
     training: bool = True
     pooled: bool = True      # run with the memory plan's buffer pool
+    cost_fn: Callable = default_cost   # (op, shapes, rule_cost_delta=...) -> float
 
 
 @dataclass
@@ -210,6 +275,36 @@ def scan_graph(g, rules=None, namespace=None) -> List[RuleMatch]:
     return matches
 
 
+def _match_cost(g, m: RuleMatch, cost_fn, ns) -> float:
+    """cost_fn of the match's result on the shapes of its nodes' current
+    values; a match with no known shape never wins (src/compiler_rules.jl:704-713)."""
+    shapes = [tuple(nd.value.shape) for nd in (g.nodes[ns].get(s) for s in m.nodes)
+              if nd is not None and nd.value is not None]
+    if not shapes:
+        return float("inf")
+    return float(cost_fn(m.rule.result, shapes, rule_cost_delta=m.rule.cost_delta))
+
+
+def choose_cheapest_alternative(g, matches: List[RuleMatch], cost_fn=default_cost,
+                                namespace=None) -> List[RuleMatch]:
+    """For each pair in ALTERNATIVE_RULE_PAIRS, of two matches (one of each
+    rule) with the same root node keep the one of lower cost — the first on a
+    tie; every other match stays (src/compiler_rules.jl:725-750)."""
+    ns = namespace or g.active_ns
+    drop = set()
+    for name_a, name_b in ALTERNATIVE_RULE_PAIRS:
+        ia_all = [i for i, m in enumerate(matches) if m.rule.name == name_a]
+        ib_all = [i for i, m in enumerate(matches) if m.rule.name == name_b]
+        for ia in ia_all:
+            for ib in ib_all:
+                if ia in drop or ib in drop or matches[ia].nodes[0] != matches[ib].nodes[0]:
+                    continue
+                ca = _match_cost(g, matches[ia], cost_fn, ns)
+                cb = _match_cost(g, matches[ib], cost_fn, ns)
+                drop.add(ib if ca <= cb else ia)
+    return [m for i, m in enumerate(matches) if i not in drop]
+
+
 def _apply_fusion(g, ns, chain, rule: RewriteRule, training=True) -> bool:
     fused_op = rule.result
     if training and fused_op != "identity" and fused_op not in BACKWARD_SUPPORT:
@@ -247,7 +342,8 @@ def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> Compi
     config = config or CompilerConfig()
     ns = namespace or g.active_ns
     fused_ops: Dict[str, str] = {}
-    for m in scan_graph(g, config.rules, ns):
+    matches = choose_cheapest_alternative(g, scan_graph(g, config.rules, ns), config.cost_fn, ns)
+    for m in matches:
         if _apply_fusion(g, ns, m.nodes, m.rule, training=config.training):
             fused_ops[m.nodes[-1]] = m.rule.result
     g._topo_cache[ns] = None
@@ -297,7 +393,9 @@ def recompile(plan: CompiledPlan, g) -> CompiledPlan:
                 continue
             affected.add(sym)
             queue.extend(consumers(g, sym, ns))
-        for m in scan_graph(g, plan.config.rules, ns):
+        matches = choose_cheapest_alternative(g, scan_graph(g, plan.config.rules, ns),
+                                              plan.config.cost_fn, ns)
+        for m in matches:
             if not affected.intersection(m.nodes):
                 continue
             if _apply_fusion(g, ns, m.nodes, m.rule, training=plan.config.training):

@@ -344,3 +344,35 @@ def test_training_guard_refuses_then_allows_a_made_up_op():
     _rule(g2, "z", ["h"], "gelu")
     C.compile(g2, C.CompilerConfig(rules=[made_up], training=False))
     assert g2.rules["default"]["z"].op == "made_up_op_no_grad"
+
+
+def test_cheapest_of_two_alternative_rules_at_one_root():
+    """test/test_compiler.jl:294-326: of an sdpa_fusion and a flash_attention
+    match at the same root only the cheaper under the cost function stays;
+    matches at different roots both stay."""
+    g = G.NeuroGraph(device=_HostDevice())
+    G.set_(g, "root", torch.randn(8, 8))
+    cheap = C.RewriteRule("sdpa_fusion", ("matmul",), "fused_sdpa", cost_delta=0.1)
+    dear = C.RewriteRule("flash_attention", ("matmul",), "flash_attention_dummy", cost_delta=0.1)
+
+    def cost_fn(op, shapes, rule_cost_delta=0.0):
+        return 1.0 if op == "fused_sdpa" else 100.0
+    kept = C.choose_cheapest_alternative(
+        g, [C.RuleMatch(cheap, ["root"], "default", 0.1),
+            C.RuleMatch(dear, ["root"], "default", 0.1)], cost_fn)
+    assert len(kept) == 1 and kept[0].rule.result == "fused_sdpa"
+    G.set_(g, "root_b", torch.randn(8, 8))
+    kept = C.choose_cheapest_alternative(
+        g, [C.RuleMatch(cheap, ["root"], "default", 0.1),
+            C.RuleMatch(dear, ["root_b"], "default", 0.1)], cost_fn)
+    assert len(kept) == 2
+
+
+def test_default_cost_model():
+    assert C.symbolic_cost("matmul", [(128, 1024), (1024, 4096)]) == 128 * 1024 * 4096 / 1e9
+    assert C.symbolic_cost("gelu", [(10, 10)]) == 100 / 1e8
+    assert C.symbolic_cost("layernorm", [(10, 10)]) == 100 / 5e7
+    assert C.symbolic_cost("flash_attention", [(2048, 64)]) == 2048 * 2048 * 64 / 1e9
+    assert C.symbolic_cost("identity", [(10, 10)]) == 0.0
+    assert C.default_cost("gelu", [(10, 10)], rule_cost_delta=1.0) == 0.0
+    assert C.CompilerConfig().cost_fn is C.default_cost
