@@ -263,8 +263,10 @@ int nd_softmax(void *stream, const float *x, float *y, int rows, int cols);
 /*
  * The residual :add of the operator graph, fp32: y = a + b over
  * [rows][cols], with b the same shape (b_mode 0), one value per column
- * (b_mode 1, length cols) or one per row (b_mode 2, length rows) — the
- * reference's matrix + vector broadcasts.
+ * (b_mode 1, length cols), one per row (b_mode 2, length rows) or a single
+ * value (b_mode 3) — the reference's matrix + vector broadcasts and the
+ * general broadcast of its fallback branch for a (1, cols), (rows, 1) or
+ * (1, 1) matrix b (src/dispatch.jl:386-417).
  */
 int nd_add(void *stream, const float *a, const float *b, float *y, int rows, int cols, int b_mode);
 

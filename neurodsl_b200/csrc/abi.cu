@@ -624,7 +624,7 @@ __attribute__((visibility("default"))) int nd_scale_mask(void* stream, const flo
 __attribute__((visibility("default"))) int nd_add(void* stream, const float* a, const float* b,
                                                   float* y, int rows, int cols, int b_mode) {
   if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_add: negative size");
-  if (b_mode < 0 || b_mode > 2) return fail(ND_ERR_INVALID_ARG, "nd_add: b_mode %d", b_mode);
+  if (b_mode < 0 || b_mode > 3) return fail(ND_ERR_INVALID_ARG, "nd_add: b_mode %d", b_mode);
   if (static_cast<long long>(rows) * cols == 0) return ok();
   if (!a || !b || !y) return fail(ND_ERR_INVALID_ARG, "nd_add: null pointer");
   int rc = check_current_device(nullptr);

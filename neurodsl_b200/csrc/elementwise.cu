@@ -48,14 +48,14 @@ __global__ void scale_mask_kernel(const float* __restrict__ x, float* __restrict
 }
 
 // y = a + b over [rows][cols] fp32; b is the same shape (mode 0), one value
-// per column (mode 1) or one per row (mode 2): the :add op with its bias
-// broadcasts (src/dispatch.jl:386-417).
+// per column (mode 1), one per row (mode 2) or a single value (mode 3): the
+// :add op with its bias broadcasts (src/dispatch.jl:386-417).
 __global__ void add_kernel(const float* __restrict__ a, const float* __restrict__ b,
                            float* __restrict__ y, int rows, int cols, int mode) {
   const long long n = static_cast<long long>(rows) * cols;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long bi = mode == 0 ? i : (mode == 1 ? i % cols : i / cols);
+    const long long bi = mode == 0 ? i : mode == 1 ? i % cols : mode == 2 ? i / cols : 0;
     y[i] = a[i] + b[bi];
   }
 }

@@ -243,7 +243,8 @@ def _infer_output_shape(op: str, inputs, attrs):
     if op == "hcat_heads":
         return (inputs[0].shape[0], sum(x.shape[1] for x in inputs))
     if op == "slice_cols":
-        return (inputs[0].shape[0], attrs["end_col"] - attrs["start_col"] + 1)
+        s, e = attrs.get("start_col", 1), attrs.get("end_col", inputs[0].shape[1])
+        return (inputs[0].shape[0], e - s + 1)
     if op == "flash_attention" and len(inputs) == 1:
         return (inputs[0].shape[0], inputs[0].shape[1] // 3)   # fused (S, 3d) projection
     if op == "add":
@@ -338,10 +339,20 @@ def _bias_vec(b):
     return b.reshape(-1).to(torch.float32).contiguous()
 
 
+def _pad_k(t):
+    """bf16 [rows][K] operand with zero columns up to a multiple of 8: the
+    GEMM moves rows in 16-byte pieces, and the zero columns add nothing to
+    the dot products, so graphs with any inner dimension (the reference's
+    tests use K = 3) run on the same kernel."""
+    K = t.shape[1]
+    return t if K % 8 == 0 else torch.nn.functional.pad(t, (0, 8 - K % 8))
+
+
 def _gemm_into(out, X, Wnk, bias=None, residual=None, act="none"):
     if out.dtype not in (torch.float32, torch.bfloat16) or not out.is_contiguous():
         raise NeuroDSLError(4, "output buffer must be contiguous fp32 or bf16")
-    ops.linear(_bf16_rows(X), Wnk, _bias_vec(bias), residual=residual, act=act, out=out)
+    ops.linear(_pad_k(_bf16_rows(X)), _pad_k(Wnk), _bias_vec(bias), residual=residual, act=act,
+               out=out)
 
 
 def _alias_safe(out, out_node, inputs):
@@ -391,6 +402,23 @@ def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, 
         if aliased:
             output_buffer.copy_(buf)
         _store_ctx(ctx_store, out_sym, {"X": X, "W": W, "n_inputs": len(inputs)})
+        return output_buffer
+    if op == "slice_cols":
+        # columns start_col..end_col (1-based, inclusive) of an (N, d) node,
+        # src/dispatch.jl:544-553: a device copy.  compile() folds the slices
+        # of a multi-head layer into the strided :flash_attention instead.
+        x = inputs[0]
+        s, e = attrs.get("start_col", 1), attrs.get("end_col", x.shape[1])
+        output_buffer.copy_(x[:, s - 1:e])
+        _store_ctx(ctx_store, out_sym, {"start_col": s, "end_col": e})
+        return output_buffer
+    if op == "hcat_heads":
+        # the heads' (N, d_h) outputs side by side, src/dispatch.jl:349-361
+        off = 0
+        for x in inputs:
+            output_buffer[:, off:off + x.shape[1]].copy_(x)
+            off += x.shape[1]
+        _store_ctx(ctx_store, out_sym, {"n_heads": len(inputs), "d_head": inputs[0].shape[1]})
         return output_buffer
     if op in CUSTOM_OPS:
         CUSTOM_OPS[op](dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store)
@@ -562,7 +590,9 @@ def _dispatch_layernorm(dev, output_buffer, inputs, attrs, out_sym, out_node, ct
 def _dispatch_add(dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store):
     """:add (src/dispatch.jl:386-417): same shapes, or a matrix and a vector
     broadcast per column (preferred when the lengths match, as in the
-    reference) or per row, in either operand order (nd_add)."""
+    reference) or per row, in either operand order; and, as the reference's
+    general broadcast, a matrix plus a (1, cols) row, a (rows, 1) column or a
+    single value (nd_add)."""
     a, b = _f32(inputs[0]), _f32(inputs[1])
     if a.dim() == 1 and b.dim() == 2:
         a, b = b, a
@@ -625,7 +655,7 @@ def _dispatch_fused_layernorm_linear(dev, output_buffer, inputs, attrs, out_sym,
             h = torch.empty((rows, K), dtype=torch.bfloat16, device=dev.torch_device)
             out_node.aux_data["_ln_buf"] = h
         ops.layernorm(x.contiguous(), g, bt, eps=eps, out=h, stats=False)
-        ops.linear(h, Wnk, _bias_vec(b), out=output_buffer)
+        ops.linear(_pad_k(h), _pad_k(Wnk), _bias_vec(b), out=output_buffer)
     _store_ctx(ctx_store, out_sym, {"x": x, "gamma": gamma, "beta": beta, "W": W})
     return output_buffer
 

@@ -302,8 +302,10 @@ def scale_mask(scores, d_head, out=None, stream=None):
 
 
 def add(a, b, out=None, stream=None):
-    """a + b for float32 tensors (nd_add, the :add op): b of a's shape, or a
-    vector of one value per column or per row of a 2-D a."""
+    """a + b for float32 tensors (nd_add, the :add op): b of a's shape; a
+    vector of one value per column, else per row, of a 2-D a (the
+    reference's vector cases, columns preferred); or, as its general
+    broadcast does, a (1, cols) row, a (rows, 1) column or a single value."""
     _need(a, "a", torch.float32)
     _need(b, "b", torch.float32)
     rows, cols = (a.shape[0], a.shape[1]) if a.dim() == 2 else (1, a.numel())
@@ -313,6 +315,12 @@ def add(a, b, out=None, stream=None):
         mode = 1
     elif a.dim() == 2 and b.dim() == 1 and b.numel() == rows:
         mode = 2
+    elif a.dim() == 2 and b.dim() == 2 and tuple(b.shape) == (1, cols):
+        mode = 1
+    elif a.dim() == 2 and b.dim() == 2 and tuple(b.shape) == (rows, 1):
+        mode = 2
+    elif b.numel() == 1 and b.dim() <= a.dim():
+        mode = 3
     else:
         raise ValueError(f"add: shapes {tuple(a.shape)} and {tuple(b.shape)} do not broadcast")
     if out is None:
