@@ -19,6 +19,8 @@ rules that map unfused transformer graphs onto the B200 fused operators.
     src/compiler_config.jl:230-283
   _choose_cheapest_alternative                    choose_cheapest_alternative
     src/compiler_rules.jl:696-750
+  (B200) MultiHeadFlashAttention layer            fold_multihead_attention
+    src/flash_attention.jl:232-256 -> :flash_attention
   _flash_condition  src/compiler_config.jl:107    _flash_condition
   memory plan + BufferPool (liveness.jl)          neurodsl_b200/liveness.py
 
@@ -337,8 +339,90 @@ def _apply_fusion(g, ns, chain, rule: RewriteRule, training=True) -> bool:
     return True
 
 
+def _multihead_sources(g, ns, heads):
+    """If the :hcat_heads inputs `heads` are the per-head :flash_attn nodes of
+    a MultiHeadFlashAttention layer (src/flash_attention.jl:232-256) — head h
+    reads columns h·D+1 .. (h+1)·D of the same three projections through
+    :slice_cols, every intermediate read only by the next step — return
+    ((q_full, k_full, v_full), D, causal, nodes to delete); else None."""
+    rules = g.rules[ns]
+    full: List[Optional[str]] = [None, None, None]
+    D = None
+    causal = None
+    dead: Dict[str, None] = {}
+    for h, sym in enumerate(heads):
+        fa = rules.get(sym)
+        if fa is None or fa.op != "flash_attn" or len(fa.inputs) != 3 or sym in dead:
+            return None
+        if len(consumers(g, sym, ns)) != 1:
+            return None
+        c = bool(fa.attrs.get("causal", True))
+        if causal is not None and c != causal:
+            return None
+        causal = c
+        for j, sl in enumerate(fa.inputs):
+            sr = rules.get(sl)
+            if sr is None or sr.op != "slice_cols" or len(sr.inputs) != 1:
+                return None
+            if consumers(g, sl, ns) != [sym]:
+                return None
+            if "start_col" not in sr.attrs or "end_col" not in sr.attrs:
+                return None
+            start, end = int(sr.attrs["start_col"]), int(sr.attrs["end_col"])
+            if D is None:
+                D = end - start + 1
+            if D <= 0 or end - start + 1 != D or start != h * D + 1:
+                return None
+            if full[j] is None:
+                full[j] = sr.inputs[0]
+            elif full[j] != sr.inputs[0]:
+                return None
+            dead[sl] = None
+        if int(fa.attrs.get("d_head", D)) != D:
+            return None
+        dead[sym] = None
+    if D is None:
+        return None
+    return (full[0], full[1], full[2]), D, causal, list(dead)
+
+
+def fold_multihead_attention(g, namespace=None) -> Dict[str, str]:
+    """Rewrite each MultiHeadFlashAttention layer — 3·H :slice_cols, H
+    :flash_attn and the :hcat_heads of their outputs — into one
+    :flash_attention over the three projections: the kernel reads every head
+    in place through strides and writes the concatenated output, so the
+    3·H + 1 copies disappear.  The output keeps the :hcat_heads node's name.
+    Returns {output: "flash_attention"} for each layer folded."""
+    ns = namespace or g.active_ns
+    folded: Dict[str, str] = {}
+    for out, r in list(g.rules[ns].items()):
+        if r.op != "hcat_heads" or not r.inputs:
+            continue
+        found = _multihead_sources(g, ns, r.inputs)
+        if found is None:
+            continue
+        (q_full, k_full, v_full), D, causal, dead = found
+        n_heads = len(r.inputs)
+        for s in dead:
+            del g.rules[ns][s]
+            del g.nodes[ns][s]
+        del g.rules[ns][out]
+        G.addrule(g, G.GraphRule(out, [q_full, k_full, v_full], "flash_attention",
+                                 attrs={"n_heads": n_heads, "d_head": D, "causal": causal},
+                                 namespace=ns))
+        G._invalidate_downstream(g, out, ns)
+        folded[out] = "flash_attention"
+    return folded
+
+
+def _fold_allowed(training) -> bool:
+    # the same training guard as the rewrite rules
+    return not training or "flash_attention" in BACKWARD_SUPPORT
+
+
 def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> CompiledPlan:
-    """Scan, apply the matches in decreasing score, recompute the order."""
+    """Scan, apply the matches in decreasing score, fold multi-head layers
+    into :flash_attention, recompute the order."""
     config = config or CompilerConfig()
     ns = namespace or g.active_ns
     fused_ops: Dict[str, str] = {}
@@ -346,6 +430,8 @@ def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> Compi
     for m in matches:
         if _apply_fusion(g, ns, m.nodes, m.rule, training=config.training):
             fused_ops[m.nodes[-1]] = m.rule.result
+    if _fold_allowed(config.training):
+        fused_ops.update(fold_multihead_attention(g, ns))
     g._topo_cache[ns] = None
     order = G.topo_order(g, ns)
     memory_plan = L.plan_memory(g, ns)
@@ -400,6 +486,8 @@ def recompile(plan: CompiledPlan, g) -> CompiledPlan:
                 continue
             if _apply_fusion(g, ns, m.nodes, m.rule, training=plan.config.training):
                 plan.fused_ops[m.nodes[-1]] = m.rule.result
+        if _fold_allowed(plan.config.training):
+            plan.fused_ops.update(fold_multihead_attention(g, ns))
         g._topo_cache[ns] = None
         plan.order = G.topo_order(g, ns)
         plan.memory_plan = L.plan_memory(g, ns)

@@ -223,3 +223,102 @@ def test_add_op_broadcasts_like_the_reference():
             else:
                 ref = m + v
             np.testing.assert_array_equal(z, ref, err_msg=name)
+
+
+def test_add_op_matrix_broadcasts():
+    """:add of a matrix and a (1, cols) row, a (rows, 1) column or a (1, 1)
+    value — the reference's general broadcast branch (src/dispatch.jl:409-410),
+    which its compiler tests use for a (1, 5) bias — each the fp32 sums NumPy
+    gives, bit for bit."""
+    _, G = _mods()
+    rng = np.random.default_rng(12)
+    a = rng.standard_normal((6, 9)).astype(np.float32)
+    for shape in ((1, 9), (6, 1), (1, 1)):
+        b = rng.standard_normal(shape).astype(np.float32)
+        g = G.NeuroGraph()
+        G.set_(g, "p", a)
+        G.set_(g, "q", b)
+        G.addrule(g, G.GraphRule("z", ["p", "q"], "add"))
+        z = G.demand(g, "z").cpu().numpy()
+        assert z.shape == a.shape
+        np.testing.assert_array_equal(z, a + b, err_msg=str(shape))
+
+
+def test_reference_matmul_add_rule_with_row_bias():
+    """The reference's compiler test of a user rule (:matmul, :add) ->
+    :fused_matmul_add with x (4, 3), W (3, 5) and a (1, 5) bias
+    (test/test_compiler.jl:34-56): the rule applies, and the compiled plan
+    gives the unfused graph's values (the reference's atol 1e-5) and the
+    oracle's within the bf16-operand tolerance.  K = 3 runs on the same GEMM
+    with the inner dimension zero-padded."""
+    C, G = _mods()
+    rng = np.random.default_rng(13)
+    x = oracle.bf16_round(rng.standard_normal((4, 3)).astype(np.float32))
+    W = oracle.bf16_round(rng.standard_normal((3, 5)).astype(np.float32))
+    b = rng.standard_normal((1, 5)).astype(np.float32)
+
+    def build(G, g):
+        G.set_(g, "x", x, is_param=True)
+        G.set_(g, "W", W)
+        G.set_(g, "b", b)
+        G.addrule(g, G.GraphRule("h", ["x", "W"], "matmul"))
+        G.addrule(g, G.GraphRule("z", ["h", "b"], "add"))
+    rule = C.RewriteRule("t_matmul_add", ("matmul", "add"), "fused_matmul_add", cost_delta=0.2)
+    g = G.NeuroGraph()
+    build(G, g)
+    n_before = len(g.rules["default"])
+    plan = C.compile(g, C.CompilerConfig(rules=[rule], training=False))
+    assert len(g.rules["default"]) < n_before
+    assert g.rules["default"]["z"].op == "fused_matmul_add" and len(plan.fused_ops) == 1
+    out_fused = plan(g, "z").cpu().numpy()
+    gref = G.NeuroGraph()
+    build(G, gref)
+    out_ref = G.demand(gref, "z", ctx_store=G.CtxStore()).cpu().numpy()
+    np.testing.assert_allclose(out_fused, out_ref, atol=1e-5, rtol=0)
+    check(out_fused, oracle.linear(x, W, b.reshape(-1), trans_w=False))
+
+
+def test_multihead_layer_runs_unfused_and_folded():
+    """The graph MultiHeadFlashAttention builds (src/flash_attention.jl:232-256:
+    projections, per head three :slice_cols and a causal :flash_attn,
+    :hcat_heads, output projection) runs as written — the slices and the
+    concatenation as device copies — and compiled, where the layer folds
+    into one strided :flash_attention; both match the oracle."""
+    rng = np.random.default_rng(14)
+    S, H, D = 130, 4, 64
+    d = H * D
+    x = oracle.bf16_round(rng.standard_normal((S, d)).astype(np.float32))
+    Ws = {n: oracle.bf16_round((0.06 * rng.standard_normal((d, d))).astype(np.float32))
+          for n in ("Wq", "Wk", "Wv", "Wo")}
+
+    def build(G, g):
+        G.set_(g, "x", x)
+        for n, w in Ws.items():
+            G.set_(g, n, w, is_param=True)
+        heads = []
+        for p in "qkv":
+            G.addrule(g, G.GraphRule(f"a_{p}", ["x", f"W{p}"], "linear"))
+        for h in range(H):
+            for p in "qkv":
+                G.addrule(g, G.GraphRule(f"a_{p}_h{h}", [f"a_{p}"], "slice_cols",
+                                         attrs={"start_col": h * D + 1, "end_col": (h + 1) * D}))
+            G.addrule(g, G.GraphRule(f"a_ao_h{h}", [f"a_q_h{h}", f"a_k_h{h}", f"a_v_h{h}"],
+                                     "flash_attn", attrs={"d_head": D, "causal": True}))
+            heads.append(f"a_ao_h{h}")
+        G.addrule(g, G.GraphRule("a_concat", heads, "hcat_heads"))
+        G.addrule(g, G.GraphRule("a_output", ["a_concat", "Wo"], "linear"))
+    y0, _, _ = _run(build, False, "a_output")
+    y1, fused, g = _run(build, True, "a_output")
+    assert fused == {"a_concat": "flash_attention"}
+    assert g.rules["default"]["a_concat"].inputs == ["a_q", "a_k", "a_v"]
+    proj = {p: oracle.linear(x, Ws[f"W{p}"]) for p in "qkv"}
+    cat = np.zeros((S, d), np.float32)
+    for h in range(H):
+        sl = slice(h * D, (h + 1) * D)
+        o, _, _ = oracle.attn_simple(*(oracle.bf16_round(proj[p][:, sl]) for p in "qkv"), D,
+                                     causal=True)
+        cat[:, sl] = o
+    ref = oracle.linear(oracle.bf16_round(cat), Ws["Wo"])
+    check(y0, ref)
+    check(y1, ref)
+    np.testing.assert_allclose(y0, y1, atol=2e-3, rtol=0)

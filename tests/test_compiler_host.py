@@ -376,3 +376,49 @@ def test_default_cost_model():
     assert C.symbolic_cost("identity", [(10, 10)]) == 0.0
     assert C.default_cost("gelu", [(10, 10)], rule_cost_delta=1.0) == 0.0
     assert C.CompilerConfig().cost_fn is C.default_cost
+
+
+def _mha_graph(H=4, D=64, order=None, extra_reader=False):
+    """The rules MultiHeadFlashAttention adds (src/flash_attention.jl:232-256):
+    three bias-free projections, per head three :slice_cols and a causal
+    :flash_attn, the :hcat_heads of the heads and the output projection."""
+    g = _graph(["x", "Wq", "Wk", "Wv", "Wo"])
+    for p in "qkv":
+        _rule(g, f"a_{p}", ["x", f"W{p}"], "linear")
+    heads = []
+    for h in range(H):
+        for p in "qkv":
+            _rule(g, f"a_{p}_h{h}", [f"a_{p}"], "slice_cols", start_col=h * D + 1,
+                  end_col=(h + 1) * D)
+        _rule(g, f"a_ao_h{h}", [f"a_q_h{h}", f"a_k_h{h}", f"a_v_h{h}"], "flash_attn", d_head=D,
+              causal=True)
+        heads.append(f"a_ao_h{h}")
+    if order is not None:
+        heads = [heads[i] for i in order]
+    _rule(g, "a_concat", heads, "hcat_heads")
+    _rule(g, "a_output", ["a_concat", "Wo"], "linear")
+    if extra_reader:
+        _rule(g, "peek", ["a_q_h0"], "gelu")
+    return g
+
+
+def test_multihead_layer_folds_into_flash_attention():
+    g = _mha_graph()
+    plan = C.compile(g, C.CompilerConfig(training=False))
+    r = g.rules["default"]["a_concat"]
+    assert (r.op, r.inputs) == ("flash_attention", ["a_q", "a_k", "a_v"])
+    assert r.attrs == {"n_heads": 4, "d_head": 64, "causal": True}
+    assert plan.fused_ops["a_concat"] == "flash_attention"
+    assert not [s for s in g.rules["default"] if "_h" in s]
+    assert not [s for s in g.nodes["default"] if "_h" in s]
+    assert plan.order.index("a_concat") < plan.order.index("a_output")
+
+
+def test_multihead_fold_needs_the_layer_exactly():
+    # heads concatenated out of order, a slice read elsewhere, training mode
+    for g, cfg in ((_mha_graph(order=[1, 0, 2, 3]), C.CompilerConfig(training=False)),
+                   (_mha_graph(extra_reader=True), C.CompilerConfig(training=False)),
+                   (_mha_graph(), C.CompilerConfig(training=True))):
+        C.compile(g, cfg)
+        assert g.rules["default"]["a_concat"].op == "hcat_heads"
+        assert "a_q_h1" in g.rules["default"]
