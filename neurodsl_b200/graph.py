@@ -12,6 +12,7 @@ the same op symbols, attrs, output-buffer ownership and CtxStore contents:
     src/graph_api.jl:12-35
   addrule!(g, rule)  src/graph_api.jl:152   addrule(g, rule)
   topo_order!        src/graph_api.jl:163   topo_order(g)
+  invalidate_all!    src/graph_api.jl:222   invalidate_all(g)
   demand!(g, sym; ctx_store)                demand(g, sym, ctx_store=...)
     src/dispatch.jl:592-615
   execute_rule!      src/dispatch.jl:106    execute_rule(g, rule, ...)
@@ -283,6 +284,15 @@ def execute_rule(g: NeuroGraph, rule: GraphRule, ctx_store=None, namespace=None)
     _dispatch_op(dev, out_node.value, rule.op, inputs, rule.attrs, rule.output, out_node, ctx_store)
     out_node.valid = True
     return out_node.value
+
+
+def invalidate_all(g: NeuroGraph, namespace: Optional[str] = None):
+    """invalidate_all!(g) (src/graph_api.jl:222-223): every node that is not a
+    parameter is marked for recomputation."""
+    ns = namespace or g.active_ns
+    for nd in g.nodes[ns].values():
+        if not nd.is_param:
+            nd.valid = False
 
 
 def demand(g: NeuroGraph, name: str, ctx_store=None, namespace=None):

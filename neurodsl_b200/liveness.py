@@ -9,6 +9,9 @@
   compute_liveness  src/liveness.jl:83-113         compute_liveness
   greedy_interval_coloring  :130-158               greedy_interval_coloring
   MemoryPlan                                       MemoryPlan
+  plan_memory!  src/liveness.jl:198-207            plan_memory_pool (plan_memory
+                                                   returns the plan alone)
+  demand_planned!  src/liveness.jl:217-257         demand_planned
 
 A node lives from the topological step that computes it to the last step
 that reads it; parameters live to the end.  The greedy sweep gives every node
@@ -58,6 +61,8 @@ class BufferPool:
         self.buckets.setdefault((tuple(buf.shape), buf.dtype), []).append(buf)
 
     def stats(self):
+        """pool_stats (src/liveness.jl:64-68): allocations, hits and the hit
+        rate in percent."""
         total = self.n_alloc + self.n_hits
         rate = round(100.0 * self.n_hits / total, 1) if total else 0.0
         return {"allocs": self.n_alloc, "hits": self.n_hits, "hit_rate_pct": rate}
@@ -169,3 +174,27 @@ def run_planned(g, plan: MemoryPlan, pool: BufferPool, output_sym, namespace=Non
         if sym == output_sym:
             break
     return g.nodes[ns][output_sym].value
+
+
+def pool_stats(pool: BufferPool):
+    return pool.stats()
+
+
+def plan_memory_pool(g, namespace=None):
+    """plan_memory!(g) (src/liveness.jl:198-207): the memory plan and an empty
+    buffer pool on the graph's device."""
+    return plan_memory(g, namespace), BufferPool(g.device)
+
+
+def demand_planned(g, sym, plan: MemoryPlan, pool: BufferPool, ctx_store=None,
+                   namespace=None):
+    """demand_planned!(g, sym, plan, pool) (src/liveness.jl:217-257): a valid
+    node's value as is, otherwise the planned run up to `sym` with pooled
+    buffers, each released once its interval has ended."""
+    ns = namespace or g.active_ns
+    if ns not in g.nodes or sym not in g.nodes[ns]:
+        raise G.NeuroDSLError(1, f":{sym} introuvable dans :{ns}")
+    nd = g.nodes[ns][sym]
+    if nd.valid and nd.value is not None:
+        return nd.value
+    return run_planned(g, plan, pool, sym, ns, ctx_store)

@@ -422,3 +422,26 @@ def test_multihead_fold_needs_the_layer_exactly():
         C.compile(g, cfg)
         assert g.rules["default"]["a_concat"].op == "hcat_heads"
         assert "a_q_h1" in g.rules["default"]
+
+
+@_quiet_shapes
+def test_memory_planning_like_the_reference(cpu_ops):
+    """test/test_runtime_optimizations.jl:20-36: plan_memory! gives at most
+    one slot per node and an untouched pool; after invalidate_all! the planned
+    demand recomputes the output."""
+    from neurodsl_b200 import liveness as L
+    g = G.NeuroGraph(device=_HostDevice())
+    G.set_(g, "x", torch.rand(2, 2), is_param=True)
+    G.set_(g, "w", torch.rand(2, 2), is_param=True)
+    _rule(g, "h", ["x", "w"], "t_mm")
+    _rule(g, "out", ["h"], "t_relu")
+    plan, pool = L.plan_memory_pool(g)
+    assert plan.n_slots <= len(plan.order)
+    assert pool.n_alloc >= 0 and pool.n_hits == 0
+    G.invalidate_all(g)
+    assert not g.nodes["default"]["h"].valid and g.nodes["default"]["x"].valid
+    val = L.demand_planned(g, "out", plan, pool)
+    x, w = g.nodes["default"]["x"].value, g.nodes["default"]["w"].value
+    torch.testing.assert_close(val, torch.relu(x @ w))
+    assert L.demand_planned(g, "out", plan, pool) is val          # valid: no recompute
+    assert L.pool_stats(pool)["allocs"] == 2
