@@ -13,6 +13,8 @@ the same op symbols, attrs, output-buffer ownership and CtxStore contents:
   addrule!(g, rule)  src/graph_api.jl:152   addrule(g, rule)
   topo_order!        src/graph_api.jl:163   topo_order(g)
   invalidate_all!    src/graph_api.jl:222   invalidate_all(g)
+  activate! / namespaces / node / params    activate / namespaces / node / params
+    src/graph_api.jl:9-10,146-150,225-226   (is_backpropable: src/types.jl:35)
   demand!(g, sym; ctx_store)                demand(g, sym, ctx_store=...)
     src/dispatch.jl:592-615
   execute_rule!      src/dispatch.jl:106    execute_rule(g, rule, ...)
@@ -125,6 +127,37 @@ class NeuroGraph:
         self.nodes.setdefault(ns, {})
         self.rules.setdefault(ns, {})
         self._topo_cache.setdefault(ns, None)
+
+
+def activate(g: NeuroGraph, ns: str) -> NeuroGraph:
+    """activate!(g, ns) (src/graph_api.jl:9): later calls without a namespace
+    use `ns`."""
+    g._ensure_namespace(ns)
+    g.active_ns = ns
+    return g
+
+
+def namespaces(g: NeuroGraph) -> List[str]:
+    return list(g.nodes)
+
+
+def is_backpropable(nd: "GraphNode") -> bool:
+    """A Quantom node carries gradients (src/types.jl:35)."""
+    return issubclass(nd.atom_type, Quantom)
+
+
+def node(g: NeuroGraph, name: str, namespace: Optional[str] = None) -> "GraphNode":
+    """node(g, name) (src/graph_api.jl:146-150)."""
+    ns = namespace or g.active_ns
+    if ns not in g.nodes or name not in g.nodes[ns]:
+        raise NeuroDSLError(1, f"Nœud :{name} introuvable dans :{ns}")
+    return g.nodes[ns][name]
+
+
+def params(g: NeuroGraph, namespace: Optional[str] = None) -> List["GraphNode"]:
+    """The backpropagable parameter nodes (src/graph_api.jl:225-226)."""
+    ns = namespace or g.active_ns
+    return [nd for nd in g.nodes[ns].values() if nd.is_param and is_backpropable(nd)]
 
 
 def _consumers(g, ns):

@@ -166,3 +166,28 @@ def test_aliased_output_goes_through_a_kept_side_buffer():
     xb = torch.zeros(4, 8, dtype=torch.bfloat16)
     third, aliased = G._alias_safe(xb, node, [xb])
     assert aliased and third is not buf and third.dtype == torch.bfloat16
+
+
+def test_graph_api_like_the_reference():
+    """test/test_graph_api.jl:4-36 restated: node / is_backpropable / params,
+    topological order, invalidation on set_, and namespace isolation with
+    activate."""
+    g = G.NeuroGraph(namespace="t", device=HostDevice())
+    G.set_(g, "x", torch.ones(2, 2), is_param=True, namespace="t")
+    G.set_(g, "d", torch.tensor([1, 2]), atom_type=G.Datom, namespace="t")
+    assert G.is_backpropable(G.node(g, "x", namespace="t"))
+    assert not G.is_backpropable(G.node(g, "d", namespace="t"))
+    assert len(G.params(g, namespace="t")) == 1
+    G.set_(g, "W", torch.ones(2, 2), is_param=True, namespace="t")
+    G.addrule(g, G.GraphRule("out", ["x", "W"], "matmul", attrs={"trans_b": False},
+                             namespace="t"))
+    order = G.topo_order(g, "t")
+    assert "out" in order and order.index("x") < order.index("out")
+    G.set_(g, "x", torch.zeros(2, 2), namespace="t")
+    assert not G.node(g, "out", namespace="t").valid
+    G.activate(g, "other")
+    assert g.active_ns == "other" and set(G.namespaces(g)) == {"t", "other"}
+    G.set_(g, "x", torch.ones(2, 2), namespace="other")
+    assert "out" not in g.nodes["other"]
+    with pytest.raises(NeuroDSLError):
+        G.node(g, "out")                      # the active namespace has no :out
