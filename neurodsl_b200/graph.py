@@ -21,7 +21,7 @@ the same op symbols, attrs, output-buffer ownership and CtxStore contents:
   _infer_output_shape  src/dispatch.jl:36   _infer_output_shape(op, inputs, attrs)
   _dispatch_op       src/dispatch.jl:212    _dispatch_op(dev, out, op, inputs, ...)
   register_op! / CUSTOM_OPS  :587-588       register_op / CUSTOM_OPS
-  @defop  src/dsl_macros.jl:9-26            @defop-style: register_op(name, fn)
+  @defop  src/dsl_macros.jl:9-26            @defop(name) decorator
 
 Op symbols are strings ("flash_attn" for :flash_attn).  Node values are torch
 CUDA tensors on the graph's B200Device: float32 (the reference's Float32
@@ -355,6 +355,15 @@ def register_op(name: str, fn: Callable):
     """register_op!(name, fn) — src/dispatch.jl:587-588."""
     CUSTOM_OPS[name] = fn
     return fn
+
+
+def defop(name: str):
+    """The @defop macro's function form (src/dsl_macros.jl:9-26) as a
+    decorator: the function (dev, out, inputs, attrs, out_sym, node, ctx)
+    writes its result into `out` and is registered under `name`."""
+    def deco(fn: Callable) -> Callable:
+        return register_op(name, fn)
+    return deco
 
 
 # ----------------------------------------------------------- op helpers ---

@@ -191,3 +191,17 @@ def test_graph_api_like_the_reference():
     assert "out" not in g.nodes["other"]
     with pytest.raises(NeuroDSLError):
         G.node(g, "out")                      # the active namespace has no :out
+
+
+def test_defop_decorator_registers_an_op():
+    @G.defop("twice_plus_one")
+    def _op(dev, out, inputs, attrs, out_sym, nd, ctx):
+        out.copy_(2 * inputs[0] + 1)
+    g = host_graph()
+    G.set_(g, "x", torch.arange(4.0).reshape(2, 2))
+    G.addrule(g, G.GraphRule("y", ["x"], "identity"))
+    G.addrule(g, G.GraphRule("z", ["y"], "twice_plus_one"))
+    assert G.CUSTOM_OPS["twice_plus_one"] is _op
+    with pytest.warns(UserWarning):
+        z = G.demand(g, "z")
+    torch.testing.assert_close(z, 2 * torch.arange(4.0).reshape(2, 2) + 1)
