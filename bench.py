@@ -114,9 +114,15 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self._t.join(timeout=2)
+        return self.summarise(self.lines)
+
+    @staticmethod
+    def summarise(lines):
+        """Median SM clock under load, the max clock and every throttle
+        reason seen Active in the sampled CSV lines."""
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in lines:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue

@@ -40,3 +40,46 @@ def test_reference_arm_other_ranks_exit_without_work():
                        text=True, timeout=300, cwd=ROOT, env=env)
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [l for l in r.stdout.splitlines() if l.startswith("{")]
+
+
+def _bench():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_under_test", os.path.join(ROOT, "bench.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_algorithmic_work_per_unit():
+    """The roofline numerators: the causal prefill FLOPs of one step and the
+    decode step's HBM bytes, 196,608·L + 393,216 at B = 64, H = 12, summing to
+    27,443,331,072 over the 128 steps L = 1025 … 1152."""
+    b = _bench()
+    assert b.FLOPS_PER_STEP == 68_753_031_168
+    assert b.dec_bytes(1) == 196_608 + 393_216
+    assert sum(b.dec_bytes(L) for L in range(1025, 1153)) == 27_443_331_072
+
+
+def test_peaks_and_traffic_are_read_from_committed_files():
+    b = _bench()
+    p = b.load_peaks()
+    assert p["hbm_gbs"] > 0 and p["bf16_tflops"] > 0
+    assert p["source"] == ("measured" if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json"))
+                           else "fallback")
+    names = [f[:-3] for f in os.listdir(os.path.join(ROOT, "profiles")) if f.endswith(".md")]
+    with_traffic = [n for n in names if b.load_traffic(n) is not None]
+    assert with_traffic and all(b.load_traffic(n) > 0 for n in with_traffic)
+    assert b.load_traffic("no_such_profile") is None
+
+
+def test_clock_samples_summary():
+    """Median SM clock and the throttle reasons seen Active (nvidia-smi's CSV
+    without units)."""
+    b = _bench()
+    lines = ["0, 1800, 1965, 700.1, 0x0, Not Active, Not Active, Not Active, Not Active",
+             "0, 1900, 1965, 900.3, 0x4, Not Active, Not Active, Not Active, Active",
+             "0, 1700, 1965, 950.0, 0x4, Not Active, Not Active, Not Active, Active",
+             "garbage"]
+    s = b.ClockSampler.summarise(lines)
+    assert s == {"sm_mhz": 1800.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"],
+                 "samples": 3}
