@@ -444,7 +444,7 @@ def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> Compi
 def _register_dirty_tracking(plan: CompiledPlan, g, ns):
     """Every node of the plan reports its invalidation (a set_ upstream) into
     plan.dirty_nodes (src/compiler.jl:126-131)."""
-    def mark(sym, plan=plan):
+    def mark(_g, sym, _ns, plan=plan):
         plan.dirty_nodes.add(sym)
     for sym in plan.order:
         nd = g.nodes[ns].get(sym)

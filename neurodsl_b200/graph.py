@@ -182,7 +182,7 @@ def _invalidate_downstream(g, sym, ns):
         if nd is not None:
             nd.valid = False
             if nd.on_change is not None:
-                nd.on_change(s)
+                nd.on_change(g, s, ns)     # the reference's (g, sym, ns) callback
         q.extend(cons.get(s, []))
 
 

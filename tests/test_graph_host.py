@@ -205,3 +205,15 @@ def test_defop_decorator_registers_an_op():
     with pytest.warns(UserWarning):
         z = G.demand(g, "z")
     torch.testing.assert_close(z, 2 * torch.arange(4.0).reshape(2, 2) + 1)
+
+
+def test_on_change_callback_gets_graph_symbol_and_namespace():
+    """A node's on_change callback fires when an upstream set_ invalidates it,
+    with the reference's (g, sym, ns) arguments (src/graph_api.jl:52-54)."""
+    g = host_graph()
+    G.set_(g, "x", torch.ones(2, 2))
+    G.addrule(g, G.GraphRule("y", ["x"], "identity"))
+    seen = []
+    g.nodes["default"]["y"].on_change = lambda gg, sym, ns: seen.append((gg, sym, ns))
+    G.set_(g, "x", torch.zeros(2, 2))
+    assert seen == [(g, "y", "default")]
