@@ -169,9 +169,15 @@ def _consumers(g, ns):
 
 
 def _invalidate_downstream(g, sym, ns):
-    """BFS invalidation of every node computed from `sym` (src/graph_api.jl:37-71)."""
+    """BFS from `sym` over its consumers and watchers (src/graph_api.jl:37-71):
+    every node reached is invalidated and its on_change callback called with
+    the reference's (g, sym, ns).  `sym` itself keeps its new value (valid)
+    but its callback fires too.  Unlike the reference, consumers that are
+    already invalid are still followed: a compiled plan's released
+    intermediates are invalid while the output computed from them is valid,
+    and must be recomputed."""
     cons = _consumers(g, ns)
-    q = deque(cons.get(sym, []))
+    q = deque([sym])
     seen = set()
     while q:
         s = q.popleft()
@@ -180,10 +186,19 @@ def _invalidate_downstream(g, sym, ns):
         seen.add(s)
         nd = g.nodes[ns].get(s)
         if nd is not None:
-            nd.valid = False
+            if s != sym:
+                nd.valid = False
             if nd.on_change is not None:
-                nd.on_change(g, s, ns)     # the reference's (g, sym, ns) callback
+                nd.on_change(g, s, ns)
+            q.extend(w for w in nd.watchers if w not in seen)
         q.extend(cons.get(s, []))
+
+
+def watch(g: NeuroGraph, observer: str, observed: str, namespace: Optional[str] = None):
+    """_watch!(g, observer, observed) (src/graph_api.jl:72-80): invalidating
+    `observed` invalidates `observer` too."""
+    ns = namespace or g.active_ns
+    g.nodes[ns][observed].watchers.append(observer)
 
 
 def set_(g: NeuroGraph, name: str, value, is_param: bool = False, namespace: Optional[str] = None,

@@ -217,3 +217,16 @@ def test_on_change_callback_gets_graph_symbol_and_namespace():
     g.nodes["default"]["y"].on_change = lambda gg, sym, ns: seen.append((gg, sym, ns))
     G.set_(g, "x", torch.zeros(2, 2))
     assert seen == [(g, "y", "default")]
+
+
+def test_watchers_are_invalidated_with_what_they_observe():
+    g = host_graph()
+    G.set_(g, "x", torch.ones(2, 2))
+    G.set_(g, "stats", torch.zeros(1))
+    G.addrule(g, G.GraphRule("y", ["x"], "identity"))
+    G.demand(g, "y")
+    G.watch(g, "stats", "y")
+    assert g.nodes["default"]["stats"].valid
+    G.set_(g, "x", torch.zeros(2, 2))
+    assert not g.nodes["default"]["y"].valid and not g.nodes["default"]["stats"].valid
+    assert g.nodes["default"]["x"].valid
