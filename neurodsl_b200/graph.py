@@ -14,6 +14,7 @@ the same op symbols, attrs, output-buffer ownership and CtxStore contents:
   topo_order!        src/graph_api.jl:163   topo_order(g)
   invalidate_all!    src/graph_api.jl:222   invalidate_all(g)
   activate! / namespaces / node / params    activate / namespaces / node / params
+  graph_summary  src/graph_api.jl:228       graph_summary
     src/graph_api.jl:9-10,146-150,225-226   (is_backpropable: src/types.jl:35)
   demand!(g, sym; ctx_store)                demand(g, sym, ctx_store=...)
     src/dispatch.jl:592-615
@@ -139,6 +140,20 @@ def activate(g: NeuroGraph, ns: str) -> NeuroGraph:
 
 def namespaces(g: NeuroGraph) -> List[str]:
     return list(g.nodes)
+
+
+def graph_summary(g: NeuroGraph) -> str:
+    """graph_summary(g) (src/graph_api.jl:228-237): the device and, per
+    namespace, the node, rule and parameter counts; printed and returned."""
+    dev = g.device.torch_device
+    lines = ["NeuroGraph — neurodsl_b200",
+             f"  Device    : {'B200 (cuda:%d)' % dev.index if dev.type == 'cuda' else dev.type.upper()}"]
+    for ns in namespaces(g):
+        n_p = sum(1 for nd in g.nodes[ns].values() if nd.is_param)
+        lines.append(f"  [:{ns}]  nodes={len(g.nodes[ns])}  rules={len(g.rules[ns])}  params={n_p}")
+    text = "\n".join(lines)
+    print(text)
+    return text
 
 
 def is_backpropable(nd: "GraphNode") -> bool:

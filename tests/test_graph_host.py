@@ -230,3 +230,13 @@ def test_watchers_are_invalidated_with_what_they_observe():
     G.set_(g, "x", torch.zeros(2, 2))
     assert not g.nodes["default"]["y"].valid and not g.nodes["default"]["stats"].valid
     assert g.nodes["default"]["x"].valid
+
+
+def test_graph_summary_counts_per_namespace(capsys):
+    g = host_graph()
+    G.set_(g, "x", torch.ones(2, 2))
+    G.set_(g, "W", torch.ones(2, 2), is_param=True)
+    G.addrule(g, G.GraphRule("y", ["x", "W"], "matmul"))
+    text = G.graph_summary(g)
+    assert "[:default]  nodes=3  rules=1  params=1" in text
+    assert "Device    : CPU" in text and text in capsys.readouterr().out
