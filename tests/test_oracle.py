@@ -210,3 +210,27 @@ def test_golden_layernorm(golden):
         y, mu, rs = oracle.layernorm(g[f"x{d}"], g[f"gamma{d}"], g[f"beta{d}"], eps=1e-5)
         np.testing.assert_allclose(y, g[f"y{d}"], atol=1e-6, rtol=1e-6)
         np.testing.assert_allclose(rs, g[f"rstd{d}"], rtol=1e-6)
+
+
+def test_golden_fixtures_regenerate_bit_for_bit(tmp_path, golden):
+    """The committed fixtures are what the committed generator and oracle
+    produce: tests/golden/make_golden.py, run into a scratch folder, gives
+    every array of every fixture bit for bit."""
+    import importlib.util
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location(
+        "make_golden", os.path.join(root, "tests", "golden", "make_golden.py"))
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    mg.OUT = str(tmp_path)
+    mg.main()
+    made = sorted(f[:-4] for f in os.listdir(tmp_path) if f.endswith(".npz"))
+    assert made == ["attn_causal_bhsd", "attn_noncausal_bhsd", "attn_ref_shape", "kv_decode",
+                    "layernorm", "linear_gelu"]
+    for name in made:
+        new = dict(np.load(os.path.join(tmp_path, name + ".npz")))
+        old = golden(name)
+        assert sorted(new) == sorted(old), name
+        for k in old:
+            np.testing.assert_array_equal(new[k], old[k], err_msg=f"{name}:{k}")
