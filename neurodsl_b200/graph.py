@@ -319,6 +319,8 @@ def _infer_output_shape(op: str, inputs, attrs):
         return tuple(inputs[0].shape)
     if op == "kv_decode_attn":
         return tuple(inputs[0].shape)
+    if op == "embedding":                                    # [E, idx]
+        return (inputs[1].numel(), inputs[0].shape[1])
     # the reference warns and falls back to the first input's shape (:93-96)
     warnings.warn(f"Shape inference non implémentée pour :{op}, utilisation de la forme du "
                   "premier argument")
@@ -493,6 +495,17 @@ def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, 
         s, e = attrs.get("start_col", 1), attrs.get("end_col", x.shape[1])
         output_buffer.copy_(x[:, s - 1:e])
         _store_ctx(ctx_store, out_sym, {"start_col": s, "end_col": e})
+        return output_buffer
+    if op == "embedding":
+        # rows idx[i] (1-based, as the reference's Julia indices) of the table
+        # E (vocab, d), src/dispatch.jl:476-491, gathered on the device where
+        # the reference copies through the host; ctx {idx, E_size}
+        E, idx = inputs[0], inputs[1]
+        rows = idx.reshape(-1).to(device=E.device, dtype=torch.int64) - 1
+        if rows.numel() and bool(((rows < 0) | (rows >= E.shape[0])).any()):
+            raise NeuroDSLError(2, f"[{out_sym}] embedding index outside 1..{E.shape[0]}")
+        torch.index_select(E, 0, rows, out=output_buffer)
+        _store_ctx(ctx_store, out_sym, {"idx": rows + 1, "E_size": tuple(E.shape)})
         return output_buffer
     if op == "hcat_heads":
         # the heads' (N, d_h) outputs side by side, src/dispatch.jl:349-361

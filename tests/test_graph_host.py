@@ -240,3 +240,21 @@ def test_graph_summary_counts_per_namespace(capsys):
     text = G.graph_summary(g)
     assert "[:default]  nodes=3  rules=1  params=1" in text
     assert "Device    : CPU" in text and text in capsys.readouterr().out
+
+
+def test_embedding_gathers_rows_by_one_based_index():
+    """:embedding (src/dispatch.jl:476-491): row idx[i] of E for each index,
+    Julia's 1-based numbering, indices given as Float32 node values like the
+    reference's; an index outside the table raises."""
+    g = host_graph()
+    E = torch.arange(12.0).reshape(4, 3)
+    G.set_(g, "E", E, is_param=True)
+    G.set_(g, "idx", torch.tensor([2.0, 4.0, 1.0, 2.0]))
+    G.addrule(g, G.GraphRule("emb", ["E", "idx"], "embedding"))
+    ctx = G.CtxStore()
+    out = G.demand(g, "emb", ctx_store=ctx)
+    torch.testing.assert_close(out, E[[1, 3, 0, 1]])
+    assert ctx["emb"]["E_size"] == (4, 3) and ctx["emb"]["idx"].tolist() == [2, 4, 1, 2]
+    G.set_(g, "idx", torch.tensor([5.0]))
+    with pytest.raises(NeuroDSLError):
+        G.demand(g, "emb")
