@@ -127,13 +127,16 @@ B200_RULES: List[RewriteRule] = [
     RewriteRule("naive_attention_to_flash", ("matmul", "scale_mask", "softmax", "matmul"),
                 "flash_attn", condition=_naive_attention_condition, cost_delta=0.70,
                 attrs={"causal": True}),
-    RewriteRule("layernorm_linear_fusion", ("layernorm", "linear"), "fused_layernorm_linear",
-                condition=_three_input_layernorm, cost_delta=0.40, attrs={"trans_b": True}),
-    RewriteRule("layernorm_matmul_fusion", ("layernorm", "matmul"), "fused_layernorm_linear",
+    # the reference's names (src/compiler_config.jl:154-172) keep their
+    # patterns; the :linear forms (weight (out, in), optional bias) are extra
+    RewriteRule("layernorm_linear_fusion", ("layernorm", "matmul"), "fused_layernorm_linear",
                 condition=_three_input_layernorm, cost_delta=0.40),
-    RewriteRule("linear_gelu_fusion", ("linear", "gelu"), "fused_linear_gelu", cost_delta=0.35,
+    RewriteRule("layernorm_linear_bias_fusion", ("layernorm", "linear"),
+                "fused_layernorm_linear", condition=_three_input_layernorm, cost_delta=0.40,
                 attrs={"trans_b": True}),
-    RewriteRule("matmul_gelu_fusion", ("matmul", "gelu"), "fused_linear_gelu", cost_delta=0.35),
+    RewriteRule("linear_gelu_fusion", ("matmul", "gelu"), "fused_linear_gelu", cost_delta=0.35),
+    RewriteRule("linear_bias_gelu_fusion", ("linear", "gelu"), "fused_linear_gelu",
+                cost_delta=0.35, attrs={"trans_b": True}),
     RewriteRule("linear_residual_fusion", ("linear", "add"), "fused_linear_residual",
                 cost_delta=0.30),
 ]

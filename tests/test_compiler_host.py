@@ -445,3 +445,15 @@ def test_memory_planning_like_the_reference(cpu_ops):
     torch.testing.assert_close(val, torch.relu(x @ w))
     assert L.demand_planned(g, "out", plan, pool) is val          # valid: no recompute
     assert L.pool_stats(pool)["allocs"] == 2
+
+
+def test_rule_names_shared_with_the_reference_keep_its_patterns():
+    """src/compiler_config.jl:154-172: linear_gelu_fusion is (:matmul, :gelu)
+    and layernorm_linear_fusion is (:layernorm, :matmul), so a caller that
+    selects or drops rules by name gets the same fusions."""
+    by_name = {r.name: r for r in C.B200_RULES}
+    assert by_name["linear_gelu_fusion"].pattern == ("matmul", "gelu")
+    assert by_name["linear_gelu_fusion"].result == "fused_linear_gelu"
+    assert by_name["layernorm_linear_fusion"].pattern == ("layernorm", "matmul")
+    assert by_name["layernorm_linear_fusion"].result == "fused_layernorm_linear"
+    assert len(by_name) == len(C.B200_RULES)
