@@ -42,6 +42,7 @@ chain and the namespace like the reference's.
 from __future__ import annotations
 
 import time
+import warnings
 from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, List, Optional, Set, Tuple
 
@@ -207,10 +208,30 @@ ALTERNATIVE_RULE_PAIRS: List[Tuple[str, str]] = [("sdpa_fusion", "flash_attentio
 
 @dataclass
 class CompilerConfig:
+    """The reference's CompilerConfig fields (src/compiler_config.jl:349-359)
+    plus `pooled`.  `budget` bounds the fusions one compilation applies;
+    `incremental=False` makes every recompilation a full one; `verify_rules`
+    warns for each applied rule not marked verified.  Only the GPU target and
+    the symbolic cost mode exist here; `inspect` keeps no e-graph (the
+    matching is direct) and is accepted for compatibility."""
     rules: List[RewriteRule] = field(default_factory=lambda: list(B200_RULES))
     training: bool = True
     pooled: bool = True      # run with the memory plan's buffer pool
     cost_fn: Callable = default_cost   # (op, shapes, rule_cost_delta=...) -> float
+    budget: int = 1000
+    target: str = "gpu"
+    incremental: bool = True
+    inspect: bool = False
+    cost_mode: str = "symbolic"
+    verify_rules: bool = False
+
+    def __post_init__(self):
+        if str(self.target).lstrip(":") != "gpu":
+            raise ValueError(f"target {self.target!r}: this library runs on the GPU only")
+        if str(self.cost_mode).lstrip(":") != "symbolic":
+            raise ValueError(f"cost_mode {self.cost_mode!r}: only the symbolic cost model exists")
+        if self.budget < 0:
+            raise ValueError("budget must be >= 0")
 
 
 @dataclass
@@ -418,6 +439,11 @@ def fold_multihead_attention(g, namespace=None) -> Dict[str, str]:
     return folded
 
 
+def _warn_unverified(config: CompilerConfig, rule: RewriteRule):
+    if config.verify_rules and not rule.verified:
+        warnings.warn(f"rewrite rule :{rule.name} is not verified")
+
+
 def _fold_allowed(training) -> bool:
     # the same training guard as the rewrite rules
     return not training or "flash_attention" in BACKWARD_SUPPORT
@@ -431,8 +457,11 @@ def compile(g, config: Optional[CompilerConfig] = None, namespace=None) -> Compi
     fused_ops: Dict[str, str] = {}
     matches = choose_cheapest_alternative(g, scan_graph(g, config.rules, ns), config.cost_fn, ns)
     for m in matches:
+        if len(fused_ops) >= config.budget:
+            break
         if _apply_fusion(g, ns, m.nodes, m.rule, training=config.training):
             fused_ops[m.nodes[-1]] = m.rule.result
+            _warn_unverified(config, m.rule)
     if _fold_allowed(config.training):
         fused_ops.update(fold_multihead_attention(g, ns))
     g._topo_cache[ns] = None
@@ -468,7 +497,7 @@ def recompile(plan: CompiledPlan, g) -> CompiledPlan:
     if not plan.is_dirty():
         return plan
     ns = plan.namespace
-    if len(g.nodes[ns]) != len(plan.order):
+    if not plan.config.incremental or len(g.nodes[ns]) != len(plan.order):
         fresh = compile(g, plan.config, namespace=ns)
         plan.order, plan.memory_plan = fresh.order, fresh.memory_plan
         plan.pool, plan.fused_ops = fresh.pool, fresh.fused_ops
@@ -489,6 +518,7 @@ def recompile(plan: CompiledPlan, g) -> CompiledPlan:
                 continue
             if _apply_fusion(g, ns, m.nodes, m.rule, training=plan.config.training):
                 plan.fused_ops[m.nodes[-1]] = m.rule.result
+                _warn_unverified(plan.config, m.rule)
         if _fold_allowed(plan.config.training):
             plan.fused_ops.update(fold_multihead_attention(g, ns))
         g._topo_cache[ns] = None

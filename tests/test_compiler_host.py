@@ -457,3 +457,35 @@ def test_rule_names_shared_with_the_reference_keep_its_patterns():
     assert by_name["layernorm_linear_fusion"].pattern == ("layernorm", "matmul")
     assert by_name["layernorm_linear_fusion"].result == "fused_layernorm_linear"
     assert len(by_name) == len(C.B200_RULES)
+
+
+def test_compiler_config_fields_of_the_reference():
+    """budget bounds the fusions applied, verify_rules warns for unverified
+    rules, only the GPU target and the symbolic cost mode are accepted."""
+    g = _graph(["x", "W1", "W2"])
+    _rule(g, "u", ["x", "W1"], "matmul")
+    _rule(g, "v", ["u"], "gelu")
+    _rule(g, "w", ["v", "W2"], "matmul")
+    _rule(g, "z", ["w"], "gelu")
+    assert C.compile(g, C.CompilerConfig(training=False, budget=1)).fused_ops == \
+        {"v": "fused_linear_gelu"}
+    g = _graph(["x", "W"])
+    _rule(g, "u", ["x", "W"], "matmul")
+    _rule(g, "v", ["u"], "gelu")
+    with pytest.warns(UserWarning, match="linear_gelu_fusion"):
+        C.compile(g, C.CompilerConfig(training=False, verify_rules=True))
+    with pytest.raises(ValueError):
+        C.CompilerConfig(target="cpu")
+    with pytest.raises(ValueError):
+        C.CompilerConfig(cost_mode="profiled")
+
+
+@_quiet_shapes
+def test_non_incremental_recompilation_is_a_full_compile(cpu_ops):
+    g = _chain()
+    plan = C.compile(g, C.CompilerConfig(rules=[_fusion()], training=False, incremental=False))
+    G.set_(g, "x", torch.randn(4, 4, generator=torch.Generator().manual_seed(5)), is_param=True)
+    out = plan(g, "z")
+    assert plan.n_recompiles == 1 and not C.is_dirty(plan)
+    ns = g.nodes["default"]
+    torch.testing.assert_close(out, torch.relu(ns["x"].value @ ns["W"].value + ns["b"].value))
