@@ -205,3 +205,23 @@ def test_matmul_trans_b_false_and_linear_alias():
     ref = A.astype(np.float64) @ B
     check(C, ref)
     check(Ct, ref)
+
+
+def test_embedding_op_on_the_device():
+    """:embedding gathers Float32 rows of E by 1-based indices on the device,
+    exactly; an index past the table raises."""
+    g_ = G()
+    rng = np.random.default_rng(21)
+    E = rng.standard_normal((50, 64)).astype(np.float32)
+    idx = np.array([3, 50, 1, 7, 7], np.float32)
+    g = g_.NeuroGraph()
+    g_.set_(g, "E", E, is_param=True)
+    g_.set_(g, "idx", idx)
+    g_.addrule(g, g_.GraphRule("emb", ["E", "idx"], "embedding"))
+    out = g_.demand(g, "emb")
+    assert out.is_cuda
+    np.testing.assert_array_equal(out.cpu().numpy(), E[idx.astype(np.int64) - 1])
+    from neurodsl_b200._lib import NeuroDSLError
+    g_.set_(g, "idx", np.array([51], np.float32))
+    with pytest.raises(NeuroDSLError):
+        g_.demand(g, "emb")
