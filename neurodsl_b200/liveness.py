@@ -112,6 +112,22 @@ class MemoryPlan:
     n_slots: int
     order: List[str] = field(default_factory=list)
 
+    def peak_live(self) -> int:
+        """Most nodes alive at one step of the order."""
+        return max((sum(1 for s in self.order if self.liveness[s].is_alive_at(t))
+                    for t in range(1, len(self.order) + 1)), default=0)
+
+    def __str__(self):
+        """The reference's summary of a plan (src/liveness.jl:172-185): nodes,
+        slots, peak of simultaneously live nodes, and the reduction against
+        one buffer per node."""
+        n = len(self.order)
+        return (f"MemoryPlan:\n  Nodes     : {n}\n"
+                f"  Slots     : {self.n_slots}  (distinct physical buffers)\n"
+                f"  Peak live : {self.peak_live()}  nodes at once\n"
+                f"  Reduction : -{100 * (1 - self.n_slots / max(1, n)):.0f}% vs naive "
+                "(1 buffer / node)")
+
 
 def plan_memory(g, namespace=None) -> MemoryPlan:
     ns = namespace or g.active_ns

@@ -489,3 +489,16 @@ def test_non_incremental_recompilation_is_a_full_compile(cpu_ops):
     assert plan.n_recompiles == 1 and not C.is_dirty(plan)
     ns = g.nodes["default"]
     torch.testing.assert_close(out, torch.relu(ns["x"].value @ ns["W"].value + ns["b"].value))
+
+
+def test_memory_plan_summary():
+    from neurodsl_b200 import liveness as L
+    g = _graph(["x", "W"])
+    _rule(g, "a", ["x", "W"], "matmul")
+    _rule(g, "b", ["a"], "gelu")
+    _rule(g, "c", ["b"], "gelu")
+    plan = L.plan_memory(g)
+    text = str(plan)
+    assert text.startswith("MemoryPlan:") and f"Slots     : {plan.n_slots}" in text
+    assert 1 <= plan.peak_live() <= len(plan.order)
+    assert f"Nodes     : {len(plan.order)}" in text and "Reduction : -" in text
