@@ -113,7 +113,25 @@ def _naive_attention_condition(g, chain, ns) -> bool:
     pv = producer(g, chain[3], ns)
     return (bool(qk.attrs.get("trans_b", False)) and len(qk.inputs) == 2
             and len(pv.inputs) == 2 and pv.inputs[0] == chain[2]
-            and not pv.attrs.get("trans_b", False))
+            and not pv.attrs.get("trans_b", False)
+            and _head_dim(g, chain, qk, ns) == FLASH_HEAD_DIM)
+
+
+# The attention kernels' head dimension: a rewrite onto :flash_attn or
+# :flash_attention only applies to heads of this width, so a graph with
+# other heads keeps its (GEMM-based) unfused form and still runs.
+FLASH_HEAD_DIM = 64
+
+
+def _head_dim(g, chain, qk, ns):
+    """The head width of a naive attention chain: the :scale_mask's d_head
+    attr, else the columns of Q's value when it is known, else None."""
+    sm = producer(g, chain[1], ns)
+    if "d_head" in sm.attrs:
+        return int(sm.attrs["d_head"])
+    nd = g.nodes[ns].get(qk.inputs[0])
+    v = None if nd is None else nd.value
+    return int(v.shape[1]) if v is not None and v.dim() == 2 else None
 
 
 def _three_input_layernorm(g, chain, ns) -> bool:
@@ -405,7 +423,7 @@ def _multihead_sources(g, ns, heads):
         if int(fa.attrs.get("d_head", D)) != D:
             return None
         dead[sym] = None
-    if D is None:
+    if D != FLASH_HEAD_DIM:
         return None
     return (full[0], full[1], full[2]), D, causal, list(dead)
 

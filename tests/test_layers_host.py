@@ -58,3 +58,16 @@ def test_multihead_layers_build_the_reference_graph_and_compile_to_one_launch(la
     assert plan.fused_ops["mha_concat"] == "flash_attention"
     assert not [s for s in g.rules["default"] if "_h" in s]
     assert g.rules["default"]["mha_output_out"].inputs == ["mha_concat", "mha_output_W"]
+
+
+@pytest.mark.parametrize("layer", [Ly.MultiHeadFlashAttention, Ly.MultiHeadAttention])
+def test_heads_the_kernels_do_not_take_stay_unfused(layer):
+    """test/test_layers.jl:23-29 builds MultiHeadAttention(16, 2): heads of 8.
+    The attention kernels take heads of 64 only, so compile leaves such a
+    layer as written (its GEMM-based ops run any head width)."""
+    g = G.NeuroGraph(device=_HostDevice())
+    G.set_(g, "x", torch.zeros(4, 16))
+    layer(16, 2)(g, "x", "mha", generator=torch.Generator().manual_seed(2))
+    before = {k: r.op for k, r in g.rules["default"].items()}
+    plan = C.compile(g, C.CompilerConfig(training=False))
+    assert plan.fused_ops == {} and {k: r.op for k, r in g.rules["default"].items()} == before
