@@ -24,6 +24,7 @@
 #include "layernorm.h"
 #include "model_ops.h"
 #include "tp_comm.h"
+#include "tma.h"
 
 namespace {
 // Device error word: one int per device (a __device__ variable exists once
@@ -33,20 +34,22 @@ __device__ int g_device_error = 0;
 
 namespace nd {
 int* device_error_word() {
-  // Several host threads may resolve the same device's address at once; they
-  // all obtain the same value, so atomic loads and stores keep the cache
-  // race-free without a lock.
-  static int* cached[64] = {};
+  // The address is cached per host thread and device, together with the id
+  // of the context it belongs to (a context torn down and created again
+  // reloads the variable, possibly elsewhere); a per-thread cache needs no
+  // lock on this per-launch path.
+  thread_local int* cached[64] = {};
+  thread_local unsigned long long cached_ctx[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  int* w = __atomic_load_n(&cached[dev], __ATOMIC_ACQUIRE);
-  if (w == nullptr) {
+  const unsigned long long ctx = current_context_id();
+  if (cached[dev] == nullptr || cached_ctx[dev] != ctx) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
-    w = static_cast<int*>(p);
-    __atomic_store_n(&cached[dev], w, __ATOMIC_RELEASE);
+    cached[dev] = static_cast<int*>(p);
+    cached_ctx[dev] = ctx;
   }
-  return w;
+  return cached[dev];
 }
 namespace {
 thread_local bool t_pdl = false;
@@ -107,7 +110,9 @@ int check_current_device(int* dev_out) {
 // Library-owned decode scratch, one buffer per device, grown on demand and
 // zero-filled when (re)allocated.  Growth synchronises the device, so a
 // caller that captures decode into a CUDA graph makes one uncaptured call of
-// the largest size first.
+// the largest size first.  The zero fill runs on the caller's stream and is
+// waited for before the call returns, so a kernel on any stream that uses the
+// buffer afterwards sees the tickets at zero.
 struct OwnedWorkspace {
   void* ptr = nullptr;
   size_t bytes = 0;
@@ -115,7 +120,7 @@ struct OwnedWorkspace {
 OwnedWorkspace g_ws[kMaxDevices];
 std::mutex g_ws_mu;
 
-int owned_workspace(int dev, size_t need, void** out) {
+int owned_workspace(int dev, size_t need, cudaStream_t stream, void** out) {
   std::lock_guard<std::mutex> lk(g_ws_mu);
   OwnedWorkspace& w = g_ws[dev];
   if (w.bytes < need) {
@@ -128,8 +133,9 @@ int owned_workspace(int dev, size_t need, void** out) {
     size_t sz = need < (1u << 20) ? (1u << 20) : need;
     cudaError_t e = cudaMalloc(&w.ptr, sz);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc (decode workspace)");
-    e = cudaMemset(w.ptr, 0, sz);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset (decode workspace)");
+    e = cudaMemsetAsync(w.ptr, 0, sz, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync (decode workspace)");
     w.bytes = sz;
   }
   *out = w.ptr;
@@ -208,7 +214,7 @@ static int kv_decode_impl(const char* fn, void* stream, const void* q, const voi
   void* ws = workspace;
   if (need > 0) {
     if (ws == nullptr) {
-      rc = owned_workspace(dev, need, &ws);
+      rc = owned_workspace(dev, need, static_cast<cudaStream_t>(stream), &ws);
       if (rc) return rc;
     } else if (workspace_bytes < need) {
       return fail(ND_ERR_WORKSPACE, "%s: workspace %zu bytes < %zu needed", fn, workspace_bytes, need);

@@ -20,6 +20,7 @@
 
 #include "kv_decode.h"
 #include "launch.cuh"
+#include "tma.h"
 
 namespace nd {
 
@@ -95,16 +96,17 @@ __global__ void __launch_bounds__(kThreads)
   const uint4* vbase = reinterpret_cast<const uint4*>(v_cache + head_off);
   const int key0 = chunk * kChunk + warp * kKeysPerWarp + grp;
 
-  // Issue every K/V load of this thread before any arithmetic.  Under
+  // Issue every K/V load of keys below L-1 before any arithmetic.  Under
   // programmatic dependent launch they go out before the previous kernel (the
   // one producing q, k_new and v_new) has finished: keys below L-1 were
-  // written by earlier, finished work, and the key at L-1, whose load may see
-  // an old value, is replaced by k_new / v_new below.
+  // written by earlier, finished work.  The key at L-1 may be the one the
+  // previous kernel is writing (a projection epilogue that fills the cache),
+  // so it is read only after pdl_wait(), from k_new / v_new or the cache.
   uint4 kr[kIters], vr[kIters];
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
     const int key = key0 + it * 4;
-    if (key < L) {
+    if (key < L - 1) {
       kr[it] = ld_stream(kbase + static_cast<size_t>(key) * (kD / 8) + sub);
       vr[it] = ld_stream(vbase + static_cast<size_t>(key) * (kD / 8) + sub);
     } else {
@@ -126,18 +128,25 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = 0; i < 8; ++i) qf[i] *= scale_log2;
   }
 
-  // Fused append: the token at L-1 comes from k_new / v_new and is written
-  // into the caches by the CTA that owns that key.
-  if (k_new != nullptr) {
+  // The key at L-1: with k_new / v_new it comes from them and is written into
+  // the caches by the CTA that owns that key (the fused append); without them
+  // it is read from the caches (coherent loads: the previous kernel may have
+  // written it).
 #pragma unroll
-    for (int it = 0; it < kIters; ++it) {
-      if (key0 + it * 4 == L - 1) {
+  for (int it = 0; it < kIters; ++it) {
+    if (key0 + it * 4 == L - 1) {
+      uint4* kdst = reinterpret_cast<uint4*>(k_cache + head_off) + static_cast<size_t>(L - 1) * (kD / 8) + sub;
+      uint4* vdst = reinterpret_cast<uint4*>(v_cache + head_off) + static_cast<size_t>(L - 1) * (kD / 8) + sub;
+      if (k_new != nullptr) {
         const uint4 kn = *reinterpret_cast<const uint4*>(k_new + qoff + sub * 8);
         const uint4 vn = *reinterpret_cast<const uint4*>(v_new + qoff + sub * 8);
         kr[it] = kn;
         vr[it] = vn;
-        reinterpret_cast<uint4*>(k_cache + head_off)[static_cast<size_t>(L - 1) * (kD / 8) + sub] = kn;
-        reinterpret_cast<uint4*>(v_cache + head_off)[static_cast<size_t>(L - 1) * (kD / 8) + sub] = vn;
+        *kdst = kn;
+        *vdst = vn;
+      } else {
+        kr[it] = __ldcg(kdst);
+        vr[it] = __ldcg(vdst);
       }
     }
   }
@@ -285,24 +294,29 @@ static __device__ __align__(256) unsigned char g_decode_static_scratch[kDecodeSt
 namespace {
 constexpr int kScratchMaxDevices = 64;
 void* g_static_scratch_addr[kScratchMaxDevices] = {};
+unsigned long long g_static_scratch_ctx[kScratchMaxDevices] = {};
 std::mutex g_static_scratch_mu;
 }  // namespace
 
 cudaError_t kv_decode_static_scratch(int device, cudaStream_t stream, void** ptr) {
   if (device < 0 || device >= kScratchMaxDevices) return cudaErrorInvalidDevice;
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lk(g_static_scratch_mu);
-  if (g_static_scratch_addr[device] == nullptr) {
-    // Set-up, once per device, with `device` current (the caller's current
-    // device): resolve this device's copy of the array and clear its ticket
-    // region, which must start at zero (every call then returns the tickets it
-    // used to zero).  The clear is ordered on the caller's stream before the
-    // first kernel that reads the tickets.
+  if (g_static_scratch_addr[device] == nullptr || g_static_scratch_ctx[device] != ctx) {
+    // Set-up, once per device (and again if the device's context was torn
+    // down and recreated since, which reloads the array at a possibly new
+    // address), with `device` current (the caller's current device): resolve
+    // this device's copy of the array and clear its ticket region, which must
+    // start at zero (every call then returns the tickets it used to zero).
+    // The clear is ordered on the caller's stream before the first kernel
+    // that reads the tickets.
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_decode_static_scratch);
     if (e != cudaSuccess) return e;
     e = cudaMemsetAsync(p, 0, kv_decode_partials_offset(), stream);
     if (e != cudaSuccess) return e;
     g_static_scratch_addr[device] = p;
+    g_static_scratch_ctx[device] = ctx;
   }
   *ptr = g_static_scratch_addr[device];
   return cudaSuccess;

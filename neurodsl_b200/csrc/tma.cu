@@ -24,7 +24,34 @@ void load_encode() {
     g_encode_status = cudaErrorSymbolNotFound;
   if (g_encode_status == cudaSuccess) g_encode = reinterpret_cast<EncodeTiledFn>(fn);
 }
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+CtxGetCurrentFn g_ctx_current = nullptr;
+CtxGetIdFn g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
+
+void load_ctx() {
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess && q == cudaDriverEntryPointSuccess)
+    g_ctx_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  fn = nullptr;
+  if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &fn, 12000, cudaEnableDefault, &q) ==
+          cudaSuccess && q == cudaDriverEntryPointSuccess)
+    g_ctx_id = reinterpret_cast<CtxGetIdFn>(fn);
+}
 }  // namespace
+
+unsigned long long current_context_id() {
+  std::call_once(g_ctx_once, load_ctx);
+  if (g_ctx_current == nullptr || g_ctx_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  unsigned long long id = 0;
+  if (g_ctx_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 cudaError_t make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank,
                                  const uint64_t* dims, const uint64_t* strides_bytes,

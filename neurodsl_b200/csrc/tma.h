@@ -16,4 +16,11 @@ cudaError_t make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank,
                                  const uint64_t* dims, const uint64_t* strides_bytes,
                                  const uint32_t* box, const char** err_msg);
 
+// Unique id of the calling thread's current CUDA context (cuCtxGetId through
+// the driver entry point), or 0 when it cannot be read.  Device addresses of
+// the library's __device__ variables are valid for one context only; callers
+// that cache such an address compare this id to notice that the context was
+// torn down and created again (cudaDeviceReset, primary-context release).
+unsigned long long current_context_id();
+
 }  // namespace nd

@@ -82,7 +82,13 @@ def compute_liveness(g, namespace=None) -> Dict[str, LivenessInterval]:
     live = {}
     for s in order:
         nd = g.nodes[ns].get(s)
-        lu = n if (nd is not None and nd.is_param) else last[s]
+        lu = last[s]
+        # parameters live for the whole pass; a backpropagable (Quantom) node's
+        # forward value is read by the backward pass, so it lives to the end as
+        # well (src/liveness.jl:101-108) — in inference its buffer goes back to
+        # the pool at the last step; Datom intermediates end at their last reader
+        if nd is not None and (nd.is_param or G.is_backpropable(nd)):
+            lu = n
         live[s] = LivenessInterval(idx[s], lu)
     return live
 

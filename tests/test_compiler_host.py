@@ -128,15 +128,38 @@ def test_failing_condition_makes_rule_inapplicable():
 
 # ------------------------------------------------------------ memory plan ---
 
-def test_liveness_and_slots_of_a_chain():
-    """x -> a -> b -> c, plus d = f(a, c): a lives until d; b's slot is free
-    again when c starts only if b's last use is before c's first step."""
-    from neurodsl_b200 import liveness as L
+def _atom_chain(atom):
     g = _graph(["x", "W"])
-    _rule(g, "a", ["x", "W"], "matmul")
-    _rule(g, "b", ["a"], "gelu")
-    _rule(g, "c", ["b"], "gelu")
-    _rule(g, "d", ["a", "c"], "add")
+    for out, ins, op in (("a", ["x", "W"], "matmul"), ("b", ["a"], "gelu"),
+                         ("c", ["b"], "gelu"), ("d", ["a", "c"], "add")):
+        G.addrule(g, G.GraphRule(out, ins, op, atom_type=atom))
+    return g
+
+
+def test_liveness_of_a_backpropagable_chain_extends_to_the_end():
+    """src/liveness.jl:101-108: parameters and backpropagable (Quantom, the
+    default atom type) nodes live to the last step of the order, whatever
+    their last reader."""
+    from neurodsl_b200 import liveness as L
+    g = _atom_chain(G.Quantom)
+    order = G.topo_order(g)
+    n = len(order)
+    live = L.compute_liveness(g)
+    pos = {s: i + 1 for i, s in enumerate(order)}
+    for s in ("a", "b", "c", "d"):
+        assert live[s] == L.LivenessInterval(pos[s], n), s
+    assert live["W"].last_use == n
+    # every intermediate alive at once: one slot each
+    slot = L.greedy_interval_coloring(live, order)
+    assert len({slot[s] for s in ("a", "b", "c", "d")}) == 4
+
+
+def test_liveness_and_slots_of_a_chain():
+    """Datom chain x -> a -> b -> c, plus d = f(a, c): a lives until d; b's
+    slot is free again when c starts only if b's last use is before c's first
+    step."""
+    from neurodsl_b200 import liveness as L
+    g = _atom_chain(G.Datom)
     order = G.topo_order(g)
     live = L.compute_liveness(g)
     pos = {s: i + 1 for i, s in enumerate(order)}

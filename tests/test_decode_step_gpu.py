@@ -169,6 +169,48 @@ def test_pdl_changes_no_result(graph):
     assert ops.device_error() == 0
 
 
+def test_pdl_decode_reads_the_cache_row_the_projection_just_wrote():
+    """With programmatic dependent launch on, a QKV projection of 64 rows (the
+    tensor-core path) whose epilogue writes cache row L-1 (nd_gemm_qkv_cache,
+    one token per sequence) is followed by decode attention without
+    k_new / v_new, which must read that row only after the projection has
+    finished: outputs and caches identical with PDL on and off, and the
+    output within the decode tolerance of the oracle."""
+    ops = _ops()
+    B, H, K, L0, L_max = 64, 12, 768, 1000, 1024
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    A = torch.randn(B, K, device="cuda", generator=gen).bfloat16()
+    W = (0.05 * torch.randn(3 * H * 64, K, device="cuda", generator=gen)).bfloat16()
+    bias = torch.zeros(3 * H * 64, device="cuda")
+    q = torch.randn(B, H, 64, device="cuda", generator=gen).bfloat16()
+    kc0 = torch.randn(B, H, L_max, 64, device="cuda", generator=gen).bfloat16()
+    vc0 = torch.randn(B, H, L_max, 64, device="cuda", generator=gen).bfloat16()
+    runs = []
+    for pdl in (False, True):
+        kc, vc = kc0.clone(), vc0.clone()
+        qkv = torch.empty(B, 3 * H * 64, device="cuda", dtype=torch.bfloat16)
+        outs = []
+        torch.cuda.synchronize()
+        with ops.pdl(pdl):
+            for L in range(L0, L0 + 8):
+                ops.linear_qkv_cache(A, W, bias, qkv, kc, vc, B, 1, pos0=L - 1)
+                o, _ = ops.kv_decode_attn(q, kc, vc, L)
+                outs.append(o.clone())
+        torch.cuda.synchronize()
+        runs.append((outs, kc, vc))
+    assert ops.set_pdl(False) is False
+    for a, b in zip(runs[0][0], runs[1][0]):
+        assert torch.equal(a, b)
+    assert torch.equal(runs[0][1], runs[1][1]) and torch.equal(runs[0][2], runs[1][2])
+    L = L0 + 7
+    ref, _ = oracle.kv_decode(q.float().cpu().numpy(), runs[1][1].float().cpu().numpy(),
+                              runs[1][2].float().cpu().numpy(), L)
+    got = runs[1][0][-1].float().cpu().numpy()
+    assert np.abs(got - ref).max() <= 2e-2
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-2
+    assert ops.device_error() == 0
+
+
 def test_model_decode_same_with_and_without_pdl():
     from neurodsl_b200.model import GPT, GPTConfig
     cfg = GPTConfig(n_layer=3, d_model=256, n_head=4, d_ff=1024, vocab=3001, n_pos=256)
