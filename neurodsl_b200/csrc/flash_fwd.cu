@@ -9,34 +9,58 @@
 // Persistent CTAs (one per SM) loop over work items of 256 query rows of one
 // head, taken heaviest first in alternating-direction rounds.  An item is two
 // 128-row query tiles sharing one stream of K/V tiles (128 keys each); Q is
-// double-buffered and the K/V ring runs on across items, so the next item's
-// loads overlap the current item's tail.  Warp roles (kHalves = 1, 384
+// double-buffered and the K/V ring runs on across items.  Warp roles (384
 // threads):
 //   warps 0..3   softmax of query tile 0 (thread = row = TMEM lane)
 //   warps 4..7   softmax of query tile 1
-//   warp 8       TMA producer: Q0/Q1 per item, then K/V tiles (kStages ring)
-//   warp 9       TMEM allocator + single-thread UMMA issuer
-//   warps 10, 11 idle (they complete the control warpgroup)
-// With kHalves = 2 every score row is split over two warpgroups that combine
-// their row maxima through shared memory (more warps to hide latency); on
-// B200 that loses to one warpgroup per tile because the exponential unit,
-// not latency, bounds the softmax, so kHalves = 1 is the configuration built.
+//   warp 8       TMA producer: K/V tiles (kStages ring); the next item's Q as
+//                soon as its buffer is free
+//   warp 9       TMEM allocator + UMMA issuer of tile 0 (one thread)
+//   warp 10      UMMA issuer of tile 1 (one thread)
+//   warp 11      idle (it completes the control warpgroup)
 // TMEM (512 columns), per tile i at base 256·i: S_i [0,128) fp32 scores,
 // P_i [128,192) packed bf16 probabilities, O_i [192,256) fp32 accumulator.
-// Because P has its own columns, S_i(j+1) = Q_i·K_{j+1}ᵀ is issued as soon as
-// softmax i has read S_i(j) (barrier s_free), so the tensor core computes the
-// next scores while the softmax computes exponentials.  O_i += P_i·V_j reads
-// P_i straight from tensor memory (A operand in TMEM, V an MN-major
-// shared-memory operand).
-// The running max is raised only when a row's max grows by more than 8
-// (log2 units); O and l share the stale offset, so the final O/l is exact.
+//
+// Each tile has its own UMMA issuer thread, so the tiles proceed
+// independently (each issuer blocks only on its own tile's barriers): S_i(k+1)
+// = Q_i·K_{k+1}ᵀ is issued once softmax i has copied S_i(k) into registers,
+// O_i (+)= P_i(k)·V_k once softmax i has written P_i(k), across item
+// boundaries too, so a tile that finishes an item early starts the next one
+// while the other tile finishes.  P_i is the A operand from tensor memory, V
+// an MN-major shared-memory operand.
+//
+// Softmax (per row, per K/V tile, in two halves of 64 keys): the half's max
+// is taken, the offset m (log2 units) raised if the max passed it by more
+// than 8, then the half's exponentials are computed against m; the second
+// half's max is independent of the first half's exponentials, so the two
+// overlap.  Raising the offset (always at a row's first half, rarely after)
+// multiplies l, O and the P already stored by 2^(old - new).  O and l share
+// the offset, so the final O/l is exact; the reported m is the true row max.  A row's output (O/l, lse, m) is
+// written during the first tile of its next item, before that item's first
+// P·V overwrites O, so no warp waits for the last P·V of an item.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <limits.h>
 #include <stdint.h>
 
 #include "flash_fwd.h"
 #include "ptx.cuh"
 #include "tma.h"
+
+// Tuning switches (compile-time): how many of every 8 score pairs of an
+// unmasked tile take the FMA-pipe polynomial exp2 instead of the exponential
+// unit, and whether probabilities are packed to bf16 with the conversion
+// instruction (1) or with integer rounding (0).
+#ifndef ND_FLASH_POLY_PAIRS
+#define ND_FLASH_POLY_PAIRS 0
+#endif
+#ifndef ND_FLASH_PACK_CVT
+#define ND_FLASH_PACK_CVT 1
+#endif
+// K/V ring depth (stages of 32 KB).
+#ifndef ND_FLASH_STAGES
+#define ND_FLASH_STAGES 3
+#endif
 
 namespace nd {
 namespace {
@@ -46,21 +70,19 @@ constexpr int kTiles = 2;              // query tiles per CTA
 constexpr int kRowsPerCta = kBM * kTiles;
 constexpr int kBN = 128;               // keys per K/V tile
 constexpr int kD = 64;
-constexpr int kStages = 3;
-constexpr int kHalves = 1;             // warpgroups sharing one score row (1 or 2)
-constexpr int kHalfCols = kBN / kHalves;   // score columns per softmax thread
-constexpr int kOutCols = kD / kHalves;     // output columns per softmax thread
-constexpr int kSoftmaxThreads = 128 * kTiles * kHalves;
-constexpr int kThreadsPerTile = 128 * kHalves;   // arrivals per softmax barrier
+constexpr int kStages = ND_FLASH_STAGES;
+constexpr int kSoftmaxThreads = 128 * kTiles;
 constexpr int kThreads = kSoftmaxThreads + 128;  // + one control warpgroup
 constexpr int kWarpProducer = kSoftmaxThreads / 32;
 constexpr int kWarpMma = kWarpProducer + 1;
-// Register split.  One half (384 threads): launch gives 168 per thread
-// (64512 total), control 72 + softmax 216: 128 x 72 + 256 x 216 = 64512.
-// Two halves (640 threads): 96 per thread (61440), 128 x 32 + 512 x 112.
+constexpr int kPolyPairs = ND_FLASH_POLY_PAIRS;
+constexpr bool kPackCvt = ND_FLASH_PACK_CVT != 0;
+static_assert(kPolyPairs >= 0 && kPolyPairs <= 8, "pairs out of 8");
+// Register split: launch gives 168 per thread (64512 total); control 72 +
+// softmax 216: 128 x 72 + 256 x 216 = 64512.
 constexpr uint32_t kLaunchRegs = (65536 / kThreads) & ~7u;
-constexpr uint32_t kRegsControl = kHalves == 1 ? 72 : 32;
-constexpr uint32_t kRegsSoftmax = kHalves == 1 ? 216 : 112;
+constexpr uint32_t kRegsControl = 72;
+constexpr uint32_t kRegsSoftmax = 216;
 static_assert(128 * kRegsControl + kSoftmaxThreads * kRegsSoftmax <= kThreads * kLaunchRegs,
               "register split exceeds the launch budget");
 constexpr uint32_t kTileBytes = kBM * kD * 2;    // 16 KB (one Q, K or V tile)
@@ -77,45 +99,45 @@ constexpr float kRescaleThreshold = 8.0f;
 constexpr uint32_t kOffQ = 0;                                   // 2 buffers x 2 x 16 KB
 constexpr uint32_t kOffK = kOffQ + 2 * kTiles * kTileBytes;
 constexpr uint32_t kOffV = kOffK + kStages * kTileBytes;
-constexpr uint32_t kOffBar = kOffV + kStages * kTileBytes;
-constexpr uint32_t kOffX = kOffBar + 256;                       // row-max / row-sum exchange
-constexpr uint32_t kSmemBytes = kOffX + 8192 + 1024;            // + alignment slack
-
-// Partner exchange between the two column halves of a score row: partial
-// maxima (double-buffered by iteration parity) and the final row sums.
-struct Exchange {
-  float max_part[2][kTiles][kHalves][kBM];
-  float sum_part[kTiles][kHalves][kBM];
-};
-static_assert(sizeof(Exchange) <= 8192, "exchange area");
+// per softmax warp, its 32 finished rows staged for a TMA tensor store
+// (bf16: one 32 x 128 B box; fp32: two, one per 32 columns)
+constexpr uint32_t kStageBytesWarp = 8192;
+constexpr uint32_t kOffStage = kOffV + kStages * kTileBytes;
+constexpr uint32_t kOffBar = kOffStage + (kSoftmaxThreads / 32) * kStageBytesWarp;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;           // + alignment slack
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(kBM, kBN, false, false);
 constexpr uint32_t kIdescO = idesc_bf16_f32(kBM, kD, false, true);
 
 struct Bars {
   uint64_t q_full[2];        // Q tiles of item n land in buffer n & 1
-  uint64_t q_empty[2];       // every S of that item has read the buffer
+  uint64_t q_empty[2];       // every S of that item has read the buffer (both issuers)
   uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t s_full[kTiles];   // S_i(j) written (UMMA commit)
-  uint64_t s_free[kTiles];   // S_i(j) read into registers (256 softmax threads)
-  uint64_t p_full[kTiles];   // P_i(j) written and O_i rescaled (256 softmax threads)
-  uint64_t o_done[kTiles];   // O_i += P_i(j)·V_j complete (UMMA commit)
-  uint64_t drained;
+  uint64_t kv_empty[kStages];  // both issuers are done with the stage
+  uint64_t s_full[kTiles];   // S_i(k) written (UMMA commit)
+  uint64_t s_free[kTiles];   // S_i(k) read into registers (128 softmax threads)
+  uint64_t p_full[kTiles];   // P_i(k) written, O_i rescaled and read out (128 threads)
+  uint64_t o_done[kTiles];   // O_i += P_i(k)·V_k complete (UMMA commit)
+  uint64_t drained[kTiles];
   uint32_t tmem_base;
   int abort_flag;
 };
+static_assert(sizeof(Bars) <= 256, "barrier area");
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 
 __host__ __device__ constexpr int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
-// bf16x2 pack of two non-negative finite floats on the integer pipe: round to
-// nearest (halfway cases up) by adding half an output ulp to the fp32 bits,
-// then keep the high halves.  The conversion instruction would run on the
-// same pipe as the exponentials; these three integer ops do not.
-__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
-  const uint32_t a = __float_as_uint(lo) + 0x8000u;
-  const uint32_t b = __float_as_uint(hi) + 0x8000u;
-  return __byte_perm(a, b, 0x7632);
+// bf16x2 pack of two non-negative finite floats: the conversion instruction
+// (round to nearest even), or integer rounding on the ALU (halfway cases up:
+// add half an output ulp to the fp32 bits, keep the high halves).
+__device__ __forceinline__ uint32_t pack_p(float lo, float hi) {
+  if constexpr (kPackCvt) {
+    return pack_bf16x2(lo, hi);
+  } else {
+    const uint32_t a = __float_as_uint(lo) + 0x8000u;
+    const uint32_t b = __float_as_uint(hi) + 0x8000u;
+    return __byte_perm(a, b, 0x7632);
+  }
 }
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -135,45 +157,79 @@ constexpr float kExpC1 = 0.69326097f;
 constexpr float kExpC2 = 0.24261113f;
 constexpr float kExpC3 = 0.05517167f;
 constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
-// Pairs out of every 8 whose exponentials use the polynomial.  Measured on
-// B200 at head_dim 64 the softmax is bound by instruction issue and latency,
-// not by the exponential unit (which sustains 16/clk/SM), so moving work to
-// the FMA pipe only adds instructions: 0 is the fastest setting.
-constexpr int kPolyPairsPer8 = 0;
 
-// Probabilities for 2·kHalfCols/2 scores: p = 2^(s·scale - m) packed to bf16
-// in pk, row-sum partials accumulated in acc (four f32x2 chains).
-template <int kPoly>
-__device__ __forceinline__ void exp2_pairs(const float* sv, uint64_t scale2, uint64_t negm2,
-                                           uint32_t* pk, uint64_t* acc) {
+__device__ __forceinline__ void poly_exp2_pair(float x0, float x1, float& p0, float& p1) {
   const uint64_t magic2 = f2_pack(kRoundMagic, kRoundMagic);
-  const uint64_t c0 = f2_pack(kExpC0, kExpC0), c1 = f2_pack(kExpC1, kExpC1);
-  const uint64_t c2 = f2_pack(kExpC2, kExpC2), c3 = f2_pack(kExpC3, kExpC3);
+  const uint64_t x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t2 = f2_add(x2, magic2);                 // magic + round(x)
+  const uint64_t fr = f2_sub(x2, f2_sub(t2, magic2));     // x - round(x)
+  uint64_t pp = f2_fma(fr, f2_pack(kExpC3, kExpC3), f2_pack(kExpC2, kExpC2));
+  pp = f2_fma(pp, fr, f2_pack(kExpC1, kExpC1));
+  pp = f2_fma(pp, fr, f2_pack(kExpC0, kExpC0));
+  float t0, t1;
+  f2_unpack(t2, t0, t1);
+  f2_unpack(pp, p0, p1);
+  // the low bits of t hold round(x); shifting by 23 drops the magic's bits
+  p0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Probabilities of the score columns [C0, C1) of one row: p = 2^(s·scale - m)
+// packed to bf16 pairs in pk[(c - C0) / 2], row-sum partials in acc (four
+// f32x2 chains).  kPoly of every 8 pairs use the FMA-pipe polynomial.
+template <int C0, int C1, int kPoly>
+__device__ __forceinline__ void exp_span(const float* sv, uint64_t scale2, uint64_t negm2,
+                                         uint32_t* pk, uint64_t* acc) {
 #pragma unroll
-  for (int c = 0; c < kHalfCols; c += 2) {
+  for (int c = C0; c < C1; c += 2) {
     const int q = c >> 1;
     float x0, x1, p0, p1;
     f2_unpack(f2_fma(f2_pack(sv[c], sv[c + 1]), scale2, negm2), x0, x1);
     if ((q & 7) < kPoly) {
-      const uint64_t x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
-      const uint64_t t2 = f2_add(x2, magic2);         // magic + round(x)
-      const uint64_t f2 = f2_add(x2, f2_sub(magic2, t2));  // x - round(x)
-      uint64_t pp = f2_fma(f2, c3, c2);
-      pp = f2_fma(pp, f2, c1);
-      pp = f2_fma(pp, f2, c0);
-      float t0, t1;
-      f2_unpack(t2, t0, t1);
-      f2_unpack(pp, p0, p1);
-      // low bits of t hold round(x); shifting by 23 drops the magic's bits
-      p0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-      p1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+      poly_exp2_pair(x0, x1, p0, p1);
     } else {
       p0 = fast_exp2(x0);
       p1 = fast_exp2(x1);
     }
     acc[q & 3] = f2_add(acc[q & 3], f2_pack(p0, p1));
-    pk[q] = pack_bf16x2_int(p0, p1);
+    pk[(c - C0) >> 1] = pack_p(p0, p1);
   }
+}
+
+// The same with the polynomial switched off in a masked tile (masked keys
+// must give exactly 0, which the exponential unit's 2^-inf does).
+template <int C0, int C1>
+__device__ __forceinline__ void exp_cols(bool masked_tile, const float* sv, uint64_t scale2,
+                                         uint64_t negm2, uint32_t* pk, uint64_t* acc) {
+  if constexpr (kPolyPairs == 0) {
+    exp_span<C0, C1, 0>(sv, scale2, negm2, pk, acc);
+  } else {
+    if (masked_tile)
+      exp_span<C0, C1, 0>(sv, scale2, negm2, pk, acc);
+    else
+      exp_span<C0, C1, kPolyPairs>(sv, scale2, negm2, pk, acc);
+  }
+}
+
+// Max of the score columns [C0, C0 + 64) of one row (four 3-input chains).
+template <int C0>
+__device__ __forceinline__ float half_max(const float* sv) {
+  float m0 = fmaxf(sv[C0], sv[C0 + 1]), m1 = fmaxf(sv[C0 + 2], sv[C0 + 3]);
+  float m2 = fmaxf(sv[C0 + 4], sv[C0 + 5]), m3 = fmaxf(sv[C0 + 6], sv[C0 + 7]);
+#pragma unroll
+  for (int c = C0 + 8; c < C0 + 64; c += 8) {
+    m0 = fmax3(m0, sv[c], sv[c + 1]);
+    m1 = fmax3(m1, sv[c + 2], sv[c + 3]);
+    m2 = fmax3(m2, sv[c + 4], sv[c + 5]);
+    m3 = fmax3(m3, sv[c + 6], sv[c + 7]);
+  }
+  return fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+}
+
+__device__ __forceinline__ float f2_sum4(const uint64_t* acc) {
+  float a0, a1;
+  f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), a0, a1);
+  return a0 + a1;
 }
 
 // One unit of work: 256 query rows (two tiles) of one (batch, head).
@@ -207,7 +263,7 @@ struct FlashLayout {
   int H;                 // heads; bh = b * H + h
   int q_token_major;     // Q map dims {64, H, S, B}
   int kv_token_major;    // K and V maps dims {64, H, S, B}
-  long long o_s, o_h, o_b;  // output element strides of a row, a head, a batch
+  int o_token_major;     // O map dims {64|32, H, S, B}
 };
 
 // 128 rows starting at `row` of head h, batch b, into one shared tile.
@@ -226,14 +282,28 @@ __device__ __forceinline__ int item_of(int n, int cta, int grid) {
   return n * grid + ((n & 1) ? (grid - 1 - cta) : cta);
 }
 
+// Position of one tile's UMMA stream (S products or P·V products) in this
+// CTA's item sequence: item n, K/V tile j of that item, ring position of the
+// item's first K/V tile, and the item's tile counts (nkv = 0: no more items).
+struct Cursor {
+  int n, j, base, nkv, total;
+};
+
+// A row whose output is still to be written (the previous item's).
+struct PendingRow {
+  float l, m_used, m_true;
+  int q_idx, bh;
+  bool valid;
+};
+
 // kStrided: Q/K/V through 4-D maps and O through FlashLayout strides; the
 // contiguous head-major case keeps 3-D maps {64, S, B·H} and bh·S row offsets.
 template <bool kCausal, bool kOutF32, bool kStrided>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_k,
-                     const __grid_constant__ CUtensorMap tm_v, void* __restrict__ out,
-                     const FlashLayout lay,
+                     const __grid_constant__ CUtensorMap tm_v,
+                     const __grid_constant__ CUtensorMap tm_o, const FlashLayout lay,
                      float* __restrict__ lse_out, float* __restrict__ max_out, int BH, int Sq,
                      int Sk, float scale_log2, int* __restrict__ err_word) {
   extern __shared__ uint8_t smem_raw[];
@@ -253,19 +323,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->q_full[b], 1);
-      mbar_init(&bars->q_empty[b], 1);
+      mbar_init(&bars->q_empty[b], kTiles);
     }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&bars->kv_full[s], 1);
-      mbar_init(&bars->kv_empty[s], 1);
+      mbar_init(&bars->kv_empty[s], kTiles);
     }
     for (int i = 0; i < kTiles; ++i) {
       mbar_init(&bars->s_full[i], 1);
-      mbar_init(&bars->s_free[i], kThreadsPerTile);
-      mbar_init(&bars->p_full[i], kThreadsPerTile);
+      mbar_init(&bars->s_free[i], 128);
+      mbar_init(&bars->p_full[i], 128);
       mbar_init(&bars->o_done[i], 1);
     }
-    mbar_init(&bars->drained, 1);
+    for (int i = 0; i < kTiles; ++i) mbar_init(&bars->drained[i], 1);
     bars->abort_flag = 0;
     fence_barrier_init();
   }
@@ -285,16 +355,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      int kv_it = 0;  // K/V tiles loaded so far (ring position)
-      int n = 0;
+      int kv_it = 0;   // K/V tiles loaded so far (ring position)
+      int n_q = 0;     // items whose Q tiles have been loaded
       bool ok = true;
-      for (int k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
-        const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
-        const int qb = n & 1;
-        if (n >= 2 && !mbar_wait(&bars->q_empty[qb], ((n >> 1) - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
+      // Load item n_q's two Q tiles into buffer n_q & 1 once the item two
+      // before it has released the buffer; without `block`, only if it has.
+      auto load_q = [&](bool block) -> bool {
+        const int k = item_of(n_q, cta, grid);
+        if (k >= n_items) return true;
+        const int qb = n_q & 1;
+        if (n_q >= 2) {
+          const uint32_t par = ((n_q >> 1) - 1) & 1;
+          if (block) {
+            if (!mbar_wait(&bars->q_empty[qb], par, abort_flag)) return false;
+          } else if (!mbar_test(&bars->q_empty[qb], par)) {
+            return true;
+          }
         }
+        const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
         const int h = kStrided ? w.bh % lay.H : 0, b = kStrided ? w.bh / lay.H : 0;
         mbar_arrive_expect_tx(&bars->q_full[qb], kTiles * kTileBytes);
         for (int i = 0; i < kTiles; ++i) {
@@ -305,13 +383,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           else
             tma_load_3d(&tm_q, &bars->q_full[qb], dst, 0, row, w.bh);
         }
-        for (int j = 0; j < w.n_total; ++j, ++kv_it) {
+        ++n_q;
+        return true;
+      };
+      int n = 0;
+      for (int k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
+        const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
+        while (ok && n_q <= n) ok = load_q(true);
+        const int h = kStrided ? w.bh % lay.H : 0, b = kStrided ? w.bh / lay.H : 0;
+        for (int j = 0; ok && j < w.n_total; ++j, ++kv_it) {
+          // the next item's Q as soon as its buffer is free
+          if (n_q == n + 1) ok = load_q(false);
           const int s = kv_it % kStages;
-          if (kv_it >= kStages &&
-              !mbar_wait(&bars->kv_empty[s], ((kv_it / kStages) - 1) & 1, abort_flag)) {
+          if (ok && kv_it >= kStages &&
+              !mbar_wait(&bars->kv_empty[s], ((kv_it / kStages) - 1) & 1, abort_flag))
             ok = false;
-            break;
-          }
+          if (!ok) break;
           mbar_arrive_expect_tx(&bars->kv_full[s], 2 * kTileBytes);
           if constexpr (kStrided) {
             load_rows(&tm_k, &bars->kv_full[s], smem + kOffK + s * kTileBytes, j * kBN, h, b,
@@ -326,250 +413,313 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutProducer);
       // Drain: every issued copy lands before the CTA may exit.
-      for (int m = (n > 2 ? n - 2 : 0); m < n; ++m)
+      for (int m = (n_q > 2 ? n_q - 2 : 0); m < n_q; ++m)
         (void)mbar_wait(&bars->q_full[m & 1], (m >> 1) & 1, abort_flag);
       for (int j = (kv_it > kStages ? kv_it - kStages : 0); j < kv_it; ++j)
         (void)mbar_wait(&bars->kv_full[j % kStages], (j / kStages) & 1, abort_flag);
     }
-  } else if (warp == kWarpMma) {
-    // ---------------------------------------------------------- UMMA issuer
+  } else if (warp == kWarpMma || warp == kWarpMma + 1) {
+    // --------------------------------------------- UMMA issuers, one per tile
     regs_decrease<kRegsControl>();
     if (elect_one()) {
+      const int i = warp - kWarpMma;   // query tile served by this thread
       const uint32_t sQ = smem_u32(smem + kOffQ);
       const uint32_t sK = smem_u32(smem + kOffK);
       const uint32_t sV = smem_u32(smem + kOffV);
+      auto start = [&](Cursor& c, int n, int base) {
+        c.n = n;
+        c.j = 0;
+        c.base = base;
+        const int k = item_of(n, cta, grid);
+        if (k < n_items) {
+          const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
+          c.nkv = i == 0 ? w.n_kv[0] : w.n_kv[1];
+          c.total = w.n_total;
+        } else {
+          c.nkv = 0;
+          c.total = 0;
+        }
+      };
+      auto advance = [&](Cursor& c) {
+        if (++c.j == c.nkv) start(c, c.n + 1, c.base + c.total);
+      };
+      // This tile's products in the order S(0), S(1), P·V(0), S(2), P·V(1), ...
+      // over all items, so each S is computed while the softmax works on the
+      // previous one.  Every ring position and Q buffer is released by both
+      // issuers (barrier counts 2); a position this tile does not use (tile 0
+      // skips the last K/V tile of an item) is released once the position
+      // after it has landed, i.e. once the ring has moved past it.
+      Cursor c, p;
+      start(c, 0, 0);
+      p = c;
+      int s_cnt = 0, pv_cnt = 0;
+      int skipped = -1;
+      // release the skipped position once a later one has been seen landed
+      auto release_skipped = [&](int landed) {
+        if (skipped >= 0 && landed > skipped) {
+          umma_commit(&bars->kv_empty[skipped % kStages]);
+          skipped = -1;
+        }
+      };
       bool ok = true;
-      int kv_base = 0;            // ring position of the item's first K/V tile
-      int kv_ready = -1;          // highest ring position whose kv_full was observed
-      int s_cnt[kTiles] = {0, 0};   // S_i products issued so far
-      int pv_cnt[kTiles] = {0, 0};  // O_i products issued so far
-      auto wait_kv = [&](int it) -> bool {
-        if (it <= kv_ready) return true;
-        if (!mbar_wait(&bars->kv_full[it % kStages], (it / kStages) & 1, abort_flag)) return false;
-        kv_ready = it;
-        return true;
-      };
-      // S_i = Q_i·K^T into TMEM once softmax i has read the previous S_i.
-      auto issue_s = [&](int i, int qb, int it) -> bool {
-        if (s_cnt[i] > 0 && !mbar_wait(&bars->s_free[i], (s_cnt[i] - 1) & 1, abort_flag))
-          return false;
-        if (!wait_kv(it)) return false;
-        tc_fence_after();
-        const int s = it % kStages;
+      while (ok && (c.nkv != 0 || p.nkv != 0)) {
+        if (c.nkv != 0) {
+          // S = Q·K^T into TMEM once the softmax has read the previous S
+          const int pos = c.base + c.j;
+          if (s_cnt > 0 && !mbar_wait(&bars->s_free[i], (s_cnt - 1) & 1, abort_flag)) { ok = false; break; }
+          if (c.j == 0 && !mbar_wait(&bars->q_full[c.n & 1], (c.n >> 1) & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&bars->kv_full[pos % kStages], (pos / kStages) & 1, abort_flag)) { ok = false; break; }
+          release_skipped(pos);
+          tc_fence_after();
+          const int s = pos % kStages, qb = c.n & 1;
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint64_t a = sdesc_sw128(sQ + (qb * kTiles + i) * kTileBytes + kk * 32, 16, 1024);
-          const uint64_t b = sdesc_sw128(sK + s * kTileBytes + kk * 32, 16, 1024);
-          umma_ss(tmem + col_s(i), a, b, kIdescS, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint64_t a = sdesc_sw128(sQ + (qb * kTiles + i) * kTileBytes + kk * 32, 16, 1024);
+            const uint64_t b = sdesc_sw128(sK + s * kTileBytes + kk * 32, 16, 1024);
+            umma_ss(tmem + col_s(i), a, b, kIdescS, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bars->s_full[i]);
+          ++s_cnt;
+          if (c.j + 1 == c.nkv) umma_commit(&bars->q_empty[qb]);  // every S of the item read Q
+          advance(c);
         }
-        umma_commit(&bars->s_full[i]);
-        ++s_cnt[i];
-        return true;
-      };
-      // O_i (+)= P_i·V once softmax i has written P_i.
-      auto issue_pv = [&](int i, int it, bool first) -> bool {
-        if (!mbar_wait(&bars->p_full[i], pv_cnt[i] & 1, abort_flag)) return false;
-        tc_fence_after();
-        const int s = it % kStages;
+        if (p.nkv != 0 && (pv_cnt + 1 < s_cnt || c.nkv == 0)) {
+          // O (+)= P·V once the softmax has written P
+          if (!mbar_wait(&bars->p_full[i], pv_cnt & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const int pos = p.base + p.j;   // landed: its S product waited for it
+          const int s = pos % kStages;
+          release_skipped(pos);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t b = sdesc_sw128(sV + s * kTileBytes + kk * 2048, 8192, 1024);
-          // P_i: 128 lanes x 64 columns of packed bf16 pairs; 16 keys = 8 columns
-          umma_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, b, kIdescO,
-                  (!first || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint64_t b = sdesc_sw128(sV + s * kTileBytes + kk * 2048, 8192, 1024);
+            // P: 128 lanes x 64 columns of packed bf16 pairs; 16 keys = 8 columns
+            umma_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, b, kIdescO,
+                    (p.j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bars->o_done[i]);
+          ++pv_cnt;
+          umma_commit(&bars->kv_empty[s]);
+          if (p.j + 1 == p.nkv && p.nkv < p.total) skipped = p.base + p.nkv;
+          advance(p);
         }
-        umma_commit(&bars->o_done[i]);
-        ++pv_cnt[i];
-        return true;
-      };
-      for (int n = 0, k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
-        const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
-        const int qb = n & 1;
-        if (!mbar_wait(&bars->q_full[qb], (n >> 1) & 1, abort_flag)) { ok = false; break; }
-        for (int i = 0; ok && i < kTiles; ++i) ok = issue_s(i, qb, kv_base);
-        for (int j = 0; ok && j < w.n_total; ++j) {
-          // next scores as soon as each softmax has read the current ones
-          for (int i = 0; ok && i < kTiles; ++i)
-            if (j + 1 < w.n_kv[i]) ok = issue_s(i, qb, kv_base + j + 1);
-          // then O_i += P_i·V_j as each P_i arrives
-          for (int i = 0; ok && i < kTiles; ++i)
-            if (j < w.n_kv[i]) ok = issue_pv(i, kv_base + j, j == 0);
-          if (ok) umma_commit(&bars->kv_empty[(kv_base + j) % kStages]);
-        }
-        if (ok) umma_commit(&bars->q_empty[qb]);  // every S of this item has read Q
-        kv_base += w.n_total;
       }
       if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutMma);
       // Every issued UMMA completes before teardown.
-      umma_commit(&bars->drained);
-      (void)mbar_wait(&bars->drained, 0, abort_flag);
+      umma_commit(&bars->drained[i]);
+      (void)mbar_wait(&bars->drained[i], 0, abort_flag);
     }
-  } else if (warp > kWarpMma) {
-    regs_decrease<kRegsControl>();  // idle warps of the control warpgroup
+  } else if (warp > kWarpMma + 1) {
+    regs_decrease<kRegsControl>();  // idle warp of the control warpgroup
   } else {
     // -------------------------------------------------------------- softmax
-    // warp -> (tile, column half, TMEM lane quarter); thread = one score row,
-    // half of its columns.  The two halves of a row meet through shared memory
-    // at a 64-thread named barrier (ids 1..8, one per tile and lane quarter).
+    // warp -> (tile, TMEM lane quarter); thread = one score row.
     regs_increase<kRegsSoftmax>();
-    Exchange* xch = reinterpret_cast<Exchange*>(smem + kOffX);
-    const int tile = warp / (4 * kHalves);
-    const int half = (warp / 4) % kHalves;
+    const int tile = warp / 4;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;            // TMEM lane = row within the tile
-    const uint32_t pair_bar = 1 + tile * 4 + quarter;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + col_s(tile) + half * kHalfCols;
-    const uint32_t p_addr = tmem + lane_base + col_p(tile) + half * (kHalfCols / 2);
-    const uint32_t o_addr = tmem + lane_base + col_o(tile) + half * kOutCols;
+    const uint32_t s_addr = tmem + lane_base + col_s(tile);
+    const uint32_t p_addr = tmem + lane_base + col_p(tile);
+    const uint32_t o_addr = tmem + lane_base + col_o(tile);
     const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+
+    // O/l, lse and m of a finished row (the previous item's), read from O_i
+    // before the next P·V of this tile may overwrite it.  The warp's 32 rows
+    // are staged in shared memory in the 128-byte-swizzled layout of a TMA
+    // box and written by one tensor store (rows past Sq are clipped by it).
+    uint8_t* stage = smem + kOffStage + warp * kStageBytesWarp;
+    const uint32_t r7 = static_cast<uint32_t>(lane & 7);
+    auto write_row = [&](const PendingRow& pr) {
+      uint32_t orr[kD];
+#pragma unroll
+      for (int c = 0; c < kD / 32; ++c)
+        tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&orr[c * 32]));
+      tmem_ld_wait();
+      const float inv_l = 1.f / pr.l;
+      // the previous store from this buffer has finished reading it
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+      const uint32_t row_s = smem_u32(stage) + static_cast<uint32_t>(lane) * 128u;
+      if constexpr (kOutF32) {
+#pragma unroll
+        for (int c = 0; c < kD / 4; ++c)
+          st_shared_v4(row_s + (c >> 3) * 4096u + (((c & 7) ^ r7) << 4),
+                       __float_as_uint(__uint_as_float(orr[4 * c]) * inv_l),
+                       __float_as_uint(__uint_as_float(orr[4 * c + 1]) * inv_l),
+                       __float_as_uint(__uint_as_float(orr[4 * c + 2]) * inv_l),
+                       __float_as_uint(__uint_as_float(orr[4 * c + 3]) * inv_l));
+      } else {
+#pragma unroll
+        for (int c = 0; c < kD / 8; ++c)
+          st_shared_v4(row_s + ((c ^ r7) << 4),
+                       pack_bf16x2(__uint_as_float(orr[8 * c]) * inv_l, __uint_as_float(orr[8 * c + 1]) * inv_l),
+                       pack_bf16x2(__uint_as_float(orr[8 * c + 2]) * inv_l, __uint_as_float(orr[8 * c + 3]) * inv_l),
+                       pack_bf16x2(__uint_as_float(orr[8 * c + 4]) * inv_l, __uint_as_float(orr[8 * c + 5]) * inv_l),
+                       pack_bf16x2(__uint_as_float(orr[8 * c + 6]) * inv_l, __uint_as_float(orr[8 * c + 7]) * inv_l));
+      }
+      fence_async_shared();  // the staged rows are visible to the tensor store
+      __syncwarp();
+      if (lane == 0) {
+        // lane 0 holds the warp's first row
+        constexpr int kBoxes = kOutF32 ? 2 : 1;
+#pragma unroll
+        for (int bx = 0; bx < kBoxes; ++bx) {
+          const void* src = stage + bx * 4096;
+          if constexpr (kStrided) {
+            const int h = pr.bh % lay.H, b = pr.bh / lay.H;
+            if (lay.o_token_major)
+              tma_store_4d(&tm_o, src, bx * 32, h, pr.q_idx, b);
+            else
+              tma_store_4d(&tm_o, src, bx * 32, pr.q_idx, h, b);
+          } else {
+            tma_store_3d(&tm_o, src, bx * 32, pr.q_idx, pr.bh);
+          }
+        }
+        bulk_commit_group();
+      }
+      if (pr.q_idx < Sq) {
+        const size_t row_off = static_cast<size_t>(pr.bh) * Sq + pr.q_idx;
+        if (lse_out) lse_out[row_off] = (pr.m_used + __log2f(pr.l)) * kLn2;
+        if (max_out) max_out[row_off] = pr.m_true * kLn2;
+      }
+    };
+
     int it = 0;  // S_i tiles processed so far, across items
     bool ok = true;
+    PendingRow pend;
+    pend.valid = false;
     for (int n = 0, k; ok && (k = item_of(n, cta, grid)) < n_items; ++n) {
       const WorkItem w = decode_item<kCausal>(k, BH, n_blk, n_k);
       const int q_idx = w.blk * kRowsPerCta + tile * kBM + row;
-      const int nkv = w.n_kv[tile];
-      float m_used = -INFINITY;  // offset used for exponentials (log2 units)
+      const int nkv = tile == 0 ? w.n_kv[0] : w.n_kv[1];
+      float m_used = -INFINITY;  // offset of the exponentials (log2 units)
       float m_true = -INFINITY;  // true running row max (log2 units)
-      float l = 0.f;             // this half's share of the row sum
+      float l = 0.f;             // row sum against m_used
       for (int j = 0; j < nkv; ++j, ++it) {
         if (!warp_wait(&bars->s_full[tile], it & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        uint32_t sr[kHalfCols];
+        uint32_t sr[kBN];
 #pragma unroll
-        for (int c = 0; c < kHalfCols / 32; ++c)
+        for (int c = 0; c < kBN / 32; ++c)
           tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[c * 32]));
         tmem_ld_wait();
         // S_i now lives in registers: let the tensor core write the next one.
         tc_fence_before();
         mbar_arrive(&bars->s_free[tile]);
         float* sv = reinterpret_cast<float*>(sr);
-        if (j == nkv - 1) {
-          const int k0 = j * kBN + half * kHalfCols;
+        const bool last = (j == nkv - 1);
+        if (last) {
+          const int k0 = j * kBN;
 #pragma unroll
-          for (int c = 0; c < kHalfCols; ++c) {
+          for (int c = 0; c < kBN; ++c) {
             const int k_idx = k0 + c;
             if ((k_idx >= Sk) || (kCausal && k_idx > q_idx)) sv[c] = -INFINITY;
           }
         }
-        // partial row max over this half: 4 independent chains of 3-input max
-        float mx0 = fmaxf(sv[0], sv[1]), mx1 = fmaxf(sv[2], sv[3]);
-        float mx2 = fmaxf(sv[4], sv[5]), mx3 = fmaxf(sv[6], sv[7]);
-        static_assert(kHalfCols % 8 == 0, "the max chains consume 8 scores per step");
-#pragma unroll
-        for (int c = 8; c < kHalfCols; c += 8) {
-          mx0 = fmax3(mx0, sv[c], sv[c + 1]);
-          mx1 = fmax3(mx1, sv[c + 2], sv[c + 3]);
-          mx2 = fmax3(mx2, sv[c + 4], sv[c + 5]);
-          mx3 = fmax3(mx3, sv[c + 6], sv[c + 7]);
-        }
-        float mx = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-        if constexpr (kHalves > 1) {
-          xch->max_part[it & 1][tile][half][row] = mx;
-          named_bar_sync(pair_bar, 64);
-          mx = fmaxf(mx, xch->max_part[it & 1][tile][half ^ 1][row]);
-        }
-        const float t_max = mx * scale_log2;
-        m_true = fmaxf(m_true, t_max);
-        float m_new = m_used;
-        float alpha = 1.f;
-        if (t_max > m_used + kRescaleThreshold) {
-          m_new = t_max;
-          alpha = (m_used == -INFINITY) ? 0.f : fast_exp2(m_used - m_new);
-        }
-        // p = 2^(s·scale_log2 - m_new), two at a time, four partial sums.  The
-        // masked last tile uses the exponential unit for every element (masked
-        // keys give exactly 0); other tiles send part of the pairs through the
-        // FMA-pipe polynomial, which relieves the exponential unit.
-        const uint64_t negm2 = f2_pack(-m_new, -m_new);
-        uint64_t acc[4] = {0, 0, 0, 0};
-        uint32_t pk[kHalfCols / 2];
-        if (j == nkv - 1)
-          exp2_pairs<0>(sv, scale2, negm2, pk, acc);
-        else
-          exp2_pairs<kPolyPairsPer8>(sv, scale2, negm2, pk, acc);
-        float a0, a1;
-        f2_unpack(f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3])), a0, a1);
-        l = l * alpha + (a0 + a1);
-        // P_i may be overwritten once the previous O_i += P_i·V has completed
-        // (for j == 0 the previous item's epilogue already waited for it).
-        if (j > 0) {
-          if (!warp_wait(&bars->o_done[tile], (it - 1) & 1, abort_flag)) { ok = false; break; }
+        // P_i may be overwritten, and O_i rescaled, once the previous
+        // O_i += P_i·V has completed (for j == 0, the previous item's last).
+        bool pv_done = (it == 0);
+        auto wait_pv = [&]() -> bool {
+          if (pv_done) return true;
+          if (!warp_wait(&bars->o_done[tile], (it - 1) & 1, abort_flag)) return false;
           tc_fence_after();
-        }
-#pragma unroll
-        for (int c = 0; c < kHalfCols / 64; ++c)
-          tmem_st32(p_addr + c * 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[c * 32]));
-        // O_i is stable here; rescale this thread's output columns if the warp
-        // has a row whose running max moved.
-        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-          for (int c = 0; c < kOutCols / 32; ++c) {
-            uint32_t orr[32];
-            tmem_ld32(o_addr + c * 32, orr);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
-            tmem_st32(o_addr + c * 32, orr);
+          pv_done = true;
+          return true;
+        };
+        // Raise the offset to t where a row's max passed it by more than the
+        // threshold (always at the row's first tile, where it is -inf): l, O
+        // (earlier tiles of this item) and the half of P_i already stored are
+        // multiplied by 2^(old - new).  Rare after a row's first tile.
+        auto raise_offset = [&](float t, bool half_stored) -> bool {
+          const bool up = t > m_used + kRescaleThreshold;
+          if (!__any_sync(0xffffffffu, up)) return true;
+          const float m_new = up ? t : m_used;
+          const float alpha = fast_exp2(m_used - m_new);   // 1 where the offset stays
+          m_used = m_new;
+          l *= alpha;
+          if (j > 0 || half_stored) {
+            if (!wait_pv()) return false;
+            tmem_st_wait();
           }
+          if (j > 0) {
+#pragma unroll 1
+            for (int c = 0; c < kD / 16; ++c) {
+              uint32_t orr[16];
+              tmem_ld16(o_addr + c * 16, orr);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) orr[e] = __float_as_uint(__uint_as_float(orr[e]) * alpha);
+              tmem_st16(o_addr + c * 16, orr);
+            }
+          }
+          if (half_stored) {
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              uint32_t prr[16];
+              tmem_ld16(p_addr + c * 16, prr);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                prr[e] = pack_bf16x2(__uint_as_float(prr[e] << 16) * alpha,
+                                     __uint_as_float(prr[e] & 0xFFFF0000u) * alpha);
+              tmem_st16(p_addr + c * 16, prr);
+            }
+          }
+          return true;
+        };
+        uint32_t pk[kBN / 4];   // half a row of packed probabilities
+        // ---- first half of the keys: its max, then its exponentials
+        const float t_a = half_max<0>(sv) * scale_log2;
+        m_true = fmaxf(m_true, t_a);
+        if (!raise_offset(t_a, false)) { ok = false; break; }
+        float sum_a;
+        {
+          uint64_t acc[4] = {0, 0, 0, 0};
+          exp_cols<0, kBN / 2>(last, sv, scale2, f2_pack(-m_used, -m_used), pk, acc);
+          sum_a = f2_sum4(acc);
         }
+        // second half's max: independent of the exponentials above
+        const float t_b = half_max<kBN / 2>(sv) * scale_log2;
+        if (!wait_pv()) { ok = false; break; }
+        tmem_st32(p_addr, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+        l += sum_a;
+        // ---- second half
+        m_true = fmaxf(m_true, t_b);
+        if (!raise_offset(t_b, true)) { ok = false; break; }
+        {
+          uint64_t acc[4] = {0, 0, 0, 0};
+          exp_cols<kBN / 2, kBN>(last, sv, scale2, f2_pack(-m_used, -m_used), pk, acc);
+          l += f2_sum4(acc);
+        }
+        tmem_st32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(pk));
+        // the previous item's rows: O_i holds them until this P_i is released
+        if (j == 0 && pend.valid) write_row(pend);
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&bars->p_full[tile]);
-        m_used = m_new;
       }
       if (!ok) break;
-      // ---------------------------------------------------------- epilogue
-      if (!warp_wait(&bars->o_done[tile], (it - 1) & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t orr[kOutCols];
-#pragma unroll
-      for (int c = 0; c < kOutCols / 32; ++c)
-        tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&orr[c * 32]));
-      tmem_ld_wait();
-      float l_row = l;
-      if constexpr (kHalves > 1) {
-        xch->sum_part[tile][half][row] = l;
-        named_bar_sync(pair_bar, 64);
-        l_row += xch->sum_part[tile][half ^ 1][row];
-        // both halves have read the partner's sum before either reuses the slot
-        named_bar_sync(pair_bar, 64);
-      }
-      if (q_idx < Sq) {
-        const float inv_l = 1.f / l_row;
-        const size_t row_off = static_cast<size_t>(w.bh) * Sq + q_idx;
-        const long long o_off =
-            kStrided ? (w.bh / lay.H) * lay.o_b + (w.bh % lay.H) * lay.o_h +
-                           static_cast<long long>(q_idx) * lay.o_s
-                     : static_cast<long long>(row_off) * kD;
-        constexpr int kCols = kOutCols;
-        if constexpr (kOutF32) {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(out) + o_off +
-                                                  half * kCols);
-#pragma unroll
-          for (int c = 0; c < kCols / 4; ++c)
-            dst[c] = make_float4(__uint_as_float(orr[4 * c]) * inv_l,
-                                 __uint_as_float(orr[4 * c + 1]) * inv_l,
-                                 __uint_as_float(orr[4 * c + 2]) * inv_l,
-                                 __uint_as_float(orr[4 * c + 3]) * inv_l);
-        } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + o_off +
-                                                half * kCols);
-#pragma unroll
-          for (int c = 0; c < kCols / 8; ++c)
-            dst[c] = make_uint4(
-                pack_bf16x2(__uint_as_float(orr[8 * c]) * inv_l, __uint_as_float(orr[8 * c + 1]) * inv_l),
-                pack_bf16x2(__uint_as_float(orr[8 * c + 2]) * inv_l, __uint_as_float(orr[8 * c + 3]) * inv_l),
-                pack_bf16x2(__uint_as_float(orr[8 * c + 4]) * inv_l, __uint_as_float(orr[8 * c + 5]) * inv_l),
-                pack_bf16x2(__uint_as_float(orr[8 * c + 6]) * inv_l, __uint_as_float(orr[8 * c + 7]) * inv_l));
-        }
-        if (half == 0) {
-          if (lse_out) lse_out[row_off] = (m_used + __log2f(l_row)) * kLn2;
-          if (max_out) max_out[row_off] = m_true * kLn2;
-        }
+      pend.l = l;
+      pend.m_used = m_used;
+      pend.m_true = m_true;
+      pend.q_idx = q_idx;
+      pend.bh = w.bh;
+      pend.valid = true;
+    }
+    // the last item's rows, once its last P·V has completed
+    if (ok && pend.valid) {
+      if (warp_wait(&bars->o_done[tile], (it - 1) & 1, abort_flag)) {
+        tc_fence_after();
+        write_row(pend);
+      } else {
+        ok = false;
       }
     }
     if (!ok) raise_abort(abort_flag, err_word, kDevErrTimeoutSoftmax);
+    // the staged rows are read and written before the CTA's memory goes away
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -582,8 +732,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <bool kCausal, bool kOutF32, bool kStrided>
 cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUtensorMap& tk,
-                         const CUtensorMap& tv, void* out, const FlashLayout& lay, float* lse,
-                         float* mx, int BH, int Sq, int Sk, float scale_log2) {
+                         const CUtensorMap& tv, const CUtensorMap& to, const FlashLayout& lay,
+                         float* lse, float* mx, int BH, int Sq, int Sk, float scale_log2) {
   auto kern = flash_fwd_kernel<kCausal, kOutF32, kStrided>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -595,7 +745,7 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUten
   if (e != cudaSuccess) return e;
   const int n_items = ceil_div(Sq, kRowsPerCta) * BH;
   dim3 grid(n_items < sms ? n_items : sms);
-  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, out, lay, lse, mx, BH, Sq, Sk, scale_log2,
+  kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, lay, lse, mx, BH, Sq, Sk, scale_log2,
                                                device_error_word());
   return cudaGetLastError();
 }
@@ -616,20 +766,24 @@ FlashStrides flash_head_major_strides(int H, int Sq, int Sk) {
 }
 
 namespace {
-// 4-D map over rows of S positions x H heads x B batches, 64 bf16 per row;
-// the row and head dims are ordered by stride (a tensor map's dims go from
-// the finest stride outwards).  Returns whether the head dim is the inner one.
+// 4-D map over rows of S positions x H heads x B batches, 64 values per row
+// (bf16, or fp32 for an fp32 output); the row and head dims are ordered by
+// stride (a tensor map's dims go from the finest stride outwards).  A box is
+// `rows` rows of 128 bytes.  Returns whether the head dim is the inner one.
 cudaError_t make_rows_map(CUtensorMap* map, const void* base, int S, int H, int B,
-                          const long long (&st)[3], int* token_major, const char** err_msg) {
+                          const long long (&st)[3], uint32_t rows, bool f32, int* token_major,
+                          const char** err_msg) {
   const bool tok = st[1] < st[0];
   const uint64_t s = static_cast<uint64_t>(S), h = static_cast<uint64_t>(H);
+  const uint64_t esz = f32 ? 4 : 2;
   const uint64_t dims[4] = {kD, tok ? h : s, tok ? s : h, static_cast<uint64_t>(B)};
-  const uint64_t strides[3] = {static_cast<uint64_t>(tok ? st[1] : st[0]) * 2,
-                               static_cast<uint64_t>(tok ? st[0] : st[1]) * 2,
-                               static_cast<uint64_t>(st[2]) * 2};
-  const uint32_t box[4] = {kD, tok ? 1u : static_cast<uint32_t>(kBM), tok ? static_cast<uint32_t>(kBM) : 1u, 1};
+  const uint64_t strides[3] = {static_cast<uint64_t>(tok ? st[1] : st[0]) * esz,
+                               static_cast<uint64_t>(tok ? st[0] : st[1]) * esz,
+                               static_cast<uint64_t>(st[2]) * esz};
+  const uint32_t box[4] = {static_cast<uint32_t>(128 / esz), tok ? 1u : rows, tok ? rows : 1u, 1};
   *token_major = tok ? 1 : 0;
-  return make_tmap_bf16_sw128(map, base, 4, dims, strides, box, err_msg);
+  return make_tmap_sw128(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                         static_cast<int>(esz), base, 4, dims, strides, box, err_msg);
 }
 }  // namespace
 
@@ -639,13 +793,10 @@ cudaError_t launch_flash_fwd(cudaStream_t stream, const __nv_bfloat16* Q, const 
                              bool causal, const FlashStrides& st, const char** err_msg) {
   const int BH = B * H;
   if (BH == 0 || Sq == 0) return cudaSuccess;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   FlashLayout lay;
   lay.H = H;
-  lay.o_s = st.o[0];
-  lay.o_h = st.o[1];
-  lay.o_b = st.o[2];
-  lay.q_token_major = lay.kv_token_major = 0;
+  lay.q_token_major = lay.kv_token_major = lay.o_token_major = 0;
   const FlashStrides hm = flash_head_major_strides(H, Sq, Sk);
   bool strided = false;
   for (int i = 0; i < 3; ++i)
@@ -654,9 +805,11 @@ cudaError_t launch_flash_fwd(cudaStream_t stream, const __nv_bfloat16* Q, const 
   cudaError_t e = cudaSuccess;
   if (strided) {
     int k_tok = 0, v_tok = 0;
-    e = make_rows_map(&tq, Q, Sq, H, B, st.q, &lay.q_token_major, err_msg);
-    if (e == cudaSuccess) e = make_rows_map(&tk, K, Sk, H, B, st.k, &k_tok, err_msg);
-    if (e == cudaSuccess) e = make_rows_map(&tv, V, Sk, H, B, st.v, &v_tok, err_msg);
+    e = make_rows_map(&tq, Q, Sq, H, B, st.q, kBM, false, &lay.q_token_major, err_msg);
+    if (e == cudaSuccess) e = make_rows_map(&tk, K, Sk, H, B, st.k, kBM, false, &k_tok, err_msg);
+    if (e == cudaSuccess) e = make_rows_map(&tv, V, Sk, H, B, st.v, kBM, false, &v_tok, err_msg);
+    if (e == cudaSuccess)
+      e = make_rows_map(&to, O, Sq, H, B, st.o, 32, out_f32, &lay.o_token_major, err_msg);
     if (e != cudaSuccess) return e;
     if (k_tok != v_tok) {
       if (err_msg) *err_msg = "K and V must share one layout (both head-major or both token-major)";
@@ -674,11 +827,18 @@ cudaError_t launch_flash_fwd(cudaStream_t stream, const __nv_bfloat16* Q, const 
     e = make_tmap_bf16_sw128(&tq, Q, 3, qdims, qstr, box, err_msg);
     if (e == cudaSuccess) e = make_tmap_bf16_sw128(&tk, K, 3, kdims, kstr, box, err_msg);
     if (e == cudaSuccess) e = make_tmap_bf16_sw128(&tv, V, 3, kdims, kstr, box, err_msg);
+    // O: boxes of 32 rows x 128 bytes (64 bf16, or 32 of 64 fp32)
+    const uint64_t esz = out_f32 ? 4 : 2;
+    const uint32_t obox[3] = {static_cast<uint32_t>(128 / esz), 32, 1};
+    const uint64_t ostr[2] = {kD * esz, static_cast<uint64_t>(Sq) * kD * esz};
+    if (e == cudaSuccess)
+      e = make_tmap_sw128(&to, out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                          static_cast<int>(esz), O, 3, qdims, ostr, obox, err_msg);
     if (e != cudaSuccess) return e;
   }
   const float sl2 = scale * kLog2e;
 #define ND_FLASH_LAUNCH(C, F, S_)                                                              \
-  launch_typed<C, F, S_>(stream, tq, tk, tv, O, lay, lse, row_max, BH, Sq, Sk, sl2)
+  launch_typed<C, F, S_>(stream, tq, tk, tv, to, lay, lse, row_max, BH, Sq, Sk, sl2)
   if (strided) {
     if (causal) return out_f32 ? ND_FLASH_LAUNCH(true, true, true) : ND_FLASH_LAUNCH(true, false, true);
     return out_f32 ? ND_FLASH_LAUNCH(false, true, true) : ND_FLASH_LAUNCH(false, false, true);

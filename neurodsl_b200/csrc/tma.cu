@@ -56,6 +56,18 @@ unsigned long long current_context_id() {
 cudaError_t make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank,
                                  const uint64_t* dims, const uint64_t* strides_bytes,
                                  const uint32_t* box, const char** err_msg) {
+  return make_tmap_sw128(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rank, dims, strides_bytes,
+                         box, err_msg);
+}
+
+cudaError_t make_tmap_sw128(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes,
+                            const void* base, int rank, const uint64_t* dims,
+                            const uint64_t* strides_bytes, const uint32_t* box,
+                            const char** err_msg) {
+  if (static_cast<uint64_t>(box[0]) * static_cast<uint64_t>(elem_bytes) != 128) {
+    if (err_msg) *err_msg = "tensor-map box rows must be 128 bytes for the 128-byte swizzle";
+    return cudaErrorInvalidValue;
+  }
   std::call_once(g_encode_once, load_encode);
   if (g_encode == nullptr) {
     if (err_msg) *err_msg = "cuTensorMapEncodeTiled entry point unavailable";
@@ -71,7 +83,7 @@ cudaError_t make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank,
     estride[i] = 1;
   }
   for (int i = 0; i + 1 < rank; ++i) gstride[i] = strides_bytes[i];
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<cuuint32_t>(rank),
+  CUresult r = g_encode(map, dtype, static_cast<cuuint32_t>(rank),
                         const_cast<void*>(base), gdim, gstride, bdim, estride,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

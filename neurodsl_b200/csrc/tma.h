@@ -16,6 +16,13 @@ cudaError_t make_tmap_bf16_sw128(CUtensorMap* map, const void* base, int rank,
                                  const uint64_t* dims, const uint64_t* strides_bytes,
                                  const uint32_t* box, const char** err_msg);
 
+// The same for another element type (CU_TENSOR_MAP_DATA_TYPE_*), 128-byte
+// swizzle: box[0] * element size must be 128 bytes.
+cudaError_t make_tmap_sw128(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes,
+                            const void* base, int rank, const uint64_t* dims,
+                            const uint64_t* strides_bytes, const uint32_t* box,
+                            const char** err_msg);
+
 // Unique id of the calling thread's current CUDA context (cuCtxGetId through
 // the driver entry point), or 0 when it cannot be read.  Device addresses of
 // the library's __device__ variables are valid for one context only; callers
