@@ -39,6 +39,8 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from neurodsl_b200.ranks import dist_env  # noqa: E402  (no CUDA library load)
+
 B, H, S, D = 8, 16, 2048, 64
 FLOPS_PER_STEP = 4 * B * H * D * S * (S + 1) // 2          # 68,753,031,168
 DEC_B, DEC_H, DEC_L0, DEC_T = 64, 12, 1024, 128
@@ -138,11 +140,29 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_env():
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return rank, world, local
+def barrier():
+    """Barrier over all ranks (a no-op for one process)."""
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def max_over_ranks(x, device=None):
+    """Max of a per-rank time over all ranks (identity for one process)."""
+    from neurodsl_b200 import ranks
+    return ranks.max_over_ranks(x, device=device)
+
+
+def cpu_model():
+    """The host CPU's model name (first 'model name' line of /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 # --------------------------------------------------------------- CPU arm ---
@@ -197,7 +217,7 @@ def run_reference(args):
                    "path": "oracle restatement of flash_attn_fwd_cpu_simple! "
                            "(src/flash_attention.jl:49-69); Julia reference not runnable here"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                         "sample": desc},
+                         "cpu_model": cpu_model(), "sample": desc},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -207,19 +227,76 @@ def run_reference(args):
 
 # --------------------------------------------------------------- GPU arm ---
 
-def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks, barrier,
-               peaks, reps, chunk):
-    """Prefill and greedy decode of a GPT-style decoder built from the library
-    (neurodsl_b200.model).  tp == world: one tensor-parallel model over all
-    ranks (Megatron shards, NCCL all-reduces; strong scaling); tp == 1: every
-    rank runs its own replica on its own batch (weak scaling)."""
+def _gather_vocab(logits, V, tp, group):
+    """Full-vocabulary logits [rows][V] from the ranks' slices of a
+    tensor-parallel LM head (rank r holds rows [r·ceil(V/tp), ...))."""
     import torch
+    w = (V + tp - 1) // tp
+    pad = torch.full((logits.shape[0], w), float("nan"), device=logits.device)
+    pad[:, :logits.shape[1]] = logits
+    parts = [torch.empty_like(pad) for _ in range(tp)]
+    torch.distributed.all_gather(parts, pad, group=group)
+    return torch.cat(parts, dim=1)[:, :V]
+
+
+def tp_parity(model, cfg, ids, group, tp, dev, steps=16):
+    """Tensor-parallel decoder against the one-GPU model of the same seed on
+    the same prompts: logits of the last prompt position (max-abs and
+    relative L2 over the full vocabulary) and the first `steps` greedy tokens
+    of every row.  Collective over the model's group; the one-GPU model runs
+    on the group's first rank, which returns the result (others None)."""
+    import torch
+    import torch.distributed as dist
+
+    from neurodsl_b200.model import GPT
+    model.release_graphs()
+    lg = model.prefill(ids, steps).clone()
+    for t in range(steps - 1):
+        model.decode_step(t)
+    toks = model.tokens().clone()
+    full = _gather_vocab(lg, cfg.vocab, tp, group)
+    out = None
+    if dist.get_rank(group) == 0:
+        ref = GPT(cfg, seed=0, device=dev)
+        rl = ref.prefill(ids, steps).clone()
+        for t in range(steps - 1):
+            ref.decode_step(t)
+        rt = ref.tokens().clone()
+        torch.cuda.synchronize()
+        diff = (full - rl).abs()
+        eq = (toks == rt)
+        first = None
+        if not bool(eq.all()):
+            bad = (~eq).nonzero()
+            first = int(bad[:, 1].min())
+        out = {"reference": "one-GPU model, same seed and prompts",
+               "logits_max_abs": float(diff.max()),
+               "logits_rel_l2": float((full - rl).norm() / rl.norm()),
+               "tokens_equal": bool(eq.all()), "tokens_checked": int(eq.numel()),
+               "first_differing_step": first}
+        del ref
+        torch.cuda.empty_cache()
+    return out
+
+
+def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, parity):
+    """Prefill and greedy decode of a GPT-style decoder built from the library
+    (neurodsl_b200.model).  The world is split into world/tp groups of tp
+    consecutive ranks; each group runs one tensor-parallel model (Megatron
+    shards; NCCL all-reduces for prefill, the NVLink peer reduction for
+    decode) on its own batch.  tp == world: one model over all GPUs (strong
+    scaling); tp == 1: one replica per GPU (weak scaling)."""
+    import torch
+    import torch.distributed as dist
 
     from neurodsl_b200.model import GPT, decode_weight_bytes, flops_prefill
-    group = torch.distributed.group.WORLD if (pg is not None and tp > 1) else None
-    model = GPT(cfg, seed=0, device=dev, tp=tp, rank=rank if tp > 1 else 0, group=group,
+    rank, world, _ = dist_env()
+    dp = world // tp
+    gi = rank // tp
+    group = groups.get((tp, gi)) if tp > 1 else None
+    model = GPT(cfg, seed=0, device=dev, tp=tp, rank=rank % tp if tp > 1 else 0, group=group,
                 nvlink_rows=B if tp > 1 else 0)
-    gen = torch.Generator(device=dev).manual_seed(99 + (0 if tp > 1 else rank))
+    gen = torch.Generator(device=dev).manual_seed(99 + (gi if tp > 1 else rank))
     ids = torch.randint(0, cfg.vocab, (B, S), device=dev, dtype=torch.int32, generator=gen)
     graphs = True
     try:
@@ -251,32 +328,43 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
         torch.cuda.synchronize()
         tp_ms.append(ev[0].elapsed_time(ev[1]))
         td_ms.append(ev[1].elapsed_time(ev[2]))
-    p_ms = max_over_ranks(min(tp_ms))
-    d_ms = max_over_ranks(min(td_ms))
+    p_ms = max_over_ranks(min(tp_ms), dev)
+    d_ms = max_over_ranks(min(td_ms), dev)
     tokens = model.tokens()[:, :4].cpu().tolist()
+    par = None
+    if parity and tp > 1:
+        if gi == 0:
+            par = tp_parity(model, cfg, ids, group, tp, dev)
+        barrier()
     model.close()
     del model
     torch.cuda.synchronize()
-    replicas = 1 if tp > 1 else world
     n_dec = steps - 1
     fl = flops_prefill(cfg, B, S)
     kv = sum(2 * B * cfg.n_layer * cfg.n_head * (S + t + 1) * 64 * 2 for t in range(n_dec))
-    dec_bytes = decode_weight_bytes(cfg) * n_dec + kv   # whole model, all ranks together
-    p_tflops = replicas * fl / (p_ms * 1e-3) / 1e12
-    d_gbs = replicas * dec_bytes / (d_ms * 1e-3) / 1e9
-    return {
+    dec_bytes = decode_weight_bytes(cfg) * n_dec + kv   # one model, all its ranks together
+    p_tflops = dp * fl / (p_ms * 1e-3) / 1e12
+    d_gbs = dp * dec_bytes / (d_ms * 1e-3) / 1e9
+    if tp == 1:
+        layout = f"dp{world} replicas"
+    elif dp == 1:
+        layout = f"tp{tp}"
+    else:
+        layout = f"tp{tp} x dp{dp}"
+    line = {
         "workload": f"{name}: {cfg.n_layer} layers d={cfg.d_model} {cfg.n_head}x64 heads "
-                    f"F={cfg.d_ff} vocab {cfg.vocab}, batch {B}, prompt {S}, {steps} greedy tokens",
-        "parallelism": f"tp{tp}" if tp > 1 else f"dp{world} replicas",
+                    f"F={cfg.d_ff} vocab {cfg.vocab}, batch {B} per model, prompt {S}, "
+                    f"{steps} greedy tokens",
+        "parallelism": layout,
         "reduction": ("prefill: NCCL all-reduce; decode: one-shot NVLink peer reduction fused "
                       "with residual + LayerNorm") if tp > 1 else None,
-        "scaling": "strong" if tp > 1 else "weak",
-        "prefill": {"value": replicas * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
+        "scaling": "strong" if (tp > 1 and dp == 1) else "weak",
+        "prefill": {"value": dp * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
                     "launch": "one CUDA graph" if graphs else "eager launches",
                     "roofline": {"bound": "tensor", "achieved": p_tflops / world,
                                  "peak": peaks["bf16_tflops"], "unit": "TFLOP/s per GPU",
                                  "frac": p_tflops / world / peaks["bf16_tflops"]}},
-        "decode": {"value": replicas * B * n_dec / (d_ms * 1e-3), "unit": "tokens/s", "ms": d_ms,
+        "decode": {"value": dp * B * n_dec / (d_ms * 1e-3), "unit": "tokens/s", "ms": d_ms,
                    "us_per_step": d_ms * 1e3 / n_dec,
                    "launch": "CUDA graphs" if graphs else "eager launches",
                    "roofline": {"bound": "hbm", "achieved": d_gbs / world,
@@ -285,6 +373,9 @@ def model_line(name, cfg, B, S, steps, tp, rank, world, dev, pg, max_over_ranks,
                                 "bytes": "bf16 weights + K/V read per step"}},
         "first_tokens": tokens[0],
     }
+    if par is not None or (parity and tp > 1):
+        line["tp_parity"] = par
+    return line
 
 
 def run_ours(args):
@@ -295,6 +386,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     pg = None
+    groups = {}
     if world > 1:
         import datetime
 
@@ -302,17 +394,12 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
         pg = dist
-
-    def barrier():
-        if pg is not None:
-            pg.barrier()
-
-    def max_over_ranks(x):
-        if pg is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
+        # tensor-parallel groups of tp consecutive ranks (every rank creates
+        # every group, in the same order)
+        for tp in sorted({world, min(world, 4)}):
+            for g in range(world // tp):
+                members = list(range(g * tp, (g + 1) * tp))
+                groups[(tp, g)] = dist.group.WORLD if tp == world else dist.new_group(members)
 
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
     sets = []
@@ -357,7 +444,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     ms_local = e0.elapsed_time(e1) / args.steps
-    ms = max_over_ranks(ms_local)
+    ms = max_over_ranks(ms_local, dev)
     value = world * FLOPS_PER_STEP / (ms * 1e-3) / 1e12
     kernel_tflops = FLOPS_PER_STEP / (ms_local * 1e-3) / 1e12
 
@@ -397,7 +484,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     dec_ms_local = d0.elapsed_time(d1) / dec_reps
-    dec_ms = max_over_ranks(dec_ms_local)
+    dec_ms = max_over_ranks(dec_ms_local, dev)
     dec_bytes_total = sum(dec_bytes(DEC_L0 + t) for t in range(1, DEC_T + 1))
     dec_tokens = world * DEC_B * DEC_T / (dec_ms * 1e-3)
     dec_gbs = dec_bytes_total / (dec_ms_local * 1e-3) / 1e9
@@ -406,35 +493,44 @@ def run_ours(args):
     # ---- fused linear + bias + GELU (the MLP-up of the 24-layer dim-1024
     # model's prefill: 32 x 2048 tokens, 1024 -> 4096) and LayerNorm over the
     # same tokens; each timed over `args.aux_reps` calls
+    # Two rotating sets of inputs and outputs each (every set is larger than
+    # the 126 MB L2), so no call finds its operands in L2 from the call before.
     gm, gn, gk = 65536, 4096, 1024
-    ga = torch.randn(gm, gk, device=dev, generator=gen).bfloat16()
-    gw = (0.02 * torch.randn(gn, gk, device=dev, generator=gen)).bfloat16()
+    gsets = [(torch.randn(gm, gk, device=dev, generator=gen).bfloat16(),
+              (0.02 * torch.randn(gn, gk, device=dev, generator=gen)).bfloat16(),
+              torch.empty(gm, gn, device=dev, dtype=torch.bfloat16)) for _ in range(2)]
     gb = torch.zeros(gn, device=dev)
-    gy = torch.empty(gm, gn, device=dev, dtype=torch.bfloat16)
-    lx = torch.randn(gm, gk, device=dev, generator=gen)
-    ly = torch.empty(gm, gk, device=dev, dtype=torch.bfloat16)
-    lmean = torch.empty(gm, device=dev)
-    lrstd = torch.empty(gm, device=dev)
+    lsets = [(torch.randn(gm, gk, device=dev, generator=gen),
+              torch.empty(gm, gk, device=dev, dtype=torch.bfloat16),
+              torch.empty(gm, device=dev), torch.empty(gm, device=dev)) for _ in range(2)]
 
     def time_calls(fn, reps):
-        for _ in range(3):
-            fn()
+        for i in range(3):
+            fn(i)
         torch.cuda.synchronize()
         a0 = torch.cuda.Event(enable_timing=True)
         a1 = torch.cuda.Event(enable_timing=True)
         a0.record(stream)
-        for _ in range(reps):
-            fn()
+        for i in range(reps):
+            fn(i)
         a1.record(stream)
         torch.cuda.synchronize()
         return a0.elapsed_time(a1) / reps
 
-    gemm_ms = time_calls(lambda: ops.linear(ga, gw, gb, act="sigmoid", out=gy), args.aux_reps)
+    def gemm_call(i):
+        ga, gw, gy = gsets[i & 1]
+        ops.linear(ga, gw, gb, act="sigmoid", out=gy)
+
+    def ln_call(i):
+        lx, ly, lmean, lrstd = lsets[i & 1]
+        ops.layernorm(lx, out=ly, mean=lmean, rstd=lrstd)
+
+    gemm_ms = time_calls(gemm_call, args.aux_reps)
     gemm_tflops = 2.0 * gm * gn * gk / (gemm_ms * 1e-3) / 1e12
-    ln_ms = time_calls(lambda: ops.layernorm(lx, out=ly, mean=lmean, rstd=lrstd), args.aux_reps)
+    ln_ms = time_calls(ln_call, args.aux_reps)
     ln_bytes = gm * gk * (4 + 2) + gm * 8
     ln_gbs = ln_bytes / (ln_ms * 1e-3) / 1e9
-    del ga, gw, gy, lx, ly
+    del gsets, lsets
     clocks = sampler.stop()
 
     # ---- end to end through the public API with host buffers (pinned)
@@ -489,7 +585,7 @@ def run_ours(args):
     x1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = max_over_ranks(x0.elapsed_time(x1) / e2e_steps)
+    e2e_ms = max_over_ranks(x0.elapsed_time(x1) / e2e_steps, dev)
     e2e_value = world * FLOPS_PER_STEP / (e2e_ms * 1e-3) / 1e12
     h2d = 3 * B * H * S * D * 2
     d2h = B * H * S * D * 2
@@ -497,16 +593,21 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, thr, desc = cpu_prefill_sample(min_seconds=args.cpu_seconds)
-        cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port", "sample": desc}
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": thr, "kind": "port",
+               "cpu_model": cpu_model(), "sample": desc}
 
     peaks = load_peaks()
     models = {}
     if not args.no_model:
         from neurodsl_b200.model import GPT2_SMALL, GPT_24L_1024
-        models["gpt2_small"] = model_line("GPT-2 small", GPT2_SMALL, 16, 512, 256, 1, rank, world,
-                                          dev, pg, max_over_ranks, barrier, peaks, 2, 32)
-        models["gpt_24l_1024"] = model_line("24-layer", GPT_24L_1024, 32, 2048, 512, world, rank,
-                                            world, dev, pg, max_over_ranks, barrier, peaks, 2, 64)
+        models["gpt2_small"] = model_line("GPT-2 small", GPT2_SMALL, 16, 512, 256, 1, groups, dev,
+                                          peaks, 2, 32, False)
+        if world > 1:
+            # 12 heads: tensor parallel over at most 4 GPUs, data parallel beyond
+            models["gpt2_small_tp"] = model_line("GPT-2 small", GPT2_SMALL, 16, 512, 256,
+                                                 min(world, 4), groups, dev, peaks, 2, 32, True)
+        models["gpt_24l_1024"] = model_line("24-layer", GPT_24L_1024, 32, 2048, 512, world, groups,
+                                            dev, peaks, 2, 64, True)
     traffic = load_traffic("flash_fwd_causal_b8_h16_s2048_d64")
     dec_traffic = load_traffic("kv_decode_b64_h12_l1024_d64")
     if rank == 0:

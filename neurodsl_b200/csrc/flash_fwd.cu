@@ -446,16 +446,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       // This tile's products in the order S(0), S(1), P·V(0), S(2), P·V(1), ...
       // over all items, so each S is computed while the softmax works on the
       // previous one.  Every ring position and Q buffer is released by both
-      // issuers (barrier counts 2); a position this tile does not use (tile 0
-      // skips the last K/V tile of an item) is released once the position
-      // after it has landed, i.e. once the ring has moved past it.
+      // issuers (barrier counts 2).  A position this tile does not use (tile 0
+      // skips the last K/V tile of an item) is released once a later
+      // position has been seen landed — the producer loads in order, so the
+      // stage's previous phase has completed and the arrival counts for this
+      // position.  That is always true when the skip is recorded (the next
+      // item's first S, one position later, was issued before this item's
+      // last P·V), except after the CTA's last item, when nothing is loaded
+      // any more.
       Cursor c, p;
       start(c, 0, 0);
       p = c;
       int s_cnt = 0, pv_cnt = 0;
-      int skipped = -1;
-      // release the skipped position once a later one has been seen landed
-      auto release_skipped = [&](int landed) {
+      int skipped = -1;   // a position this tile skips, not yet released
+      int landed = -1;    // highest ring position seen landed
+      auto release_skipped = [&]() {
         if (skipped >= 0 && landed > skipped) {
           umma_commit(&bars->kv_empty[skipped % kStages]);
           skipped = -1;
@@ -469,7 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s_cnt > 0 && !mbar_wait(&bars->s_free[i], (s_cnt - 1) & 1, abort_flag)) { ok = false; break; }
           if (c.j == 0 && !mbar_wait(&bars->q_full[c.n & 1], (c.n >> 1) & 1, abort_flag)) { ok = false; break; }
           if (!mbar_wait(&bars->kv_full[pos % kStages], (pos / kStages) & 1, abort_flag)) { ok = false; break; }
-          release_skipped(pos);
+          landed = pos > landed ? pos : landed;
+          release_skipped();
           tc_fence_after();
           const int s = pos % kStages, qb = c.n & 1;
 #pragma unroll
@@ -489,7 +495,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const int pos = p.base + p.j;   // landed: its S product waited for it
           const int s = pos % kStages;
-          release_skipped(pos);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             const uint64_t b = sdesc_sw128(sV + s * kTileBytes + kk * 2048, 8192, 1024);
@@ -500,7 +505,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(&bars->o_done[i]);
           ++pv_cnt;
           umma_commit(&bars->kv_empty[s]);
-          if (p.j + 1 == p.nkv && p.nkv < p.total) skipped = p.base + p.nkv;
+          if (p.j + 1 == p.nkv && p.nkv < p.total) {
+            skipped = p.base + p.nkv;
+            release_skipped();
+          }
           advance(p);
         }
       }

@@ -112,3 +112,36 @@ def test_rejects_bad_strides():
     assert _strided_call(t, (64, 128 * 64, 64), t, hm, t, hm, o, hm, B, H) == 2
     # K head-major, V token-major
     assert _strided_call(t, hm, t, hm, t, tm, o, hm, B, H) == 2
+
+
+@pytest.mark.parametrize("B,H,S", [(16, 12, 512), (13, 12, 300)])
+@pytest.mark.parametrize("token_major", [True, False])
+def test_many_light_items_per_cta(B, H, S, token_major):
+    """More (batch, head) pairs than SMs with short sequences: a persistent CTA
+    processes several consecutive items of only one or two K/V tiles, whose
+    ring stages must be released in order (the first query tile skips the
+    last K/V tile of every item).  The kernel completes without a wait
+    deadline (device error word 0) and matches the oracle on the first and
+    last batch entries."""
+    ops = _ops()
+    ops.device_error()
+    q_np, q = _token_major(B, S, H, 31)
+    k_np, k = _token_major(B, S, H, 32)
+    v_np, v = _token_major(B, S, H, 33)
+    tr = lambda t: t.permute(0, 2, 1, 3)
+    if token_major:
+        o = torch.empty(B, S, H, 64, device="cuda", dtype=torch.bfloat16)
+        ops.flash_attn_fwd(tr(q), tr(k), tr(v), causal=True, out=tr(o))
+        got = tr(o)
+    else:
+        got = torch.empty(B, H, S, 64, device="cuda", dtype=torch.bfloat16)
+        ops.flash_attn_fwd(tr(q).contiguous(), tr(k).contiguous(), tr(v).contiguous(),
+                           causal=True, out=got)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    for b in (0, B - 1):
+        sel = lambda a: np.ascontiguousarray(a[b:b + 1].transpose(0, 2, 1, 3))
+        ref, _, _ = oracle.attn_bhsd(sel(q_np), sel(k_np), sel(v_np), causal=True)
+        g = got[b:b + 1].float().cpu().numpy()
+        assert np.abs(g - ref).max() <= MAX_ABS
+        assert rel_l2(g, ref) <= REL_L2
