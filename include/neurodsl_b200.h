@@ -43,6 +43,11 @@
  *                       src/kernels.jl:48-64,104-131, used by :rmsnorm
  *                       src/dispatch.jl:426-438)
  *   nd_convert_2d       Backend.to_device / Array() copies, src/backend.jl:20-26
+ *   nd_convert_2d_padded  the same, writing an inner dimension padded with zeros
+ *                       (the GEMMs' 16-byte rows; no reference counterpart)
+ *   nd_gather_rows      :embedding src/dispatch.jl:476-491 (on the device)
+ *   nd_copy_2d          :slice_cols src/dispatch.jl:544-553, :hcat_heads
+ *                       :349-361 and :identity (device copies between views)
  *   nd_embed            :embedding src/dispatch.jl:476-491 (on the device) plus the
  *                       learned-position add of the GPT-2 graph
  *   nd_argmax           the greedy argmax over LM-head logits (:matmul trans_b
@@ -77,6 +82,8 @@ extern "C" {
 /* ---- element types ---------------------------------------------------- */
 #define ND_F32 0
 #define ND_BF16 1
+#define ND_I32 2   /* index arrays only (nd_gather_rows) */
+#define ND_I64 3   /* index arrays only (nd_gather_rows) */
 
 /* ---- GEMM epilogue activation ------------------------------------------ */
 #define ND_ACT_NONE 0
@@ -287,6 +294,36 @@ int nd_layernorm(void *stream, const void *x, int x_dtype, const float *gamma, c
  */
 int nd_convert_2d(void *stream, const void *src, int src_dtype, int src_col_major, void *dst,
                   int dst_dtype, int rows, int cols);
+
+/*
+ * nd_convert_2d writing dst rows ld_dst elements apart (ld_dst >= cols), with
+ * columns [cols, ld_dst) set to zero: an operand whose inner dimension is
+ * not a multiple of 8 becomes a GEMM operand (16-byte rows) in one pass.
+ */
+int nd_convert_2d_padded(void *stream, const void *src, int src_dtype, int src_col_major,
+                         void *dst, int dst_dtype, int rows, int cols, int ld_dst);
+
+/*
+ * The :embedding op on the device: out[i][:] = table[idx[i] - index_base][:]
+ * for i < n.  table [vocab][d] and out [n][d] in dtype (ND_F32 or ND_BF16),
+ * row strides ld_table / ld_out elements; idx holds n indices of idx_dtype:
+ * ND_F32 (the reference's Float32 index arrays, 1-based with index_base 1),
+ * ND_I32 or ND_I64.  An index outside [index_base, index_base + vocab), or a
+ * Float32 index that is not an integer, gives a zero row and sets the device
+ * error word to 16 (read and cleared by nd_device_error); the call itself
+ * does not synchronise with the device.
+ */
+int nd_gather_rows(void *stream, const void *table, int dtype, long long ld_table, int vocab,
+                   const void *idx, int idx_dtype, int index_base, int n, int d, void *out,
+                   long long ld_out);
+
+/*
+ * dst[r][c] = src[r][c] for r < rows, c < cols, elements of elem_bytes (2 or
+ * 4), row strides ld_src / ld_dst elements: the :slice_cols, :hcat_heads and
+ * :identity copies between 2-D views (16-byte moves when the views allow).
+ */
+int nd_copy_2d(void *stream, const void *src, long long ld_src, void *dst, long long ld_dst,
+               int rows, int cols, int elem_bytes);
 
 /*
  * Token embedding with learned positions: y[t] = wte[ids[t]] + wpe[pos[t]].

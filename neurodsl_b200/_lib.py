@@ -24,6 +24,8 @@ ND_ERR_TIMEOUT = 8
 
 ND_F32 = 0
 ND_BF16 = 1
+ND_I32 = 2
+ND_I64 = 3
 
 ND_ACT_NONE = 0
 ND_ACT_GELU_SIGMOID = 1
@@ -63,6 +65,10 @@ SIGNATURES = {
     "nd_add": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i]),
     "nd_layernorm": (_i, [_vp, _vp, _i, _vp, _vp, _vp, _i, _vp, _vp, _i, _i, _f]),
     "nd_convert_2d": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i]),
+    "nd_convert_2d_padded": (_i, [_vp, _vp, _i, _i, _vp, _i, _i, _i, _i]),
+    "nd_gather_rows": (_i, [_vp, _vp, _i, ctypes.c_longlong, _i, _vp, _i, _i, _i, _i, _vp,
+                            ctypes.c_longlong]),
+    "nd_copy_2d": (_i, [_vp, _vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _i, _i, _i]),
     "nd_embed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "nd_argmax": (_i, [_vp, _vp, _i, ctypes.c_int64, _i, _i, _vp, _vp]),
     "nd_kv_store": (_i, [_vp, _vp, ctypes.c_int64, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i]),

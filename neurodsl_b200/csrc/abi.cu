@@ -150,9 +150,11 @@ template <> __device__ __forceinline__ __nv_bfloat16 cvt<float, __nv_bfloat16>(f
 template <> __device__ __forceinline__ float cvt<__nv_bfloat16, float>(__nv_bfloat16 v) { return __bfloat162float(v); }
 template <> __device__ __forceinline__ __nv_bfloat16 cvt<__nv_bfloat16, __nv_bfloat16>(__nv_bfloat16 v) { return v; }
 
+// dst rows are ld_dst elements apart; columns [cols, ld_dst) are written as
+// zeros (an inner dimension padded to the GEMM's 16-byte rows in the same pass).
 template <typename TS, typename TD, bool kColMajor>
 __global__ void convert_kernel(const TS* __restrict__ src, TD* __restrict__ dst, int rows,
-                               int cols) {
+                               int cols, int ld_dst) {
   __shared__ TS tile[32][33];
   const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
   if (kColMajor) {
@@ -170,18 +172,20 @@ __global__ void convert_kernel(const TS* __restrict__ src, TD* __restrict__ dst,
   __syncthreads();
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
     const int r = r0 + i, c = c0 + threadIdx.x;
-    if (r < rows && c < cols) dst[static_cast<size_t>(r) * cols + c] = cvt<TS, TD>(tile[i][threadIdx.x]);
+    if (r < rows && c < ld_dst)
+      dst[static_cast<size_t>(r) * ld_dst + c] =
+          c < cols ? cvt<TS, TD>(tile[i][threadIdx.x]) : cvt<float, TD>(0.f);
   }
 }
 
 template <typename TS, typename TD>
 cudaError_t launch_convert(cudaStream_t st, const void* src, void* dst, int rows, int cols,
-                           bool col_major) {
-  dim3 block(32, 8), grid((cols + 31) / 32, (rows + 31) / 32);
+                           bool col_major, int ld_dst) {
+  dim3 block(32, 8), grid((ld_dst + 31) / 32, (rows + 31) / 32);
   if (col_major)
-    convert_kernel<TS, TD, true><<<grid, block, 0, st>>>(static_cast<const TS*>(src), static_cast<TD*>(dst), rows, cols);
+    convert_kernel<TS, TD, true><<<grid, block, 0, st>>>(static_cast<const TS*>(src), static_cast<TD*>(dst), rows, cols, ld_dst);
   else
-    convert_kernel<TS, TD, false><<<grid, block, 0, st>>>(static_cast<const TS*>(src), static_cast<TD*>(dst), rows, cols);
+    convert_kernel<TS, TD, false><<<grid, block, 0, st>>>(static_cast<const TS*>(src), static_cast<TD*>(dst), rows, cols, ld_dst);
   return cudaGetLastError();
 }
 
@@ -675,25 +679,88 @@ __attribute__((visibility("default"))) int nd_layernorm(void* stream, const void
   return ok();
 }
 
-__attribute__((visibility("default"))) int nd_convert_2d(void* stream, const void* src,
-                                                         int src_dtype, int src_col_major,
-                                                         void* dst, int dst_dtype, int rows,
-                                                         int cols) {
-  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_convert_2d: negative size");
-  if (!valid_dtype(src_dtype) || !valid_dtype(dst_dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_convert_2d: bad dtype");
-  if (rows == 0 || cols == 0) return ok();
-  if (!src || !dst) return fail(ND_ERR_INVALID_ARG, "nd_convert_2d: null pointer");
-  if ((rows + 31) / 32 > 65535) return fail(ND_ERR_SHAPE, "nd_convert_2d: too many rows");
+static int convert_2d_impl(const char* fn, void* stream, const void* src, int src_dtype,
+                           int src_col_major, void* dst, int dst_dtype, int rows, int cols,
+                           int ld_dst) {
+  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "%s: negative size", fn);
+  if (ld_dst < cols) return fail(ND_ERR_SHAPE, "%s: ld_dst %d < cols %d", fn, ld_dst, cols);
+  if (!valid_dtype(src_dtype) || !valid_dtype(dst_dtype)) return fail(ND_ERR_UNSUPPORTED, "%s: bad dtype", fn);
+  if (rows == 0 || ld_dst == 0) return ok();
+  if (!dst || (cols > 0 && !src)) return fail(ND_ERR_INVALID_ARG, "%s: null pointer", fn);
+  if ((rows + 31) / 32 > 65535) return fail(ND_ERR_SHAPE, "%s: too many rows", fn);
   int rc = check_current_device(nullptr);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool cm = src_col_major != 0;
   cudaError_t e;
-  if (src_dtype == ND_F32 && dst_dtype == ND_F32) e = launch_convert<float, float>(st, src, dst, rows, cols, cm);
-  else if (src_dtype == ND_F32) e = launch_convert<float, __nv_bfloat16>(st, src, dst, rows, cols, cm);
-  else if (dst_dtype == ND_F32) e = launch_convert<__nv_bfloat16, float>(st, src, dst, rows, cols, cm);
-  else e = launch_convert<__nv_bfloat16, __nv_bfloat16>(st, src, dst, rows, cols, cm);
-  if (e != cudaSuccess) return cuda_fail(e, "nd_convert_2d");
+  if (src_dtype == ND_F32 && dst_dtype == ND_F32) e = launch_convert<float, float>(st, src, dst, rows, cols, cm, ld_dst);
+  else if (src_dtype == ND_F32) e = launch_convert<float, __nv_bfloat16>(st, src, dst, rows, cols, cm, ld_dst);
+  else if (dst_dtype == ND_F32) e = launch_convert<__nv_bfloat16, float>(st, src, dst, rows, cols, cm, ld_dst);
+  else e = launch_convert<__nv_bfloat16, __nv_bfloat16>(st, src, dst, rows, cols, cm, ld_dst);
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_convert_2d(void* stream, const void* src,
+                                                         int src_dtype, int src_col_major,
+                                                         void* dst, int dst_dtype, int rows,
+                                                         int cols) {
+  return convert_2d_impl("nd_convert_2d", stream, src, src_dtype, src_col_major, dst, dst_dtype,
+                         rows, cols, cols);
+}
+
+__attribute__((visibility("default"))) int nd_convert_2d_padded(void* stream, const void* src,
+                                                                int src_dtype, int src_col_major,
+                                                                void* dst, int dst_dtype, int rows,
+                                                                int cols, int ld_dst) {
+  return convert_2d_impl("nd_convert_2d_padded", stream, src, src_dtype, src_col_major, dst,
+                         dst_dtype, rows, cols, ld_dst);
+}
+
+__attribute__((visibility("default"))) int nd_gather_rows(void* stream, const void* table,
+                                                          int dtype, long long ld_table, int vocab,
+                                                          const void* idx, int idx_dtype,
+                                                          int index_base, int n, int d, void* out,
+                                                          long long ld_out) {
+  if (n < 0 || d < 0 || vocab < 0) return fail(ND_ERR_INVALID_ARG, "nd_gather_rows: negative size");
+  if (!valid_dtype(dtype)) return fail(ND_ERR_UNSUPPORTED, "nd_gather_rows: bad dtype %d", dtype);
+  if (idx_dtype != ND_F32 && idx_dtype != ND_I32 && idx_dtype != ND_I64)
+    return fail(ND_ERR_UNSUPPORTED, "nd_gather_rows: bad index dtype %d", idx_dtype);
+  if (ld_table < d || ld_out < d)
+    return fail(ND_ERR_SHAPE, "nd_gather_rows: row strides (%lld, %lld) below d = %d", ld_table,
+                ld_out, d);
+  if (n == 0 || d == 0) return ok();
+  if (!table || !idx || !out) return fail(ND_ERR_INVALID_ARG, "nd_gather_rows: null pointer");
+  if (vocab == 0) return fail(ND_ERR_SHAPE, "nd_gather_rows: empty table");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_gather_rows(static_cast<cudaStream_t>(stream), table,
+                                         dtype == ND_F32 ? 4 : 2, ld_table, vocab, idx,
+                                         idx_dtype == ND_F32 ? 0 : idx_dtype == ND_I32 ? 1 : 2,
+                                         index_base, n, d, out, ld_out, nd::device_error_word());
+  if (e != cudaSuccess) return cuda_fail(e, "nd_gather_rows");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_copy_2d(void* stream, const void* src,
+                                                      long long ld_src, void* dst,
+                                                      long long ld_dst, int rows, int cols,
+                                                      int elem_bytes) {
+  if (rows < 0 || cols < 0) return fail(ND_ERR_INVALID_ARG, "nd_copy_2d: negative size");
+  if (elem_bytes != 2 && elem_bytes != 4)
+    return fail(ND_ERR_UNSUPPORTED, "nd_copy_2d: element size %d (2 or 4)", elem_bytes);
+  if (ld_src < cols || ld_dst < cols)
+    return fail(ND_ERR_SHAPE, "nd_copy_2d: row strides (%lld, %lld) below cols = %d", ld_src,
+                ld_dst, cols);
+  if (rows == 0 || cols == 0) return ok();
+  if (!src || !dst) return fail(ND_ERR_INVALID_ARG, "nd_copy_2d: null pointer");
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % elem_bytes)
+    return fail(ND_ERR_ALIGNMENT, "nd_copy_2d: pointers not aligned to the element size");
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_copy_2d(static_cast<cudaStream_t>(stream), src, ld_src, dst, ld_dst,
+                                     rows, cols, elem_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "nd_copy_2d");
   return ok();
 }
 

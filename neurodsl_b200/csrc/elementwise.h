@@ -18,6 +18,18 @@ cudaError_t launch_scale_mask(cudaStream_t stream, const float* x, float* y, int
 cudaError_t launch_add(cudaStream_t stream, const float* a, const float* b, float* y, int rows,
                        int cols, int mode);
 
+// out[i][:] = table[idx[i] - base][:] for i < n (d elements of elem_bytes 4
+// or 2, row strides in elements); idx_kind 0: float indices, 1: int32,
+// 2: int64.  Bad indices give zero rows and set *err_word.
+cudaError_t launch_gather_rows(cudaStream_t stream, const void* table, int elem_bytes,
+                               long long ld_table, int vocab, const void* idx, int idx_kind,
+                               int base, int n, int d, void* out, long long ld_out, int* err_word);
+
+// dst[r][c] = src[r][c], rows x cols elements of elem_bytes (2 or 4), row
+// strides in elements.
+cudaError_t launch_copy_2d(cudaStream_t stream, const void* src, long long ld_src, void* dst,
+                           long long ld_dst, int rows, int cols, int elem_bytes);
+
 // Row softmax of [rows][cols] fp32 (rows of -Inf give zeros).
 cudaError_t launch_softmax(cudaStream_t stream, const float* x, float* y, int rows, int cols);
 

@@ -74,25 +74,40 @@ struct GemmBars {
 constexpr float kGeluC0 = 0.7978845608028654f;
 constexpr float kGeluC1 = 0.7978845608028654f * 0.044715f;
 
+// 1 / x on the special-function unit (relative error about 2^-23).
+__device__ __forceinline__ float fast_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // The activation of two pre-activation values, packed as f32x2.
 //   sigmoid form  z·σ(1.702 z) = ½z + ½z·tanh(0.851 z), using the identity
-//                 σ(a) = (1 + tanh(a/2)) / 2: one hardware tanh per value;
-//   tanh form     ½z (1 + tanh(√(2/π) (z + 0.044715 z³)));
+//                 σ(a) = (1 + tanh(a/2)) / 2: one hardware tanh per value
+//                 (relative error about 2^-11; this form is the throughput one);
+//   tanh form     ½z (1 + tanh(u)), u = √(2/π) (z + 0.044715 z³), evaluated
+//                 as z·σ(2u) = z / (1 + 2^(-2u·log2 e)) with the hardware
+//                 exp2 and reciprocal (relative error about 1e-6), so the bf16
+//                 activations round as the fp32 definition does — the
+//                 decoders use this form, and a 2^-11 error in every layer's
+//                 MLP activations shows up in 12-layer logits;
 //   erf form      ½z (1 + erf(z / √2)) (CUDA's erff).
 template <int kAct>
 __device__ __forceinline__ uint64_t act2(uint64_t z) {
-  if constexpr (kAct == ND_ACT_GELU_SIGMOID || kAct == ND_ACT_GELU_TANH) {
+  if constexpr (kAct == ND_ACT_GELU_SIGMOID) {
     const uint64_t hz = f2_mul(z, f2_pack(0.5f, 0.5f));
-    uint64_t u;
-    if constexpr (kAct == ND_ACT_GELU_SIGMOID) {
-      u = f2_mul(z, f2_pack(0.851f, 0.851f));
-    } else {
-      const uint64_t c = f2_fma(f2_mul(z, z), f2_pack(kGeluC1, kGeluC1), f2_pack(kGeluC0, kGeluC0));
-      u = f2_mul(c, z);
-    }
+    const uint64_t u = f2_mul(z, f2_pack(0.851f, 0.851f));
     float u0, u1;
     f2_unpack(u, u0, u1);
     return f2_fma(hz, f2_pack(tanh_approx(u0), tanh_approx(u1)), hz);
+  } else if constexpr (kAct == ND_ACT_GELU_TANH) {
+    constexpr float kM2Log2e = -2.0f * 1.4426950408889634f;
+    const uint64_t c = f2_fma(f2_mul(z, z), f2_pack(kGeluC1 * kM2Log2e, kGeluC1 * kM2Log2e),
+                              f2_pack(kGeluC0 * kM2Log2e, kGeluC0 * kM2Log2e));
+    float t0, t1, z0, z1;
+    f2_unpack(f2_mul(c, z), t0, t1);   // -2u·log2 e
+    f2_unpack(z, z0, z1);
+    return f2_pack(z0 * fast_rcp(1.f + fast_exp2(t0)), z1 * fast_rcp(1.f + fast_exp2(t1)));
   } else if constexpr (kAct == ND_ACT_GELU_ERF) {
     float z0, z1;
     f2_unpack(z, z0, z1);

@@ -38,6 +38,7 @@ import warnings
 from collections import deque
 from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, List, Optional
+import weakref
 
 import torch
 
@@ -400,21 +401,55 @@ def defop(name: str):
 
 # ----------------------------------------------------------- op helpers ---
 
+def _ceil8(k):
+    return (k + 7) // 8 * 8
+
+
 def _bf16_rows(x):
-    """A 2-D operand as contiguous bf16 (converted on the device by the library)."""
-    if x.dtype == torch.bfloat16 and x.is_contiguous():
-        return x
+    """A 2-D GEMM operand as contiguous bf16 rows whose length is a multiple
+    of 8 (converted on the device by the library, the zero columns of an
+    inner dimension that is not a multiple of 8 written in the same pass:
+    the GEMM moves rows in 16-byte pieces, and zero columns add nothing to
+    the dot products, so graphs with any inner dimension — the reference's
+    tests use K = 3 — run on the same kernel)."""
     rows, cols = x.shape
-    return ops.convert_2d(x.contiguous(), rows, cols, False, torch.bfloat16)
+    if x.dtype == torch.bfloat16 and x.is_contiguous() and cols % 8 == 0:
+        return x
+    return ops.convert_2d_padded(x.contiguous(), rows, cols, False, torch.bfloat16, _ceil8(cols))
 
 
-def _weight_nk(W, trans_b):
-    """The weight as [N][K] bf16: trans_b=true weights already are; a (K, N)
-    row-major matrix is the column-major (N, K) one and is converted."""
+def _convert_weight_nk(W, trans_b):
     if trans_b:
         return _bf16_rows(W)
     K, N = W.shape
-    return ops.convert_2d(W.contiguous(), N, K, True, torch.bfloat16)
+    return ops.convert_2d_padded(W.contiguous(), N, K, True, torch.bfloat16, _ceil8(K))
+
+
+# bf16 [N][K] copies of Float32 weights, per weight tensor: a node's value is
+# converted once and reused by every later call until the tensor is replaced
+# (set!) or written in place (its version counter moves).
+_WEIGHT_CACHE = {}
+
+
+def _weight_nk(W, trans_b):
+    """The weight as [N][K] bf16 (K padded to a multiple of 8): trans_b=true
+    weights already are; a (K, N) row-major matrix is the column-major (N, K)
+    one and is converted.  Cached per tensor (see _WEIGHT_CACHE)."""
+    if W.dtype == torch.bfloat16 and trans_b and W.is_contiguous() and W.shape[1] % 8 == 0:
+        return W
+    key = id(W)
+    hit = _WEIGHT_CACHE.get(key)
+    if hit is not None:
+        ref, version, tb, conv = hit
+        if ref() is W and version == W._version and tb == trans_b:
+            return conv
+    conv = _convert_weight_nk(W, trans_b)
+    try:
+        ref = weakref.ref(W, lambda _r, k=key: _WEIGHT_CACHE.pop(k, None))
+    except TypeError:
+        return conv
+    _WEIGHT_CACHE[key] = (ref, W._version, trans_b, conv)
+    return conv
 
 
 def _bias_vec(b):
@@ -423,20 +458,16 @@ def _bias_vec(b):
     return b.reshape(-1).to(torch.float32).contiguous()
 
 
-def _pad_k(t):
-    """bf16 [rows][K] operand with zero columns up to a multiple of 8: the
-    GEMM moves rows in 16-byte pieces, and the zero columns add nothing to
-    the dot products, so graphs with any inner dimension (the reference's
-    tests use K = 3) run on the same kernel."""
-    K = t.shape[1]
-    return t if K % 8 == 0 else torch.nn.functional.pad(t, (0, 8 - K % 8))
-
-
 def _gemm_into(out, X, Wnk, bias=None, residual=None, act="none"):
     if out.dtype not in (torch.float32, torch.bfloat16) or not out.is_contiguous():
         raise NeuroDSLError(4, "output buffer must be contiguous fp32 or bf16")
-    ops.linear(_pad_k(_bf16_rows(X)), _pad_k(Wnk), _bias_vec(bias), residual=residual, act=act,
-               out=out)
+    ops.linear(_bf16_rows(X), Wnk, _bias_vec(bias), residual=residual, act=act, out=out)
+
+
+def _copy_back(buf, out):
+    """The side buffer of an aliased output copied into the node's buffer."""
+    rows = out.shape[0] if out.dim() else 1
+    ops.copy_2d(buf.reshape(rows, -1), out.view(rows, -1))
 
 
 def _alias_safe(out, out_node, inputs):
@@ -468,7 +499,7 @@ def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, 
         buf, aliased = _alias_safe(output_buffer, out_node, inputs)
         _gemm_into(buf, A, _weight_nk(B, tb))
         if aliased:
-            output_buffer.copy_(buf)
+            _copy_back(buf, output_buffer)
         _store_ctx(ctx_store, out_sym, {"trans_b": tb, "A": A.clone() if ctx_store is not None else A,
                                         "B": B})
         return output_buffer
@@ -482,9 +513,9 @@ def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, 
         X, W = inputs[0], inputs[1]
         bias = inputs[2] if len(inputs) == 3 else None
         buf, aliased = _alias_safe(output_buffer, out_node, inputs)
-        _gemm_into(buf, X, _bf16_rows(W), bias=bias)
+        _gemm_into(buf, X, _weight_nk(W, True), bias=bias)
         if aliased:
-            output_buffer.copy_(buf)
+            _copy_back(buf, output_buffer)
         _store_ctx(ctx_store, out_sym, {"X": X, "W": W, "n_inputs": len(inputs)})
         return output_buffer
     if op == "slice_cols":
@@ -493,25 +524,26 @@ def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, 
         # of a multi-head layer into the strided :flash_attention instead.
         x = inputs[0]
         s, e = attrs.get("start_col", 1), attrs.get("end_col", x.shape[1])
-        output_buffer.copy_(x[:, s - 1:e])
+        ops.copy_2d(x[:, s - 1:e], output_buffer)
         _store_ctx(ctx_store, out_sym, {"start_col": s, "end_col": e})
         return output_buffer
     if op == "embedding":
         # rows idx[i] (1-based, as the reference's Julia indices) of the table
         # E (vocab, d), src/dispatch.jl:476-491, gathered on the device where
         # the reference copies through the host; ctx {idx, E_size}
+        # (nd_gather_rows: an index outside 1..vocab gives a zero row and sets
+        # the device error word, read by ops.device_error(); no host sync)
         E, idx = inputs[0], inputs[1]
-        rows = idx.reshape(-1).to(device=E.device, dtype=torch.int64) - 1
-        if rows.numel() and bool(((rows < 0) | (rows >= E.shape[0])).any()):
-            raise NeuroDSLError(2, f"[{out_sym}] embedding index outside 1..{E.shape[0]}")
-        torch.index_select(E, 0, rows, out=output_buffer)
-        _store_ctx(ctx_store, out_sym, {"idx": rows + 1, "E_size": tuple(E.shape)})
+        if idx.device != E.device:
+            raise NeuroDSLError(2, f"[{out_sym}] embedding indices must be on the table's device")
+        ops.gather_rows(E, idx, index_base=1, out=output_buffer)
+        _store_ctx(ctx_store, out_sym, {"idx": idx.reshape(-1), "E_size": tuple(E.shape)})
         return output_buffer
     if op == "hcat_heads":
         # the heads' (N, d_h) outputs side by side, src/dispatch.jl:349-361
         off = 0
         for x in inputs:
-            output_buffer[:, off:off + x.shape[1]].copy_(x)
+            ops.copy_2d(x, output_buffer[:, off:off + x.shape[1]])
             off += x.shape[1]
         _store_ctx(ctx_store, out_sym, {"n_heads": len(inputs), "d_head": inputs[0].shape[1]})
         return output_buffer
@@ -519,7 +551,8 @@ def _dispatch_op(dev, output_buffer, op: str, inputs, attrs, out_sym, out_node, 
         CUSTOM_OPS[op](dev, output_buffer, inputs, attrs, out_sym, out_node, ctx_store)
         return output_buffer
     if op == "identity":
-        output_buffer.copy_(inputs[0])
+        x = inputs[0]
+        ops.copy_2d(x.reshape(x.shape[0], -1), output_buffer.view(x.shape[0], -1))
         return output_buffer
     raise NeuroDSLError(4, f"Opérateur inconnu : :{op}. Utilisez register_op! pour enregistrer "
                            "un op custom.")
@@ -600,7 +633,7 @@ def _dispatch_flash_attention(dev, output_buffer, inputs, attrs, out_sym, out_no
                        out=_token_major_view(buf, S, H, D), lse=lse.view(1, H, S),
                        row_max=m.view(1, H, S))
     if aliased:
-        output_buffer.copy_(buf)
+        _copy_back(buf, output_buffer)
     _store_ctx(ctx_store, out_sym, {"Q": q, "K": k, "V": v, "out": output_buffer,
                                     "l": lse, "m": m, "d_head": D, "causal": causal,
                                     "n_heads": H})
@@ -750,7 +783,7 @@ def _dispatch_fused_layernorm_linear(dev, output_buffer, inputs, attrs, out_sym,
             h = torch.empty((rows, K), dtype=torch.bfloat16, device=dev.torch_device)
             out_node.aux_data["_ln_buf"] = h
         ops.layernorm(x.contiguous(), g, bt, eps=eps, out=h, stats=False)
-        ops.linear(_pad_k(h), _pad_k(Wnk), _bias_vec(b), out=output_buffer)
+        ops.linear(_bf16_rows(h), Wnk, _bias_vec(b), out=output_buffer)
     _store_ctx(ctx_store, out_sym, {"x": x, "gamma": gamma, "beta": beta, "W": W})
     return output_buffer
 

@@ -375,6 +375,67 @@ def convert_2d(src, rows, cols, src_col_major, dst_dtype, out=None, stream=None)
     return out
 
 
+def convert_2d_padded(src, rows, cols, src_col_major, dst_dtype, ld_dst, out=None, stream=None):
+    """convert_2d into rows of ld_dst >= cols elements, the columns past cols
+    zero (nd_convert_2d_padded): [rows][ld_dst]."""
+    _need(src, "src")
+    if src.numel() != rows * cols:
+        raise ValueError("src size != rows*cols")
+    if out is None:
+        out = torch.empty((rows, ld_dst), dtype=dst_dtype, device=src.device)
+    if tuple(out.shape) != (rows, ld_dst) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [rows][ld_dst] matrix")
+    check(_lib.load().nd_convert_2d_padded(_stream(stream), _ptr(src), _DT[src.dtype],
+                                           int(bool(src_col_major)), _ptr(out), _DT[out.dtype],
+                                           rows, cols, ld_dst))
+    return out
+
+
+_IDX_DT = {torch.float32: _lib.ND_F32, torch.int32: _lib.ND_I32, torch.int64: _lib.ND_I64}
+
+
+def gather_rows(table, idx, index_base=1, out=None, stream=None):
+    """out[i] = table[idx[i] - index_base] on the device (nd_gather_rows: the
+    :embedding op).  table [vocab][d] fp32 or bf16 with unit column stride;
+    idx any shape of float32 / int32 / int64 indices on the device.  A bad
+    index gives a zero row and sets the device error word (device_error()),
+    without a host synchronisation."""
+    if table.dim() != 2 or table.stride(1) != 1:
+        raise ValueError("table must be 2-D with contiguous rows")
+    if table.dtype not in _DT:
+        raise ValueError(f"table dtype {table.dtype} not supported")
+    if idx.dtype not in _IDX_DT:
+        raise ValueError(f"index dtype {idx.dtype} not supported")
+    if idx.device != table.device:
+        raise ValueError("indices and table must be on the same device")
+    idx = idx.reshape(-1).contiguous()
+    n = idx.numel()
+    vocab, d = table.shape
+    if out is None:
+        out = torch.empty((n, d), dtype=table.dtype, device=table.device)
+    if out.dim() != 2 or tuple(out.shape) != (n, d) or out.stride(1) != 1 or out.dtype != table.dtype:
+        raise ValueError("out must be an [n][d] matrix of the table's dtype with contiguous rows")
+    check(_lib.load().nd_gather_rows(_stream(stream), _ptr(table), _DT[table.dtype],
+                                     table.stride(0), vocab, _ptr(idx), _IDX_DT[idx.dtype],
+                                     int(index_base), n, d, _ptr(out), out.stride(0)))
+    return out
+
+
+def copy_2d(src, dst, stream=None):
+    """dst[:, :] = src[:, :] for 2-D views with unit column strides
+    (nd_copy_2d: the :slice_cols, :hcat_heads and :identity copies)."""
+    for name, t in (("src", src), ("dst", dst)):
+        if t.dim() != 2 or (t.shape[1] > 1 and t.stride(1) != 1):
+            raise ValueError(f"{name} must be 2-D with contiguous rows")
+    if tuple(src.shape) != tuple(dst.shape) or src.dtype != dst.dtype:
+        raise ValueError("src and dst differ in shape or dtype")
+    rows, cols = src.shape
+    ld = lambda t: t.stride(0) if rows > 1 else cols
+    check(_lib.load().nd_copy_2d(_stream(stream), _ptr(src), ld(src), _ptr(dst), ld(dst), rows,
+                                 cols, src.element_size()))
+    return dst
+
+
 def device_error():
     """Read and clear the device error word (non-zero after a timed-out wait)."""
     c = ctypes.c_int(0)

@@ -211,7 +211,7 @@ def bf16_round(a):
     return out
 
 
-def gpt_last_logits(W, ids, act="tanh", eps=1e-5, reduce=None):
+def gpt_last_logits(W, ids, act="tanh", eps=1e-5, reduce=None, last_k=1):
     """LM-head logits of the last position of each sequence ids [B][T] for a
     pre-LayerNorm GPT decoder — the composition of the reference's GPT-2 graph
     (notebook/GPT2.ipynb cells 4 and 10): token + position :embedding
@@ -230,6 +230,11 @@ def gpt_last_logits(W, ids, act="tanh", eps=1e-5, reduce=None):
     of a tensor-parallel split (identity for one rank).  Values that the GPU
     path stores in bf16 are rounded to bf16 at the same points, so the two
     differ only in accumulation order and approximate functions.
+
+    Returns the logits of the last position of each sequence, [B][V_local];
+    with last_k > 1, those of the last last_k positions, [B][last_k][V_local]
+    (the causal model's predictions after each of those positions, so one
+    pass over a prompt plus generated tokens checks every decode step).
     """
     ids = np.asarray(ids)
     B, T = ids.shape
@@ -258,5 +263,7 @@ def gpt_last_logits(W, ids, act="tanh", eps=1e-5, reduce=None):
         nxt = W["layers"][i + 1] if i + 1 < n else None
         g, be = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (W["lnf_g"], W["lnf_b"])
         h = bf16_round(layernorm(x, g, be, eps)[0])
-    last = h.reshape(B, T, -1)[:, -1]
-    return linear(last, W["w_head"])
+    if last_k == 1:
+        return linear(h.reshape(B, T, -1)[:, -1], W["w_head"])
+    last = h.reshape(B, T, -1)[:, -last_k:].reshape(B * last_k, -1)
+    return linear(last, W["w_head"]).reshape(B, last_k, -1)

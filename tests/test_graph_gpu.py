@@ -208,9 +208,14 @@ def test_matmul_trans_b_false_and_linear_alias():
 
 
 def test_embedding_op_on_the_device():
-    """:embedding gathers Float32 rows of E by 1-based indices on the device,
-    exactly; an index past the table raises."""
+    """:embedding (src/dispatch.jl:476-491) gathers Float32 rows of E by
+    1-based Float32 indices on the device (nd_gather_rows), exactly, with the
+    reference's ctx {idx, E_size}.  An index past the table, or one that is
+    not an integer, gives a zero row and sets the device error word (16)
+    instead of synchronising the host; good calls leave the word at 0."""
+    from neurodsl_b200 import ops
     g_ = G()
+    ops.device_error()
     rng = np.random.default_rng(21)
     E = rng.standard_normal((50, 64)).astype(np.float32)
     idx = np.array([3, 50, 1, 7, 7], np.float32)
@@ -218,10 +223,68 @@ def test_embedding_op_on_the_device():
     g_.set_(g, "E", E, is_param=True)
     g_.set_(g, "idx", idx)
     g_.addrule(g, g_.GraphRule("emb", ["E", "idx"], "embedding"))
-    out = g_.demand(g, "emb")
+    ctx = g_.CtxStore()
+    out = g_.demand(g, "emb", ctx_store=ctx)
     assert out.is_cuda
     np.testing.assert_array_equal(out.cpu().numpy(), E[idx.astype(np.int64) - 1])
-    from neurodsl_b200._lib import NeuroDSLError
-    g_.set_(g, "idx", np.array([51], np.float32))
-    with pytest.raises(NeuroDSLError):
-        g_.demand(g, "emb")
+    assert ctx["emb"]["E_size"] == (50, 64)
+    assert ctx["emb"]["idx"].cpu().tolist() == [3, 50, 1, 7, 7]
+    assert ops.device_error() == 0
+    for bad in ([51.0], [0.0], [2.5]):
+        g_.set_(g, "idx", np.array([1.0] + bad, np.float32))
+        out = g_.demand(g, "emb").cpu().numpy()
+        np.testing.assert_array_equal(out[0], E[0])
+        assert not out[1].any()
+        assert ops.device_error() == 16
+
+
+def test_copy_ops_run_on_the_library():
+    """:slice_cols, :hcat_heads and :identity (src/dispatch.jl:544-553,
+    :349-361) are device copies by nd_copy_2d: the sliced columns, the heads
+    side by side and the input itself, bit for bit; odd widths and offsets
+    take the narrower copy units."""
+    g_ = G()
+    rng = np.random.default_rng(22)
+    X = rng.standard_normal((37, 130)).astype(np.float32)
+    g = g_.NeuroGraph()
+    g_.set_(g, "X", X)
+    g_.addrule(g, g_.GraphRule("s1", ["X"], "slice_cols", {"start_col": 1, "end_col": 64}))
+    g_.addrule(g, g_.GraphRule("s2", ["X"], "slice_cols", {"start_col": 66, "end_col": 130}))
+    g_.addrule(g, g_.GraphRule("s3", ["X"], "slice_cols", {"start_col": 3, "end_col": 3}))
+    g_.addrule(g, g_.GraphRule("cat", ["s1", "s2", "s3"], "hcat_heads"))
+    g_.addrule(g, g_.GraphRule("same", ["X"], "identity"))
+    cat = g_.demand(g, "cat").cpu().numpy()
+    np.testing.assert_array_equal(cat, np.concatenate([X[:, :64], X[:, 65:130], X[:, 2:3]], axis=1))
+    np.testing.assert_array_equal(g_.demand(g, "same").cpu().numpy(), X)
+
+
+def test_linear_weight_converted_once_and_refreshed_on_change():
+    """A :linear weight node's bf16 copy is made once and reused by later
+    runs; replacing the node's value (set!) or writing the tensor in place
+    makes the next run convert again, so results follow the weight.  K = 13
+    is padded to 16 in the same conversion."""
+    from neurodsl_b200 import graph as GR
+    g_ = G()
+    rng = np.random.default_rng(23)
+    X = oracle.bf16_round(rng.standard_normal((64, 13)).astype(np.float32))
+    W = oracle.bf16_round((0.1 * rng.standard_normal((24, 13))).astype(np.float32))
+    g = g_.NeuroGraph()
+    g_.set_(g, "X", X)
+    g_.set_(g, "W", W, is_param=True)
+    g_.addrule(g, g_.GraphRule("Y", ["X", "W"], "linear"))
+    y1 = g_.demand(g, "Y").cpu().numpy()
+    Wt = g.nodes["default"]["W"].value
+    hit = GR._WEIGHT_CACHE.get(id(Wt))
+    assert hit is not None and hit[3].shape == (24, 16)
+    conv = hit[3]
+    g_.set_(g, "X", X * 2)                 # recompute with the same weight
+    y2 = g_.demand(g, "Y").cpu().numpy()
+    assert GR._WEIGHT_CACHE[id(Wt)][3] is conv
+    np.testing.assert_allclose(y2, 2 * y1, rtol=1e-5, atol=1e-6)
+    Wt.mul_(2)                             # in place: the version moves
+    g_.set_(g, "X", X)
+    y3 = g_.demand(g, "Y").cpu().numpy()
+    np.testing.assert_allclose(y3, 2 * y1, rtol=1e-5, atol=1e-6)
+    g_.set_(g, "W", -W, is_param=True)     # a new tensor
+    y4 = g_.demand(g, "Y").cpu().numpy()
+    np.testing.assert_allclose(y4, -y1, rtol=1e-5, atol=1e-6)
