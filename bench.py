@@ -667,6 +667,98 @@ def run_ours(args):
     return 0
 
 
+def run_decoder_only(args):
+    """A short eager run of one decoder (prefill, then `--decoder-steps`
+    greedy decode steps, one launch per kernel, no CUDA graphs) for ncu
+    captures of the decode-step kernels; prints one line of step times."""
+    import torch
+
+    from neurodsl_b200.model import GPT, GPT2_SMALL, GPT_24L_1024
+    cfg, B, S = {"gpt2_small": (GPT2_SMALL, 16, 512),
+                 "gpt_24l_1024": (GPT_24L_1024, 32, 2048)}[args.decoder_only]
+    torch.cuda.set_device(0)
+    model = GPT(cfg, seed=0)
+    gen = torch.Generator(device="cuda").manual_seed(99)
+    ids = torch.randint(0, cfg.vocab, (B, S), device="cuda", dtype=torch.int32, generator=gen)
+    n = max(2, args.decoder_steps)
+    model.prefill(ids, n + 1)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
+    ev[0].record()
+    for t in range(n):
+        model.decode_step(t)
+        ev[t + 1].record()
+    torch.cuda.synchronize()
+    us = [ev[t].elapsed_time(ev[t + 1]) * 1e3 for t in range(n)]
+    print(json.dumps({"decoder": args.decoder_only, "batch": B, "prompt": S,
+                      "eager_decode_step_us": us}), flush=True)
+    return 0
+
+
+def run_comm_bench(args):
+    """The tensor-parallel reduction of a decode step on its own (torchrun,
+    one rank per GPU): rows x d bf16 partial sums combined with the residual
+    add, bias and LayerNorm by the NVLink kernel (nd_allreduce_add_layernorm),
+    against an NCCL all-reduce of the same bytes followed by the library's
+    add + LayerNorm; CUDA-event times over back-to-back calls, max over
+    ranks.  Prints one JSON line on rank 0."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from neurodsl_b200 import ops
+    from neurodsl_b200.comm import PeerReduce
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    rows, d, n = 32, 1024, 500
+    x = torch.randn(rows, d, device=dev).bfloat16()
+    h = torch.empty_like(x)
+    bias = torch.zeros(d, device=dev)
+    g = torch.ones(d, device=dev)
+    bt = torch.zeros(d, device=dev)
+    pr = PeerReduce(rows, d, device=dev)
+    for _ in range(2):
+        pr.partial(rows).copy_(x)
+        pr.k ^= 1
+    buf = torch.randn(rows, d, device=dev).bfloat16()
+
+    def timed(fn):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) * 1e3 / n, dev)
+
+    def nvlink():
+        pr.add_layernorm(x, bias, g, bt, 1e-5, x, h)
+
+    def nccl():
+        dist.all_reduce(buf)
+        ops.add_layernorm(x, buf, bias, g, bt, 1e-5, s_out=x, out=h)
+
+    res = {"workload": f"tensor-parallel reduction of {rows} x {d} bf16 partial sums + residual "
+                       f"+ bias + LayerNorm, {world} ranks",
+           "nvlink_fused_us": timed(nvlink)}
+    with ops.pdl(True):
+        res["nvlink_fused_pdl_us"] = timed(nvlink)
+    res["nccl_allreduce_then_add_layernorm_us"] = timed(nccl)
+    res["device_error"] = ops.device_error()
+    pr.close()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -681,11 +773,20 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the GPT-2-small and 24-layer decoder lines")
+    ap.add_argument("--decoder-only", choices=["gpt2_small", "gpt_24l_1024"],
+                    help="only a short eager run of this decoder (for kernel profiles)")
+    ap.add_argument("--decoder-steps", type=int, default=4)
+    ap.add_argument("--comm-bench", action="store_true",
+                    help="only the tensor-parallel reduction microbenchmark (torchrun)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.decoder_only:
+        return run_decoder_only(args)
+    if args.comm_bench:
+        return run_comm_bench(args)
     return run_ours(args)
 
 

@@ -378,7 +378,9 @@ int nd_add_layernorm(void *stream, const void *x, const void *p, int p_dtype, co
  * every rank calls nd_allreduce_add_layernorm with the same arguments except
  * `rank` (regions[r] = rank r's region as mapped in this process) and gets
  *   s_out = x + Σ_r partial_r + bias (bf16),  y = LayerNorm(s_out)
- * computed with the same bits on every rank.  Calls must alternate slots
+ * computed with the same bits on every rank.  The call pushes the partial
+ * into a receive area of every peer's region over NVLink and then reads only
+ * local memory.  Calls must alternate slots
  * (0, 1, 0, ...), every rank makes the same calls in the same order, and a
  * peer that does not arrive within the library's wait limit (2 s) leaves
  * garbage in the outputs and sets the device error word (nd_device_error).

@@ -209,8 +209,27 @@ __global__ void kv_store_kernel(const __nv_bfloat16* __restrict__ src, long long
 // One warp per row, the row in registers (d <= 2048, d % 8 == 0).
 // s = x + p (+ bias) is rounded to bf16 and written to s_out (which may be x
 // itself: every thread reads its 16-byte pieces of x before writing them),
-// and y = (s - mean) * rstd * gamma + beta over the stored s.
-template <typename TP, int kMaxVec>
+// and y = (s - mean) * rstd * gamma + beta over the stored s.  All of a row's
+// x and p loads are issued before any arithmetic or store; with kVecParams
+// (bias, gamma and beta 16-byte aligned) the parameters are read as float4.
+template <bool kVecParams>
+__device__ __forceinline__ void ld_param8(const float* __restrict__ v, int c, float dflt,
+                                          float (&o)[8]) {
+  if (v == nullptr) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = dflt;
+  } else if constexpr (kVecParams) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(v) + 2 * c);
+    const float4 b = __ldg(reinterpret_cast<const float4*>(v) + 2 * c + 1);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = __ldg(v + c * 8 + e);
+  }
+}
+
+template <typename TP, int kMaxVec, bool kVecParams>
 __global__ void __launch_bounds__(256)
     add_ln_kernel(const __nv_bfloat16* x, const TP* __restrict__ p,
                   const float* __restrict__ bias, const float* __restrict__ gamma,
@@ -223,24 +242,36 @@ __global__ void __launch_bounds__(256)
   if (row >= rows) return;
   const int nvec = d >> 3;
   const size_t off = static_cast<size_t>(row) * d;
+  constexpr int kPV = sizeof(TP) == 4 ? 2 : 1;   // 16-byte pieces of p per 8 values
+  uint4 xr[kMaxVec], pr[kMaxVec][kPV];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
+#pragma unroll
+      for (int k = 0; k < kPV; ++k) pr[i][k] = reinterpret_cast<const uint4*>(p + off)[kPV * c + k];
+    }
+  }
   float v[kMaxVec][8];
   float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i) {
     const int c = lane + i * 32;
     if (c < nvec) {
-      bf16x8_to_f32(reinterpret_cast<const uint4*>(x + off)[c], v[i]);
-      float q[8];
+      bf16x8_to_f32(xr[i], v[i]);
+      float q[8], bs[8];
       if constexpr (sizeof(TP) == 4) {
-        const float4 a = reinterpret_cast<const float4*>(p + off)[2 * c];
-        const float4 b = reinterpret_cast<const float4*>(p + off)[2 * c + 1];
-        q[0] = a.x; q[1] = a.y; q[2] = a.z; q[3] = a.w;
-        q[4] = b.x; q[5] = b.y; q[6] = b.z; q[7] = b.w;
-      } else {
-        bf16x8_to_f32(reinterpret_cast<const uint4*>(p + off)[c], q);
-      }
+        const uint32_t w[8] = {pr[i][0].x, pr[i][0].y, pr[i][0].z, pr[i][0].w,
+                               pr[i][1].x, pr[i][1].y, pr[i][1].z, pr[i][1].w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] += q[e] + (bias ? bias[c * 8 + e] : 0.f);
+        for (int e = 0; e < 8; ++e) q[e] = __uint_as_float(w[e]);
+      } else {
+        bf16x8_to_f32(pr[i][0], q);
+      }
+      ld_param8<kVecParams>(bias, c, 0.f, bs);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] += q[e] + bs[e];
       const uint4 packed = f32_to_bf16x8(v[i]);
       bf16x8_to_f32(packed, v[i]);
       reinterpret_cast<uint4*>(s_out + off)[c] = packed;
@@ -265,16 +296,28 @@ __global__ void __launch_bounds__(256)
   for (int i = 0; i < kMaxVec; ++i) {
     const int c = lane + i * 32;
     if (c < nvec) {
-      float o[8];
+      float g[8], b[8], o[8];
+      ld_param8<kVecParams>(gamma, c, 1.f, g);
+      ld_param8<kVecParams>(beta, c, 0.f, b);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float g = gamma ? gamma[c * 8 + e] : 1.f;
-        const float b = beta ? beta[c * 8 + e] : 0.f;
-        o[e] = (v[i][e] - mu) * rs * g + b;
-      }
+      for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mu) * rs * g[e] + b[e];
       reinterpret_cast<uint4*>(y + off)[c] = f32_to_bf16x8(o);
     }
   }
+}
+
+template <typename TP, bool kVec>
+cudaError_t launch_add_ln_vec(cudaStream_t stream, const __nv_bfloat16* x, const TP* pp,
+                              const float* bias, const float* gamma, const float* beta,
+                              __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d, float eps) {
+  const dim3 grid((rows + 7) / 8), block(256);
+  if (d <= 256)
+    return launch_ex(add_ln_kernel<TP, 1, kVec>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  if (d <= 512)
+    return launch_ex(add_ln_kernel<TP, 2, kVec>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  if (d <= 1024)
+    return launch_ex(add_ln_kernel<TP, 4, kVec>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  return launch_ex(add_ln_kernel<TP, 8, kVec>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
 }
 
 template <typename TP>
@@ -282,15 +325,11 @@ cudaError_t launch_add_ln_typed(cudaStream_t stream, const __nv_bfloat16* x, con
                                 const float* bias, const float* gamma, const float* beta,
                                 __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d,
                                 float eps) {
-  const dim3 grid((rows + 7) / 8), block(256);
   const TP* pp = static_cast<const TP*>(p);
-  if (d <= 256)
-    return launch_ex(add_ln_kernel<TP, 1>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  if (d <= 512)
-    return launch_ex(add_ln_kernel<TP, 2>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  if (d <= 1024)
-    return launch_ex(add_ln_kernel<TP, 4>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
-  return launch_ex(add_ln_kernel<TP, 8>, grid, block, 0, stream, 1, true, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
+  const bool vec = ((reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(gamma) |
+                     reinterpret_cast<uintptr_t>(beta)) & 15u) == 0;
+  return vec ? launch_add_ln_vec<TP, true>(stream, x, pp, bias, gamma, beta, s_out, y, rows, d, eps)
+             : launch_add_ln_vec<TP, false>(stream, x, pp, bias, gamma, beta, s_out, y, rows, d, eps);
 }
 
 }  // namespace

@@ -5,22 +5,27 @@
 //   s = x + Σ_r p_r + bias   (p_r: rank r's partial sum),  y = LayerNorm(s)
 //
 // Every rank owns a "region" of device memory shared with the other ranks
-// through CUDA IPC handles: a header of flags and counters, then two slots of
-// rows_max x d bf16 partial sums.  A caller's GEMM writes its partial into
-// its own region's slot; this kernel then
-//   1. per CTA, publishes a sequence number into every peer's flag array
-//      (release at system scope) and waits, bounded, for every peer's number
-//      for the same CTA (acquire): a peer that has reached this point has
-//      finished the GEMM that wrote its partial;
-//   2. reads the rows of its share from all ranks' slots with plain loads over
-//      NVLink (no multicast), sums them in rank order — every rank computes
-//      the same bits — adds x and the bias, stores s and the LayerNorm of s.
-// Slots alternate between calls: a peer that publishes call n+1 has finished
-// every read of call n (its kernels run in stream order), so a rank's GEMM of
-// call n+2 may overwrite the slot of call n.  Each CTA keeps its own sequence
-// counter in the local header, so captured CUDA graphs replay correctly.
-// A wait that passes the deadline sets the device error word and the CTA
-// skips its rows (garbage out, no hang).
+// through CUDA IPC handles: a header of flags and counters, two slots of
+// rows_max x d bf16 for this rank's own partial sum (a caller's GEMM writes
+// it there), and two receive areas of kCommMaxRanks such blocks, one block
+// per sending rank.  Per call, each CTA of the kernel
+//   1. pushes its rows of this rank's partial into the receive block of this
+//      rank in every peer's region, with plain 16-byte stores over NVLink
+//      (no multicast), then — after one release fence — writes a sequence
+//      number into each peer's flag for this CTA;
+//   2. waits, bounded, for every peer's flag for this CTA in its own
+//      (local) header, with acquire loads;
+//   3. reads the rows from local memory only — its own partial and the
+//      peers' pushed ones — sums them in rank order (every rank computes the
+//      same bits), adds x and the bias, stores s and the LayerNorm of s.
+// So the exchange costs one NVLink write latency and one flag latency, and
+// no rank waits on a remote read.  Slots and receive areas alternate between
+// calls: a peer that publishes call n+1 has finished every read of call n
+// (its kernels run in stream order), so a push of call n+2 may overwrite the
+// area call n used.  Each CTA keeps its own sequence counter in the local
+// header, so captured CUDA graphs replay correctly.  A wait that passes the
+// deadline sets the device error word and the CTA skips its rows (garbage
+// out, no hang).
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -36,19 +41,18 @@ namespace {
 constexpr size_t kFlagsBytes = sizeof(uint32_t) * kCommMaxRanks * kCommMaxCtas;
 constexpr size_t kCountersOff = kFlagsBytes;
 
-// Flags use the fence / relaxed-access form of release and acquire: one
-// system-scope fence before the stores to every peer (a st.release per peer
-// would wait for each earlier remote store to complete before the next), and
-// relaxed polls followed by one fence once every peer's flag is seen.
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-// 16 bytes, cached in L2 only (a slot is rewritten every other call)
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+// 16 bytes, cached in L2 only (the areas are rewritten every other call)
 __device__ __forceinline__ uint4 ld_cg16(const void* p) {
   uint4 r;
   asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -80,15 +84,15 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// kTP is the rank count: a compile-time count lets every rank's slot load of
-// a row issue before the first one is used (a runtime count leaves each load
-// behind its own branch, so the NVLink reads of a row go out one at a time).
-// `own` is this rank's region (regs.r[rank]), passed on its own so that no
-// dynamic index into the region array puts that array in local memory.
+// kTP is the rank count (a compile-time count keeps the per-rank loops
+// unrolled, every load of a row in flight together).  `own` is this rank's
+// region (regs.r[rank]), passed on its own so that no dynamic index into the
+// region array puts that array in local memory.  own_off: this rank's
+// partial; recv_off: receive area of this call (block r at r * block).
 template <int kMaxVec, int kTP>
 __global__ void __launch_bounds__(256)
-    allreduce_add_ln_kernel(CommRegions regs, char* own, int rank, size_t slot_off,
-                            const __nv_bfloat16* x, const float* __restrict__ bias,
+    allreduce_add_ln_kernel(CommRegions regs, char* own, int rank, size_t own_off, size_t recv_off,
+                            size_t block, const __nv_bfloat16* x, const float* __restrict__ bias,
                             const float* __restrict__ gamma, const float* __restrict__ beta,
                             __nv_bfloat16* s_out, __nv_bfloat16* __restrict__ y, int rows, int d,
                             float eps, int* __restrict__ err_word) {
@@ -97,12 +101,10 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const int nvec = d >> 3;
   const int row0 = blockIdx.x * warps + (threadIdx.x >> 5);
-  // This rank's inputs (x, bias, gamma, beta) come from earlier work on this
-  // stream, so the first row's loads go out before the peers' flags are
-  // awaited; only the partial sums in the slots wait for them.  bias, gamma
-  // and beta (the same for every row) are constant operands and go out even
-  // before the previous kernel has finished (programmatic dependent launch).
-  uint4 xr[kMaxVec];
+  const int row_step = gridDim.x * warps;
+  // bias, gamma and beta are constant operands: loaded before the previous
+  // kernel (the GEMM writing this rank's partial) has finished, under
+  // programmatic dependent launch
   float bs[kMaxVec][8], gm[kMaxVec][8], bt[kMaxVec][8];
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i) {
@@ -118,72 +120,84 @@ __global__ void __launch_bounds__(256)
   }
   pdl_wait();  // x and this rank's partial come from earlier kernels
   pdl_trigger();
-  if (row0 < rows) {
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = lane + i * 32;
-      if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + static_cast<size_t>(row0) * d)[c];
-    }
-  }
 
-  if (threadIdx.x == 0) {
-    uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
-    const uint32_t seq = counters[blockIdx.x] + 1;
-    __threadfence_system();  // release: this rank's slot before the flags
+  // 1. push this CTA's rows of the partial to every peer
+  const char* mine_p = own + own_off;
+  if constexpr (kTP > 1) {
+    for (int row = row0; row < rows; row += row_step) {
+      const size_t off = static_cast<size_t>(row) * d * 2;
 #pragma unroll
-    for (int p = 0; p < kTP; ++p) {
-      if (p == rank) continue;
-      uint32_t* flags = reinterpret_cast<uint32_t*>(regs.r[p]);
-      st_relaxed_sys(flags + rank * kCommMaxCtas + blockIdx.x, seq);
-    }
-    int ok = 1;
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(own);
-    const uint64_t t0 = globaltimer();
-    for (int p = 0; p < kTP && ok; ++p) {
-      if (p == rank) continue;
-      const uint32_t* f = mine + p * kCommMaxCtas + blockIdx.x;
-      uint32_t it = 0;
-      while (static_cast<int32_t>(ld_relaxed_sys(f) - seq) < 0) {
-        if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
-          ok = 0;
-          if (err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
-          break;
+      for (int i = 0; i < kMaxVec; ++i) {
+        const int c = lane + i * 32;
+        if (c < nvec) {
+          const uint4 v = ld_cg16(mine_p + off + c * 16);
+#pragma unroll
+          for (int p = 0; p < kTP; ++p) {
+            if (p == rank) continue;
+            *reinterpret_cast<uint4*>(static_cast<char*>(regs.r[p]) + recv_off + rank * block +
+                                      off + c * 16) = v;
+          }
         }
       }
     }
-    __threadfence_system();  // acquire: the peers' slots after their flags
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
+    const uint32_t seq = counters[blockIdx.x] + 1;
+    int ok = 1;
+    if constexpr (kTP > 1) {
+      // release: the CTA's pushes (ordered before this thread by the barrier)
+      // become visible before the flags
+      fence_acq_rel_sys();
+#pragma unroll
+      for (int p = 0; p < kTP; ++p) {
+        if (p == rank) continue;
+        uint32_t* flags = reinterpret_cast<uint32_t*>(regs.r[p]);
+        st_relaxed_sys(flags + rank * kCommMaxCtas + blockIdx.x, seq);
+      }
+      // 2. acquire every peer's pushes for this CTA (local flags)
+      const uint32_t* mine = reinterpret_cast<const uint32_t*>(own);
+      const uint64_t t0 = globaltimer();
+      for (int p = 0; p < kTP && ok; ++p) {
+        if (p == rank) continue;
+        const uint32_t* f = mine + p * kCommMaxCtas + blockIdx.x;
+        uint32_t it = 0;
+        while (static_cast<int32_t>(ld_acquire_sys(f) - seq) < 0) {
+          if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
+            ok = 0;
+            if (err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
+            break;
+          }
+        }
+      }
+    }
     counters[blockIdx.x] = seq;
     s_ok = ok;
   }
   __syncthreads();
   if (!s_ok) return;
 
-  for (int row = row0; row < rows; row += gridDim.x * warps) {
+  // 3. sum in rank order from local memory, residual, bias, LayerNorm
+  for (int row = row0; row < rows; row += row_step) {
     const size_t off = static_cast<size_t>(row) * d;
-    if (row != row0) {
-#pragma unroll
-      for (int i = 0; i < kMaxVec; ++i) {
-        const int c = lane + i * 32;
-        if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
-      }
-    }
     float v[kMaxVec][8];
     float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + i * 32;
       if (c < nvec) {
-        // every rank's 16 bytes in flight together, then the partial sums in
-        // rank order, the residual and the bias
         uint4 pv[kTP];
 #pragma unroll
         for (int p = 0; p < kTP; ++p)
-          pv[p] = ld_cg16(static_cast<const char*>(regs.r[p]) + slot_off + (off + c * 8) * 2);
+          pv[p] = p == rank ? ld_cg16(mine_p + (off + c * 8) * 2)
+                            : ld_cg16(own + recv_off + p * block + (off + c * 8) * 2);
+        const uint4 xr = reinterpret_cast<const uint4*>(x + off)[c];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
 #pragma unroll
         for (int p = 0; p < kTP; ++p) bf16x8_add(pv[p], v[i]);
-        bf16x8_add(xr[i], v[i]);
+        bf16x8_add(xr, v[i]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] += bs[i][e];
         const uint4 packed = f32_to_bf16x8(v[i]);
@@ -223,17 +237,17 @@ __global__ void __launch_bounds__(256)
 
 template <int kMaxVec, int kTP>
 cudaError_t launch_one(dim3 grid, cudaStream_t stream, const CommRegions& regs, int rank,
-                       size_t so, const __nv_bfloat16* x, const float* bias, const float* gamma,
-                       const float* beta, __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d,
-                       float eps, int* err_word) {
+                       const size_t (&so)[3], const __nv_bfloat16* x, const float* bias,
+                       const float* gamma, const float* beta, __nv_bfloat16* s_out,
+                       __nv_bfloat16* y, int rows, int d, float eps, int* err_word) {
   return launch_ex(allreduce_add_ln_kernel<kMaxVec, kTP>, grid, dim3(256), 0, stream, 1, true,
-                   regs, static_cast<char*>(regs.r[rank]), rank, so, x, bias, gamma, beta, s_out,
-                   y, rows, d, eps, err_word);
+                   regs, static_cast<char*>(regs.r[rank]), rank, so[0], so[1], so[2], x, bias,
+                   gamma, beta, s_out, y, rows, d, eps, err_word);
 }
 
 template <int kMaxVec>
 cudaError_t launch_tp(int tp, dim3 grid, cudaStream_t stream, const CommRegions& regs, int rank,
-                      size_t so, const __nv_bfloat16* x, const float* bias, const float* gamma,
+                      const size_t (&so)[3], const __nv_bfloat16* x, const float* bias, const float* gamma,
                       const float* beta, __nv_bfloat16* s_out, __nv_bfloat16* y, int rows, int d,
                       float eps, int* err_word) {
   switch (tp) {
@@ -250,8 +264,10 @@ cudaError_t launch_tp(int tp, dim3 grid, cudaStream_t stream, const CommRegions&
 
 }  // namespace
 
+// [header][own slot 0][own slot 1][receive area 0: kCommMaxRanks blocks][receive area 1]
 size_t comm_region_bytes(int rows_max, int d) {
-  return comm_slot_offset(0, rows_max, d) + 2 * static_cast<size_t>(rows_max) * d * 2;
+  return comm_slot_offset(2, rows_max, d) +
+         2 * static_cast<size_t>(kCommMaxRanks) * rows_max * d * 2;
 }
 
 size_t comm_slot_offset(int slot, int rows_max, int d) {
@@ -274,7 +290,10 @@ cudaError_t launch_allreduce_add_layernorm(cudaStream_t stream, const CommRegion
                                            int d, float eps, int sms, int* err_word) {
   if (tp < 1 || tp > kCommMaxRanks || rank < 0 || rank >= tp) return cudaErrorInvalidValue;
   const dim3 grid(comm_grid(rows, sms));
-  const size_t so = comm_slot_offset(slot, rows_max, d);
+  const size_t block = static_cast<size_t>(rows_max) * d * 2;
+  const size_t so[3] = {comm_slot_offset(slot, rows_max, d),
+                        comm_slot_offset(2, rows_max, d) + static_cast<size_t>(slot) * kCommMaxRanks * block,
+                        block};
   if (d <= 256)
     return launch_tp<1>(tp, grid, stream, regs, rank, so, x, bias, gamma, beta, s_out, y, rows, d, eps, err_word);
   else if (d <= 512)
