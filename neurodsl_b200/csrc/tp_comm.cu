@@ -5,27 +5,30 @@
 //   s = x + Σ_r p_r + bias   (p_r: rank r's partial sum),  y = LayerNorm(s)
 //
 // Every rank owns a "region" of device memory shared with the other ranks
-// through CUDA IPC handles: a header of flags and counters, two slots of
-// rows_max x d bf16 for this rank's own partial sum (a caller's GEMM writes
-// it there), and two receive areas of kCommMaxRanks such blocks, one block
-// per sending rank.  Per call, each CTA of the kernel
-//   1. pushes its rows of this rank's partial into the receive block of this
-//      rank in every peer's region, with plain 16-byte stores over NVLink
-//      (no multicast), then — after one release fence — writes a sequence
-//      number into each peer's flag for this CTA;
-//   2. waits, bounded, for every peer's flag for this CTA in its own
-//      (local) header, with acquire loads;
-//   3. reads the rows from local memory only — its own partial and the
-//      peers' pushed ones — sums them in rank order (every rank computes the
-//      same bits), adds x and the bias, stores s and the LayerNorm of s.
-// So the exchange costs one NVLink write latency and one flag latency, and
-// no rank waits on a remote read.  Slots and receive areas alternate between
-// calls: a peer that publishes call n+1 has finished every read of call n
-// (its kernels run in stream order), so a push of call n+2 may overwrite the
-// area call n used.  Each CTA keeps its own sequence counter in the local
-// header, so captured CUDA graphs replay correctly.  A wait that passes the
-// deadline sets the device error word and the CTA skips its rows (garbage
-// out, no hang).
+// through CUDA IPC handles: a header of per-CTA sequence counters, two slots
+// of rows_max x d bf16 for this rank's own partial sum (a caller's GEMM
+// writes it there), and two receive areas of kCommMaxRanks blocks, one block
+// per sending rank.  The exchange carries its own completion flags: every
+// 8-byte word a rank pushes holds 4 bytes of data (two bf16) and, in its high
+// half, the call's sequence number; an aligned 8-byte store is single-copy
+// atomic, so a receiver that reads a word with the current sequence number
+// has its data.  Per call, each CTA
+//   1. pushes its rows of this rank's partial into this rank's block of every
+//      peer's receive area, with plain 16-byte stores over NVLink (no
+//      multicast, no fence, no separate flag);
+//   2. reads its rows from local memory — its own partial, and every peer's
+//      pushed words, polling (bounded) until their sequence numbers are the
+//      current one — sums them in rank order (every rank computes the same
+//      bits), adds x and the bias, and stores s and the LayerNorm of s.
+// So a call costs one NVLink write latency and no rank waits on a remote
+// read.  Slots and receive areas alternate between calls: a peer that pushes
+// call n+2 has finished call n+1, which waited for this rank's call n+1 push,
+// issued after this rank's call n had read everything, so a push never
+// overwrites words still to be read; and the words of call n carry an older
+// sequence number than those of call n+2.  Each CTA keeps its sequence
+// counter in the local header, so captured CUDA graphs replay correctly.  A
+// wait that passes the deadline sets the device error word and the CTA skips
+// its rows (garbage out, no hang).
 #include <cuda_bf16.h>
 #include <stdint.h>
 
@@ -41,16 +44,12 @@ namespace {
 constexpr size_t kFlagsBytes = sizeof(uint32_t) * kCommMaxRanks * kCommMaxCtas;
 constexpr size_t kCountersOff = kFlagsBytes;
 
-__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// two 8-byte words, each single-copy atomic, at system scope
+__device__ __forceinline__ void st_words_sys(void* p, uint64_t a, uint64_t b) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void fence_acq_rel_sys() {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
+__device__ __forceinline__ void ld_words_sys(const void* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 // 16 bytes, cached in L2 only (the areas are rewritten every other call)
 __device__ __forceinline__ uint4 ld_cg16(const void* p) {
@@ -96,7 +95,6 @@ __global__ void __launch_bounds__(256)
                             const float* __restrict__ gamma, const float* __restrict__ beta,
                             __nv_bfloat16* s_out, __nv_bfloat16* __restrict__ y, int rows, int d,
                             float eps, int* __restrict__ err_word) {
-  __shared__ int s_ok;
   const int warps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nvec = d >> 3;
@@ -120,63 +118,38 @@ __global__ void __launch_bounds__(256)
   }
   pdl_wait();  // x and this rank's partial come from earlier kernels
   pdl_trigger();
+  __shared__ uint32_t s_seq;
+  uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
+  if (threadIdx.x == 0) s_seq = counters[blockIdx.x] + 1;
+  __syncthreads();
+  const uint32_t seq = s_seq;
+  const uint64_t tag = static_cast<uint64_t>(seq) << 32;
 
-  // 1. push this CTA's rows of the partial to every peer
+  // 1. push this CTA's rows of the partial to every peer: 8 bf16 (16 bytes)
+  //    become two 16-byte stores of {seq | 2 bf16} words
   const char* mine_p = own + own_off;
   if constexpr (kTP > 1) {
     for (int row = row0; row < rows; row += row_step) {
-      const size_t off = static_cast<size_t>(row) * d * 2;
 #pragma unroll
       for (int i = 0; i < kMaxVec; ++i) {
         const int c = lane + i * 32;
         if (c < nvec) {
-          const uint4 v = ld_cg16(mine_p + off + c * 16);
+          const uint4 v = ld_cg16(mine_p + (static_cast<size_t>(row) * d + c * 8) * 2);
+          const size_t w = (static_cast<size_t>(row) * d + c * 8) * 4;   // 8 values -> 32 bytes
 #pragma unroll
           for (int p = 0; p < kTP; ++p) {
             if (p == rank) continue;
-            *reinterpret_cast<uint4*>(static_cast<char*>(regs.r[p]) + recv_off + rank * block +
-                                      off + c * 16) = v;
+            char* dst = static_cast<char*>(regs.r[p]) + recv_off + rank * block + w;
+            st_words_sys(dst, tag | v.x, tag | v.y);
+            st_words_sys(dst + 16, tag | v.z, tag | v.w);
           }
         }
       }
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
-    const uint32_t seq = counters[blockIdx.x] + 1;
-    int ok = 1;
-    if constexpr (kTP > 1) {
-      // release: the CTA's pushes (ordered before this thread by the barrier)
-      // become visible before the flags
-      fence_acq_rel_sys();
-#pragma unroll
-      for (int p = 0; p < kTP; ++p) {
-        if (p == rank) continue;
-        uint32_t* flags = reinterpret_cast<uint32_t*>(regs.r[p]);
-        st_relaxed_sys(flags + rank * kCommMaxCtas + blockIdx.x, seq);
-      }
-      // 2. acquire every peer's pushes for this CTA (local flags)
-      const uint32_t* mine = reinterpret_cast<const uint32_t*>(own);
-      const uint64_t t0 = globaltimer();
-      for (int p = 0; p < kTP && ok; ++p) {
-        if (p == rank) continue;
-        const uint32_t* f = mine + p * kCommMaxCtas + blockIdx.x;
-        uint32_t it = 0;
-        while (static_cast<int32_t>(ld_acquire_sys(f) - seq) < 0) {
-          if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
-            ok = 0;
-            if (err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
-            break;
-          }
-        }
-      }
-    }
-    counters[blockIdx.x] = seq;
-    s_ok = ok;
-  }
-  __syncthreads();
-  if (!s_ok) return;
+  if (threadIdx.x == 0) counters[blockIdx.x] = seq;
+  int ok = 1;
+  const uint64_t t0 = kTP > 1 ? globaltimer() : 0;
 
   // 3. sum in rank order from local memory, residual, bias, LayerNorm
   for (int row = row0; row < rows; row += row_step) {
@@ -189,9 +162,29 @@ __global__ void __launch_bounds__(256)
       if (c < nvec) {
         uint4 pv[kTP];
 #pragma unroll
-        for (int p = 0; p < kTP; ++p)
-          pv[p] = p == rank ? ld_cg16(mine_p + (off + c * 8) * 2)
-                            : ld_cg16(own + recv_off + p * block + (off + c * 8) * 2);
+        for (int p = 0; p < kTP; ++p) {
+          if (p == rank) {
+            pv[p] = ld_cg16(mine_p + (off + c * 8) * 2);
+            continue;
+          }
+          // 2. the peer's words of this call: poll until all four carry seq
+          const char* src = own + recv_off + p * block + (off + c * 8) * 4;
+          uint64_t w0, w1, w2, w3;
+          uint32_t it = 0;
+          for (;;) {
+            ld_words_sys(src, w0, w1);
+            ld_words_sys(src + 16, w2, w3);
+            if (static_cast<uint32_t>(w0 >> 32) == seq && static_cast<uint32_t>(w1 >> 32) == seq &&
+                static_cast<uint32_t>(w2 >> 32) == seq && static_cast<uint32_t>(w3 >> 32) == seq)
+              break;
+            if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
+              ok = 0;
+              break;
+            }
+          }
+          pv[p] = make_uint4(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1),
+                             static_cast<uint32_t>(w2), static_cast<uint32_t>(w3));
+        }
         const uint4 xr = reinterpret_cast<const uint4*>(x + off)[c];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
@@ -232,7 +225,9 @@ __global__ void __launch_bounds__(256)
         reinterpret_cast<uint4*>(y + off)[c] = f32_to_bf16x8(o);
       }
     }
+    if (!ok) break;
   }
+  if (!ok && err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
 }
 
 template <int kMaxVec, int kTP>
@@ -264,10 +259,11 @@ cudaError_t launch_tp(int tp, dim3 grid, cudaStream_t stream, const CommRegions&
 
 }  // namespace
 
-// [header][own slot 0][own slot 1][receive area 0: kCommMaxRanks blocks][receive area 1]
+// [header][own slot 0][own slot 1][receive area 0: kCommMaxRanks blocks][receive area 1];
+// a block holds rows_max x d values as {sequence | 2 bf16} 8-byte words
 size_t comm_region_bytes(int rows_max, int d) {
   return comm_slot_offset(2, rows_max, d) +
-         2 * static_cast<size_t>(kCommMaxRanks) * rows_max * d * 2;
+         2 * static_cast<size_t>(kCommMaxRanks) * rows_max * d * 4;
 }
 
 size_t comm_slot_offset(int slot, int rows_max, int d) {
@@ -290,7 +286,7 @@ cudaError_t launch_allreduce_add_layernorm(cudaStream_t stream, const CommRegion
                                            int d, float eps, int sms, int* err_word) {
   if (tp < 1 || tp > kCommMaxRanks || rank < 0 || rank >= tp) return cudaErrorInvalidValue;
   const dim3 grid(comm_grid(rows, sms));
-  const size_t block = static_cast<size_t>(rows_max) * d * 2;
+  const size_t block = static_cast<size_t>(rows_max) * d * 4;
   const size_t so[3] = {comm_slot_offset(slot, rows_max, d),
                         comm_slot_offset(2, rows_max, d) + static_cast<size_t>(slot) * kCommMaxRanks * block,
                         block};
