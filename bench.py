@@ -699,8 +699,10 @@ def run_comm_bench(args):
     one rank per GPU): rows x d bf16 partial sums combined with the residual
     add, bias and LayerNorm by the NVLink kernel (nd_allreduce_add_layernorm),
     against an NCCL all-reduce of the same bytes followed by the library's
-    add + LayerNorm; CUDA-event times over back-to-back calls, max over
-    ranks.  Prints one JSON line on rank 0."""
+    add + LayerNorm; then the same with the row-parallel projection that
+    produces the partials (nd_gemm_allreduce_add_layernorm, one launch).
+    CUDA-event times over back-to-back calls, max over ranks.  Prints one
+    JSON line on rank 0."""
     import datetime
 
     import torch
@@ -750,6 +752,30 @@ def run_comm_bench(args):
     with ops.pdl(True):
         res["nvlink_fused_pdl_us"] = timed(nvlink)
     res["nccl_allreduce_then_add_layernorm_us"] = timed(nccl)
+    # the MLP-down projection of the 24-layer d=1024 decoder (d_ff 4096 split
+    # over the ranks) with its reduction: one fused launch, against the
+    # projection into this rank's slot followed by the reduction kernel
+    K = 4096 // world
+    a = (torch.randn(rows, K, device=dev) * 0.05).bfloat16()
+    w = (torch.randn(d, K, device=dev) * 0.02).bfloat16()
+
+    def fused_projection():
+        pr.linear_add_layernorm(a, w, x, bias, g, bt, 1e-5, x, h)
+
+    def projection_then_reduce():
+        ops.linear(a, w, out=pr.partial(rows))
+        pr.add_layernorm(x, bias, g, bt, 1e-5, x, h)
+
+    def projection_then_nccl():
+        ops.linear(a, w, out=buf)
+        dist.all_reduce(buf)
+        ops.add_layernorm(x, buf, bias, g, bt, 1e-5, s_out=x, out=h)
+
+    res["projection_k"] = K
+    with ops.pdl(True):
+        res["projection_fused_pdl_us"] = timed(fused_projection)
+        res["projection_then_nvlink_reduce_pdl_us"] = timed(projection_then_reduce)
+    res["projection_then_nccl_us"] = timed(projection_then_nccl)
     res["device_error"] = ops.device_error()
     pr.close()
     if rank == 0:

@@ -57,6 +57,8 @@
  *   nd_add_layernorm    residual :add src/dispatch.jl:386-417 + :layernorm
  *   nd_comm_*, nd_allreduce_add_layernorm  no reference counterpart (multi-GPU
  *                       tensor-parallel reduction fused with :add + :layernorm)
+ *   nd_gemm_allreduce_add_layernorm  the same, with the row-parallel :linear
+ *                       before it in one launch
  */
 #ifndef NEURODSL_B200_H
 #define NEURODSL_B200_H
@@ -395,6 +397,27 @@ int nd_allreduce_add_layernorm(void *stream, void *const *regions, int tp, int r
                                size_t region_bytes, int rows_max, int slot, const void *x,
                                const float *bias, const float *gamma, const float *beta,
                                void *s_out, void *y, int rows, int d, float eps);
+
+/*
+ * The row-parallel projection of a decode step and the reduction after it in
+ * one launch (no reference counterpart: the tensor-parallel out-projection /
+ * MLP-down :linear, src/dispatch.jl:363-384, plus :add and :layernorm):
+ *   s_out = x + Σ_r bf16(A_r [rows][K] · W_r [d][K]ᵀ) + bias,  y = LayerNorm(s_out)
+ * where rank r passes its own A (bf16, its heads' attention output or its MLP
+ * columns) and W (bf16, the matching columns of the projection).  The same
+ * regions, rows_max and slot alternation as nd_allreduce_add_layernorm (the
+ * two may be mixed, each call taking the next slot); the GEMM's tiles go
+ * straight into every rank's receive area, so the own-partial slots are not
+ * used.  Supported: tp 1, 2, 4 or 8, rows <= 32, d a multiple of 8 up to 1024,
+ * K a multiple of 32 (ND_ERR_UNSUPPORTED otherwise).  The results are
+ * bit-identical to nd_gemm_bias_act (no bias) into the own slot followed by
+ * nd_allreduce_add_layernorm.
+ */
+int nd_gemm_allreduce_add_layernorm(void *stream, const void *A, const void *W, int K,
+                                    void *const *regions, int tp, int rank, size_t region_bytes,
+                                    int rows_max, int slot, const void *x, const float *bias,
+                                    const float *gamma, const float *beta, void *s_out, void *y,
+                                    int rows, int d, float eps);
 
 #ifdef __cplusplus
 }

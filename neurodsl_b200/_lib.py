@@ -81,6 +81,8 @@ SIGNATURES = {
     "nd_comm_free": (_i, [_vp]),
     "nd_allreduce_add_layernorm": (_i, [_vp, ctypes.POINTER(_vp), _i, _i, _sz, _i, _i, _vp, _vp,
                                         _vp, _vp, _vp, _vp, _i, _i, _f]),
+    "nd_gemm_allreduce_add_layernorm": (_i, [_vp, _vp, _vp, _i, ctypes.POINTER(_vp), _i, _i, _sz,
+                                             _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _f]),
 }
 
 

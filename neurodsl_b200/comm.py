@@ -6,8 +6,10 @@ exchanged through the torch.distributed group, and each rank maps the other
 ranks' regions.  A caller writes its partial sum into `partial(rows)` (a view
 of its own region's current slot, e.g. as a GEMM's output) and then calls
 `add_layernorm`, which sums all ranks' partials over NVLink, adds the
-residual and bias and applies the LayerNorm; slots alternate automatically.
-All ranks must make the same calls in the same order.
+residual and bias and applies the LayerNorm; or it calls
+`linear_add_layernorm`, which also computes the partial (the row-parallel
+projection) in the same launch.  Slots alternate automatically.  All ranks
+must make the same calls in the same order.
 """
 import torch
 import torch.distributed as dist
@@ -50,6 +52,21 @@ class PeerReduce:
     def add_layernorm(self, x, bias, gamma, beta, eps, s_out, out):
         ops.allreduce_add_layernorm(self.regions, self.rank, self.nbytes, self.rows_max, self.k,
                                     x, bias, gamma, beta, s_out, out, eps)
+        self.k ^= 1
+        return s_out, out
+
+    def fused_supported(self, rows, K):
+        """Whether linear_add_layernorm takes rows x K projection inputs
+        (tp 1, 2, 4 or 8; rows <= 32; d a multiple of 8 up to 1024; K a
+        multiple of 32)."""
+        return (self.tp in (1, 2, 4, 8) and 1 <= rows <= min(32, self.rows_max)
+                and self.d % 8 == 0 and 8 <= self.d <= 1024 and K >= 32 and K % 32 == 0)
+
+    def linear_add_layernorm(self, a, w, x, bias, gamma, beta, eps, s_out, out):
+        """s_out = x + Σ_r bf16(a_r · w_rᵀ) + bias, out = LayerNorm(s_out), where
+        a [rows][K] and w [d][K] are this rank's shards (one launch)."""
+        ops.gemm_allreduce_add_layernorm(a, w, self.regions, self.rank, self.nbytes, self.rows_max,
+                                         self.k, x, bias, gamma, beta, s_out, out, eps)
         self.k ^= 1
         return s_out, out
 

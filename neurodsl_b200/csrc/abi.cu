@@ -961,4 +961,45 @@ __attribute__((visibility("default"))) int nd_allreduce_add_layernorm(
   return ok();
 }
 
+__attribute__((visibility("default"))) int nd_gemm_allreduce_add_layernorm(
+    void* stream, const void* A, const void* W, int K, void* const* regions, int tp, int rank,
+    size_t region_bytes, int rows_max, int slot, const void* x, const float* bias,
+    const float* gamma, const float* beta, void* s_out, void* y, int rows, int d, float eps) {
+  const char* fn = "nd_gemm_allreduce_add_layernorm";
+  if (!regions) return fail(ND_ERR_INVALID_ARG, "%s: regions is NULL", fn);
+  if (tp < 1 || tp > nd::kCommMaxRanks || rank < 0 || rank >= tp)
+    return fail(ND_ERR_INVALID_ARG, "%s: tp %d / rank %d (tp <= %d)", fn, tp, rank, nd::kCommMaxRanks);
+  if (slot != 0 && slot != 1) return fail(ND_ERR_INVALID_ARG, "%s: slot %d (0 or 1)", fn, slot);
+  if (rows < 0 || rows > rows_max)
+    return fail(ND_ERR_SHAPE, "%s: rows %d outside [0, rows_max %d]", fn, rows, rows_max);
+  if (rows == 0) return ok();
+  if (!nd::fused_projection_supported(tp, rows, d, K))
+    return fail(ND_ERR_UNSUPPORTED,
+                "%s: tp %d rows %d d %d K %d (tp 1, 2, 4 or 8; rows <= 32; d a multiple of 8 up to 1024; "
+                "K a multiple of 32)", fn, tp, rows, d, K);
+  if (nd::comm_region_bytes(rows_max, d) > region_bytes)
+    return fail(ND_ERR_SHAPE, "%s: %zu-byte regions cannot hold %d x %d slots", fn, region_bytes,
+                rows_max, d);
+  if (!A || !W || !x || !s_out || !y) return fail(ND_ERR_INVALID_ARG, "%s: null tensor pointer", fn);
+  if (!aligned16(A) || !aligned16(W) || !aligned16(x) || !aligned16(s_out) || !aligned16(y))
+    return fail(ND_ERR_ALIGNMENT, "%s: A/W/x/s_out/y must be 16-byte aligned", fn);
+  nd::CommRegions regs = {};
+  for (int r = 0; r < tp; ++r) {
+    if (!regions[r] || !aligned16(regions[r]))
+      return fail(ND_ERR_INVALID_ARG, "%s: region %d is NULL or unaligned", fn, r);
+    regs.r[r] = regions[r];
+  }
+  int dev = 0;
+  int rc = check_current_device(&dev);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_gemm_allreduce_add_layernorm(
+      static_cast<cudaStream_t>(stream), regs, tp, rank, slot, rows_max,
+      static_cast<const __nv_bfloat16*>(A), static_cast<const __nv_bfloat16*>(W), K,
+      static_cast<const __nv_bfloat16*>(x), bias, gamma, beta,
+      static_cast<__nv_bfloat16*>(s_out), static_cast<__nv_bfloat16*>(y), rows, d, eps,
+      nd::device_error_word());
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return ok();
+}
+
 }  // extern "C"

@@ -27,6 +27,7 @@
 #include "gemm.h"
 #include "launch.cuh"
 #include "ptx.cuh"
+#include "skinny_core.cuh"
 #include "tma.h"
 
 namespace nd {
@@ -614,109 +615,17 @@ cudaError_t launch_bn(int BN, int act, cudaStream_t stream, const CUtensorMap& t
 // Under programmatic dependent launch the first batch of W loads is issued
 // before pdl_wait(): W is a constant operand; A and the residual are read
 // after it.
-constexpr int kSkinnyWarps = 8;
-constexpr int kSkinnyBatch = 4;  // k chunks whose loads are issued together
-constexpr int kSkinnyMaxSplit = 8;
-
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
-                                               uint32_t a2, uint32_t a3, uint32_t b0,
-                                               uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
-      "{%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 ldg16_or_zero(const __nv_bfloat16* p, bool ok) {
-  return ok ? __ldg(reinterpret_cast<const uint4*>(p)) : make_uint4(0, 0, 0, 0);
-}
-
 template <int kMB, bool kOutF32, int kAct, bool kRes>
 __global__ void __launch_bounds__(kSkinnyWarps * 32)
     skinny_gemm_kernel(const __nv_bfloat16* __restrict__ A, const __nv_bfloat16* __restrict__ W,
                        const float* __restrict__ bias, const void* __restrict__ residual,
                        int residual_f32, void* __restrict__ Y, int M, int N, int K) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;  // fragment group (row / column) and slot
   const int ksplit = static_cast<int>(cluster_nctarank());
   const int kr = static_cast<int>(cluster_ctarank());
   const int n0 = (blockIdx.x / ksplit) * 8;
-  const bool w_ok = n0 + g < N;
-  const __nv_bfloat16* wrow = W + static_cast<size_t>(w_ok ? n0 + g : 0) * K + t * 8;
-  const int n_chunks = K / 32;
-  const int per = (n_chunks + ksplit - 1) / ksplit;
-  const int cbeg = kr * per;
-  const int cend = min(n_chunks, cbeg + per);
-  constexpr int kStep = kSkinnyWarps * kSkinnyBatch;
-
-  uint4 wv[kSkinnyBatch];
-#pragma unroll
-  for (int u = 0; u < kSkinnyBatch; ++u) {
-    const int ch = cbeg + warp + u * kSkinnyWarps;
-    wv[u] = ldg16_or_zero(wrow + ch * 32, ch < cend && w_ok);
-  }
-  pdl_wait();
-  pdl_trigger();
-
-  const __nv_bfloat16* arow[kMB][2];
-  bool a_ok[kMB][2];
-#pragma unroll
-  for (int mb = 0; mb < kMB; ++mb)
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int m = mb * 16 + h * 8 + g;
-      a_ok[mb][h] = m < M;
-      arow[mb][h] = A + static_cast<size_t>(a_ok[mb][h] ? m : 0) * K + t * 8;
-    }
-  float c[kMB][4];
-#pragma unroll
-  for (int mb = 0; mb < kMB; ++mb)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) c[mb][i] = 0.f;
-  for (int c0 = cbeg + warp; c0 < cend; c0 += kStep) {
-    uint4 av[kSkinnyBatch][kMB][2];
-#pragma unroll
-    for (int u = 0; u < kSkinnyBatch; ++u) {
-      const int ch = c0 + u * kSkinnyWarps;
-      const bool in = ch < cend;
-      if (c0 != cbeg + warp) wv[u] = ldg16_or_zero(wrow + ch * 32, in && w_ok);
-#pragma unroll
-      for (int mb = 0; mb < kMB; ++mb)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) av[u][mb][h] = ldg16_or_zero(arow[mb][h] + ch * 32, in && a_ok[mb][h]);
-    }
-#pragma unroll
-    for (int u = 0; u < kSkinnyBatch; ++u) {
-      const uint32_t w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-#pragma unroll
-      for (int mb = 0; mb < kMB; ++mb) {
-        const uint32_t lo[4] = {av[u][mb][0].x, av[u][mb][0].y, av[u][mb][0].z, av[u][mb][0].w};
-        const uint32_t hi[4] = {av[u][mb][1].x, av[u][mb][1].y, av[u][mb][1].z, av[u][mb][1].w};
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
-          mma_bf16_16816(c[mb], lo[2 * s], hi[2 * s], lo[2 * s + 1], hi[2 * s + 1], w[2 * s],
-                         w[2 * s + 1]);
-      }
-    }
-  }
-  // sum the warps' partial tiles: red[warp][m][n] for the 16·kMB x 8 tile
   __shared__ float red[kSkinnyWarps][kMB * 16][8];
   __shared__ float part[kMB * 16 * 8];
-#pragma unroll
-  for (int mb = 0; mb < kMB; ++mb) {
-    red[warp][mb * 16 + g][2 * t] = c[mb][0];
-    red[warp][mb * 16 + g][2 * t + 1] = c[mb][1];
-    red[warp][mb * 16 + g + 8][2 * t] = c[mb][2];
-    red[warp][mb * 16 + g + 8][2 * t + 1] = c[mb][3];
-  }
-  __syncthreads();
-  for (int o = threadIdx.x; o < kMB * 16 * 8; o += blockDim.x) {
-    float z = 0.f;
-#pragma unroll
-    for (int w = 0; w < kSkinnyWarps; ++w) z += red[w][o >> 3][o & 7];
-    part[o] = z;
-  }
+  skinny_tile<kMB>(A, W, M, N, K, n0, ksplit, kr, red, part, true);
   // every CTA of the cluster reaches both barriers (no early exit above)
   if (ksplit > 1) cluster_sync();
   else __syncthreads();
@@ -738,19 +647,6 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32)
   }
   // rank 0 has read every peer's tile before any CTA of the cluster exits
   if (ksplit > 1) cluster_sync();
-}
-
-// K split across a cluster: enough CTAs that each warp's share of K is one
-// batch of loads, at most kSkinnyMaxSplit, and only while the grid has fewer
-// CTAs than two per SM (a larger grid already keeps every SM's loads busy).
-int skinny_ksplit(int N, int K) {
-  const int n_chunks = K / 32;
-  const int nblk = (N + 7) / 8;
-  int ks = (n_chunks + kSkinnyWarps * kSkinnyBatch - 1) / (kSkinnyWarps * kSkinnyBatch);
-  if (ks > kSkinnyMaxSplit) ks = kSkinnyMaxSplit;
-  if (ks < 1) ks = 1;
-  if (nblk >= 2 * 148) ks = 1;
-  return ks;
 }
 
 template <int kMB, bool kOutF32, int kAct>

@@ -34,15 +34,21 @@
 
 #include "launch.cuh"
 #include "ptx.cuh"
+#include "skinny_core.cuh"
 #include "tp_comm.h"
 
 namespace nd {
 namespace {
 
-// header: flags[kCommMaxRanks][kCommMaxCtas] (written by peers), then
-// counters[kCommMaxCtas] (this rank's own sequence numbers)
-constexpr size_t kFlagsBytes = sizeof(uint32_t) * kCommMaxRanks * kCommMaxCtas;
-constexpr size_t kCountersOff = kFlagsBytes;
+// header: counters[kCommMaxCtas] (this rank's per-CTA sequence numbers of the
+// reduction kernel), then one call counter of the fused projection kernel.
+// The two kernels number their calls in disjoint ranges (bit 31 clear / set),
+// so a word left by one never passes for a word of the other.
+constexpr size_t kCountersOff = 0;
+constexpr size_t kFusedCounterOff = sizeof(uint32_t) * kCommMaxCtas;
+constexpr size_t kHeaderBytes = 256 * ((sizeof(uint32_t) * (kCommMaxCtas + 1) + 255) / 256);
+constexpr uint32_t kSeqMask = 0x7fffffffu;
+constexpr uint32_t kFusedSeqBit = 0x80000000u;
 
 // two 8-byte words, each single-copy atomic, at system scope
 __device__ __forceinline__ void st_words_sys(void* p, uint64_t a, uint64_t b) {
@@ -83,6 +89,81 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// 8 bf16 of one sender at value offset v of a receive block: four words,
+// polled until all carry `seq` (bounded by the deadline t0 + timeout; on
+// expiry *ok is cleared and whatever was read is returned).
+__device__ __forceinline__ uint4 poll_words(const char* block_base, size_t v, uint32_t seq,
+                                            uint64_t t0, int* ok) {
+  const char* src = block_base + v * 4;
+  uint64_t w0, w1, w2, w3;
+  uint32_t it = 0;
+  for (;;) {
+    ld_words_sys(src, w0, w1);
+    ld_words_sys(src + 16, w2, w3);
+    if (static_cast<uint32_t>(w0 >> 32) == seq && static_cast<uint32_t>(w1 >> 32) == seq &&
+        static_cast<uint32_t>(w2 >> 32) == seq && static_cast<uint32_t>(w3 >> 32) == seq)
+      break;
+    if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
+      *ok = 0;
+      break;
+    }
+  }
+  return make_uint4(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1),
+                    static_cast<uint32_t>(w2), static_cast<uint32_t>(w3));
+}
+
+// s = x + Σ_p pv[p] + bias in rank order, rounded to bf16 and stored to
+// s_out; then LayerNorm(s) stored to y — for the vectors of one row a lane
+// holds (the same arithmetic and order in the reduction kernel and the fused
+// projection kernel, so both give the same bits).
+template <int kMaxVec>
+__device__ __forceinline__ void add_ln_row(float (&v)[kMaxVec][8], int lane, int nvec, int d,
+                                           size_t off, const float* __restrict__ gamma,
+                                           const float* __restrict__ beta, __nv_bfloat16* s_out,
+                                           __nv_bfloat16* __restrict__ y, float eps) {
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      const uint4 packed = f32_to_bf16x8(v[i]);
+      reinterpret_cast<uint4*>(s_out + off)[c] = packed;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+      bf16x8_add(packed, v[i]);  // normalise the stored (bf16) residual
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += v[i][e];
+    }
+  }
+  const float mu = warp_sum(sum) / static_cast<float>(d);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    if (lane + i * 32 < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float t = v[i][e] - mu;
+        q += t * t;
+      }
+    }
+  }
+  const float rs = rsqrtf(warp_sum(q) / static_cast<float>(d) + eps);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float g = gamma ? __ldg(gamma + c * 8 + e) : 1.f;
+        const float b = beta ? __ldg(beta + c * 8 + e) : 0.f;
+        o[e] = (v[i][e] - mu) * rs * g + b;
+      }
+      reinterpret_cast<uint4*>(y + off)[c] = f32_to_bf16x8(o);
+    }
+  }
+}
+
 // kTP is the rank count (a compile-time count keeps the per-rank loops
 // unrolled, every load of a row in flight together).  `own` is this rank's
 // region (regs.r[rank]), passed on its own so that no dynamic index into the
@@ -100,27 +181,23 @@ __global__ void __launch_bounds__(256)
   const int nvec = d >> 3;
   const int row0 = blockIdx.x * warps + (threadIdx.x >> 5);
   const int row_step = gridDim.x * warps;
-  // bias, gamma and beta are constant operands: loaded before the previous
-  // kernel (the GEMM writing this rank's partial) has finished, under
-  // programmatic dependent launch
-  float bs[kMaxVec][8], gm[kMaxVec][8], bt[kMaxVec][8];
+  // the bias is a constant operand: loaded before the previous kernel (the
+  // GEMM writing this rank's partial) has finished, under programmatic
+  // dependent launch
+  float bs[kMaxVec][8];
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i) {
     const int c = lane + i * 32;
     if (c < nvec) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        bs[i][e] = bias ? __ldg(bias + c * 8 + e) : 0.f;
-        gm[i][e] = gamma ? __ldg(gamma + c * 8 + e) : 1.f;
-        bt[i][e] = beta ? __ldg(beta + c * 8 + e) : 0.f;
-      }
+      for (int e = 0; e < 8; ++e) bs[i][e] = bias ? __ldg(bias + c * 8 + e) : 0.f;
     }
   }
   pdl_wait();  // x and this rank's partial come from earlier kernels
   pdl_trigger();
   __shared__ uint32_t s_seq;
   uint32_t* counters = reinterpret_cast<uint32_t*>(own + kCountersOff);
-  if (threadIdx.x == 0) s_seq = counters[blockIdx.x] + 1;
+  if (threadIdx.x == 0) s_seq = (counters[blockIdx.x] + 1) & kSeqMask;
   __syncthreads();
   const uint32_t seq = s_seq;
   const uint64_t tag = static_cast<uint64_t>(seq) << 32;
@@ -155,36 +232,16 @@ __global__ void __launch_bounds__(256)
   for (int row = row0; row < rows; row += row_step) {
     const size_t off = static_cast<size_t>(row) * d;
     float v[kMaxVec][8];
-    float sum = 0.f;
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + i * 32;
       if (c < nvec) {
         uint4 pv[kTP];
 #pragma unroll
-        for (int p = 0; p < kTP; ++p) {
-          if (p == rank) {
-            pv[p] = ld_cg16(mine_p + (off + c * 8) * 2);
-            continue;
-          }
-          // 2. the peer's words of this call: poll until all four carry seq
-          const char* src = own + recv_off + p * block + (off + c * 8) * 4;
-          uint64_t w0, w1, w2, w3;
-          uint32_t it = 0;
-          for (;;) {
-            ld_words_sys(src, w0, w1);
-            ld_words_sys(src + 16, w2, w3);
-            if (static_cast<uint32_t>(w0 >> 32) == seq && static_cast<uint32_t>(w1 >> 32) == seq &&
-                static_cast<uint32_t>(w2 >> 32) == seq && static_cast<uint32_t>(w3 >> 32) == seq)
-              break;
-            if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
-              ok = 0;
-              break;
-            }
-          }
-          pv[p] = make_uint4(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1),
-                             static_cast<uint32_t>(w2), static_cast<uint32_t>(w3));
-        }
+        for (int p = 0; p < kTP; ++p)
+          pv[p] = p == rank ? ld_cg16(mine_p + (off + c * 8) * 2)
+                            // 2. the peer's words of this call
+                            : poll_words(own + recv_off + p * block, off + c * 8, seq, t0, &ok);
         const uint4 xr = reinterpret_cast<const uint4*>(x + off)[c];
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
@@ -193,41 +250,112 @@ __global__ void __launch_bounds__(256)
         bf16x8_add(xr, v[i]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] += bs[i][e];
-        const uint4 packed = f32_to_bf16x8(v[i]);
-        reinterpret_cast<uint4*>(s_out + off)[c] = packed;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
-        bf16x8_add(packed, v[i]);  // normalise the stored (bf16) residual
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sum += v[i][e];
       }
     }
-    const float mu = warp_sum(sum) / static_cast<float>(d);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      if (lane + i * 32 < nvec) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float t = v[i][e] - mu;
-          q += t * t;
-        }
-      }
-    }
-    const float rs = rsqrtf(warp_sum(q) / static_cast<float>(d) + eps);
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = lane + i * 32;
-      if (c < nvec) {
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = (v[i][e] - mu) * rs * gm[i][e] + bt[i][e];
-        reinterpret_cast<uint4*>(y + off)[c] = f32_to_bf16x8(o);
-      }
-    }
+    add_ln_row<kMaxVec>(v, lane, nvec, d, off, gamma, beta, s_out, y, eps);
     if (!ok) break;
   }
   if (!ok && err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
+}
+
+// The row-parallel projection of a decode step fused with its reduction:
+//   s = x + Σ_r (A_r · W_rᵀ) + bias (bf16 partials, summed in rank order),
+//   y = LayerNorm(s)
+// where rank r holds A_r [M][K] (its heads' attention output or its MLP
+// columns) and W_r [d][K] (the matching columns of the projection).  Each CTA
+// computes an 8-column tile of this rank's partial for all M rows (the skinny
+// path's weight-streaming tile, split-K over a cluster), rounds it to bf16 —
+// as the separate GEMM stores it — and pushes it as {sequence | 2 bf16} words
+// into this rank's block of the receive area of every rank, itself included.
+// The first ceil(M/8) CTAs then each take 8 rows (a warp per row): they poll
+// all ranks' words of their rows (local memory) and finish like the reduction
+// kernel.  So the projection, the exchange and the LayerNorm are one launch,
+// and the exchange is spread over every CTA of the projection.  Only the
+// reducing CTAs wait, and every other CTA pushes and exits, so the grid needs
+// no co-residency: CTAs not yet resident run on the SMs the finished ones
+// free.  Each CTA releases the dependent kernel only after its push, so the
+// dependent grid (which holds SMs while it waits) starts once every CTA of
+// this grid has pushed.
+template <int kMB, int kMaxVec, int kTP>
+__global__ void __launch_bounds__(kSkinnyWarps * 32, 2)
+    gemm_allreduce_ln_kernel(const __nv_bfloat16* __restrict__ A,
+                             const __nv_bfloat16* __restrict__ W, int M, int d, int K,
+                             CommRegions regs, char* own, int rank, size_t recv_off, size_t block,
+                             const __nv_bfloat16* x, const float* __restrict__ bias,
+                             const float* __restrict__ gamma, const float* __restrict__ beta,
+                             __nv_bfloat16* s_out, __nv_bfloat16* __restrict__ y, float eps,
+                             int* __restrict__ err_word) {
+  const int ksplit = static_cast<int>(cluster_nctarank());
+  const int kr = static_cast<int>(cluster_ctarank());
+  const int n0 = (blockIdx.x / ksplit) * 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ float red[kSkinnyWarps][kMB * 16][8];
+  __shared__ float part[kMB * 16 * 8];
+  __shared__ uint32_t s_seq;
+  skinny_tile<kMB>(A, W, M, d, K, n0, ksplit, kr, red, part, false);
+  uint32_t* fused_counter = reinterpret_cast<uint32_t*>(own + kFusedCounterOff);
+  if (threadIdx.x == 0) s_seq = ((*fused_counter + 1) & kSeqMask) | kFusedSeqBit;
+  // every CTA of the cluster has its part[] before rank 0 reads them
+  if (ksplit > 1) cluster_sync();
+  else __syncthreads();
+  const uint32_t seq = s_seq;
+  const uint64_t tag = static_cast<uint64_t>(seq) << 32;
+  if (kr == 0) {
+    // this rank's tile, 4 columns per thread: two words to every rank
+    for (int o = threadIdx.x; o < kMB * 16 * 2; o += blockDim.x) {
+      const int m = o >> 1, q = (o & 1) * 4;
+      if (m >= M || n0 + q >= d) continue;
+      float z[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        z[j] = part[m * 8 + q + j];
+        for (int r = 1; r < ksplit; ++r) z[j] += ld_dsmem_f32(&part[m * 8 + q + j], static_cast<uint32_t>(r));
+      }
+      const uint64_t w0 = tag | pack_bf16x2(z[0], z[1]);
+      const uint64_t w1 = tag | pack_bf16x2(z[2], z[3]);
+      const size_t v = static_cast<size_t>(m) * d + n0 + q;
+#pragma unroll
+      for (int p = 0; p < kTP; ++p) {
+        char* base = p == rank ? own : static_cast<char*>(regs.r[p]);
+        st_words_sys(base + recv_off + rank * block + v * 4, w0, w1);
+      }
+    }
+  }
+  // rank 0 has read every peer's part[] before any CTA of the cluster exits
+  if (ksplit > 1) cluster_sync();
+  pdl_trigger();   // every CTA of this grid is resident once all have pushed
+  if (static_cast<int>(blockIdx.x) * kSkinnyWarps >= M) return;
+
+  const int row = blockIdx.x * kSkinnyWarps + warp;
+  if (row >= M) return;
+  const int nvec = d >> 3;
+  int ok = 1;
+  const uint64_t t0 = globaltimer();
+  const size_t off = static_cast<size_t>(row) * d;
+  float v[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) {
+      uint4 pv[kTP];
+#pragma unroll
+      for (int p = 0; p < kTP; ++p)
+        pv[p] = poll_words(own + recv_off + p * block, off + c * 8, seq, t0, &ok);
+      const uint4 xr = reinterpret_cast<const uint4*>(x + off)[c];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+#pragma unroll
+      for (int p = 0; p < kTP; ++p) bf16x8_add(pv[p], v[i]);
+      bf16x8_add(xr, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] += bias ? __ldg(bias + c * 8 + e) : 0.f;
+    }
+  }
+  add_ln_row<kMaxVec>(v, lane, nvec, d, off, gamma, beta, s_out, y, eps);
+  // the call counter moves on once every rank's words of row 0 (pushed by
+  // every CTA of every rank, after reading the counter) have arrived
+  if (row == 0 && lane == 0) *fused_counter = seq & kSeqMask;
+  if (!ok && lane == 0 && err_word) atomicCAS(err_word, 0, kDevErrTimeoutComm);
 }
 
 template <int kMaxVec, int kTP>
@@ -257,7 +385,74 @@ cudaError_t launch_tp(int tp, dim3 grid, cudaStream_t stream, const CommRegions&
   }
 }
 
+template <int kMB, int kMaxVec, int kTP>
+cudaError_t launch_fused_one(cudaStream_t stream, const __nv_bfloat16* A,
+                             const __nv_bfloat16* W, int M, int d, int K, const CommRegions& regs,
+                             int rank, size_t recv_off, size_t block, const __nv_bfloat16* x,
+                             const float* bias, const float* gamma, const float* beta,
+                             __nv_bfloat16* s_out, __nv_bfloat16* y, float eps, int* err_word) {
+  auto kern = gemm_allreduce_ln_kernel<kMB, kMaxVec, kTP>;
+  const int ks = skinny_ksplit(d, K);
+  const int grid = (d / 8) * ks;
+  return launch_ex(kern, dim3(grid), dim3(kSkinnyWarps * 32), 0, stream, ks, true, A, W, M, d, K,
+                   regs, static_cast<char*>(regs.r[rank]), rank, recv_off, block, x, bias, gamma,
+                   beta, s_out, y, eps, err_word);
+}
+
+template <int kMB, int kMaxVec>
+cudaError_t launch_fused_tp(int tp, cudaStream_t stream, const __nv_bfloat16* A,
+                            const __nv_bfloat16* W, int M, int d, int K, const CommRegions& regs,
+                            int rank, size_t recv_off, size_t block, const __nv_bfloat16* x,
+                            const float* bias, const float* gamma, const float* beta,
+                            __nv_bfloat16* s_out, __nv_bfloat16* y, float eps, int* err_word) {
+#define ND_FUSED(n)                                                                            \
+  launch_fused_one<kMB, kMaxVec, n>(stream, A, W, M, d, K, regs, rank, recv_off, block, x, \
+                                    bias, gamma, beta, s_out, y, eps, err_word)
+  switch (tp) {
+    case 1: return ND_FUSED(1);
+    case 2: return ND_FUSED(2);
+    case 4: return ND_FUSED(4);
+    case 8: return ND_FUSED(8);
+    default: return cudaErrorInvalidValue;
+  }
+#undef ND_FUSED
+}
+
+template <int kMB>
+cudaError_t launch_fused_d(int tp, cudaStream_t stream, const __nv_bfloat16* A,
+                           const __nv_bfloat16* W, int M, int d, int K, const CommRegions& regs,
+                           int rank, size_t recv_off, size_t block, const __nv_bfloat16* x,
+                           const float* bias, const float* gamma, const float* beta,
+                           __nv_bfloat16* s_out, __nv_bfloat16* y, float eps, int* err_word) {
+  if (d <= 256)
+    return launch_fused_tp<kMB, 1>(tp, stream, A, W, M, d, K, regs, rank, recv_off, block, x, bias, gamma, beta, s_out, y, eps, err_word);
+  if (d <= 512)
+    return launch_fused_tp<kMB, 2>(tp, stream, A, W, M, d, K, regs, rank, recv_off, block, x, bias, gamma, beta, s_out, y, eps, err_word);
+  return launch_fused_tp<kMB, 4>(tp, stream, A, W, M, d, K, regs, rank, recv_off, block, x, bias, gamma, beta, s_out, y, eps, err_word);
+}
+
 }  // namespace
+
+bool fused_projection_supported(int tp, int M, int d, int K) {
+  return (tp == 1 || tp == 2 || tp == 4 || tp == 8) && M >= 1 && M <= 32 && d >= 8 &&
+         d % 8 == 0 && d <= 1024 && K >= 32 && K % 32 == 0;
+}
+
+cudaError_t launch_gemm_allreduce_add_layernorm(cudaStream_t stream, const CommRegions& regs,
+                                                int tp, int rank, int slot, int rows_max,
+                                                const __nv_bfloat16* A, const __nv_bfloat16* W,
+                                                int K, const __nv_bfloat16* x, const float* bias,
+                                                const float* gamma, const float* beta,
+                                                __nv_bfloat16* s_out, __nv_bfloat16* y, int M,
+                                                int d, float eps, int* err_word) {
+  if (!fused_projection_supported(tp, M, d, K) || rank < 0 || rank >= tp || M > rows_max)
+    return cudaErrorInvalidValue;
+  const size_t block = static_cast<size_t>(rows_max) * d * 4;
+  const size_t recv_off = comm_slot_offset(2, rows_max, d) + static_cast<size_t>(slot) * kCommMaxRanks * block;
+  if (M <= 16)
+    return launch_fused_d<1>(tp, stream, A, W, M, d, K, regs, rank, recv_off, block, x, bias, gamma, beta, s_out, y, eps, err_word);
+  return launch_fused_d<2>(tp, stream, A, W, M, d, K, regs, rank, recv_off, block, x, bias, gamma, beta, s_out, y, eps, err_word);
+}
 
 // [header][own slot 0][own slot 1][receive area 0: kCommMaxRanks blocks][receive area 1];
 // a block holds rows_max x d values as {sequence | 2 bf16} 8-byte words
@@ -267,7 +462,7 @@ size_t comm_region_bytes(int rows_max, int d) {
 }
 
 size_t comm_slot_offset(int slot, int rows_max, int d) {
-  const size_t header = (kFlagsBytes + sizeof(uint32_t) * kCommMaxCtas + 255) & ~static_cast<size_t>(255);
+  const size_t header = kHeaderBytes;
   return header + static_cast<size_t>(slot) * rows_max * d * 2;
 }
 

@@ -33,4 +33,21 @@ cudaError_t launch_allreduce_add_layernorm(cudaStream_t stream, const CommRegion
                                            __nv_bfloat16* s_out, __nv_bfloat16* y, int rows,
                                            int d, float eps, int sms, int* err_word);
 
+// Whether the fused projection below supports the shape (tp in {1, 2, 4, 8},
+// M <= 32 rows, d a multiple of 8 up to 1024, K a multiple of 32).
+bool fused_projection_supported(int tp, int M, int d, int K);
+
+// The row-parallel projection fused with the reduction:
+//   s_out = x + Σ_r bf16(A_r [M][K] · W_r [d][K]ᵀ) + bias,  y = LayerNorm(s_out)
+// through the receive areas `slot` of the ranks' regions (the same regions
+// and slot alternation as launch_allreduce_add_layernorm; the own-partial
+// slots are not used).  Every rank makes the same calls in the same order.
+cudaError_t launch_gemm_allreduce_add_layernorm(cudaStream_t stream, const CommRegions& regs,
+                                                int tp, int rank, int slot, int rows_max,
+                                                const __nv_bfloat16* A, const __nv_bfloat16* W,
+                                                int K, const __nv_bfloat16* x, const float* bias,
+                                                const float* gamma, const float* beta,
+                                                __nv_bfloat16* s_out, __nv_bfloat16* y, int M,
+                                                int d, float eps, int* err_word);
+
 }  // namespace nd

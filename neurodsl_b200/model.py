@@ -28,9 +28,11 @@ MLP columns [r·F/tp, (r+1)·F/tp) of the up projection and the matching
 columns of the down projection, and vocabulary rows [r·V/tp, ...) of the LM
 head.  The output and down projections produce partial sums that are
 all-reduced before the fused residual + LayerNorm — with NCCL, or for decode
-batches of up to `nvlink_rows` rows by one kernel that reads the peers'
-partials over NVLink and applies the residual and LayerNorm itself
-(neurodsl_b200.comm, nd_allreduce_add_layernorm); the LM head gives a
+batches of up to `nvlink_rows` rows by one kernel that computes this rank's
+projection tile, pushes it to every rank over NVLink and applies the
+residual and LayerNorm to the sum (neurodsl_b200.comm,
+nd_gemm_allreduce_add_layernorm; nd_allreduce_add_layernorm after a separate
+projection where the fused kernel does not take the shapes); the LM head gives a
 local (max, index) per row that is all-gathered and reduced to the global
 first maximum.  Weights are generated from one seed on every rank and sliced,
 so any `tp` computes the same model.
@@ -80,13 +82,16 @@ class GPT:
     """Weights of one rank plus the buffers of one (batch, length) shape."""
 
     def __init__(self, cfg: GPTConfig, seed=0, device=None, tp=1, rank=0, group=None,
-                 weight_std=0.02, bias_std=0.0, nvlink_rows=0, pdl=True):
+                 weight_std=0.02, bias_std=0.0, nvlink_rows=0, pdl=True, fused_projection=True):
         if cfg.d_head != 64:
             raise ValueError("head_dim must be 64")
         self.cfg = cfg
         # decode steps launch with programmatic dependent launch: their weights
         # and earlier cache entries are written by no kernel of the step
         self.pdl = pdl
+        # NVLink decode reductions compute the row-parallel projection in the
+        # same launch where the shapes allow it
+        self.fused_projection = fused_projection
         self.tp, self.rank, self.group = tp, rank, group
         self.device = torch.device(device or "cuda")
         dev = self.device
@@ -271,11 +276,9 @@ class GPT:
                 nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
                 g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
                 if peer:
-                    ops.linear(b["ad"], L["w_o"], out=self.comm.partial(B))
-                    self.comm.add_layernorm(xd, L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, xd, hd)
+                    self._peer_projection(b["ad"], L["w_o"], L["b_o"], L["ln2_g"], L["ln2_b"])
                     ops.linear(hd, L["w_1"], L["b_1"], act=cfg.act, out=b["ud"])
-                    ops.linear(b["ud"], L["w_2"], out=self.comm.partial(B))
-                    self.comm.add_layernorm(xd, L["b_2"], g_, b_, cfg.eps, xd, hd)
+                    self._peer_projection(b["ud"], L["w_2"], L["b_2"], g_, b_)
                     continue
                 ops.linear(b["ad"], L["w_o"], out=b["pd"])
                 self._all_reduce(b["pd"])
@@ -287,6 +290,19 @@ class GPT:
                 ops.add_layernorm(xd, b["pd"], L["b_2"], g_, b_, cfg.eps, s_out=xd, out=hd)
             self._next_token(hd, out_ids)
         return b["logits"]
+
+    def _peer_projection(self, a, w, bias, gamma, beta):
+        """Row-parallel projection a · wᵀ, summed over the ranks through NVLink
+        peer memory, + residual + bias, LayerNorm: one launch where the shapes
+        allow it (nd_gemm_allreduce_add_layernorm), else the projection into
+        this rank's slot and nd_allreduce_add_layernorm."""
+        b, eps = self.buf, self.cfg.eps
+        xd, hd = b["xd"], b["hd"]
+        if self.fused_projection and self.comm.fused_supported(a.shape[0], a.shape[1]):
+            self.comm.linear_add_layernorm(a, w, xd, bias, gamma, beta, eps, xd, hd)
+            return
+        ops.linear(a, w, out=self.comm.partial(a.shape[0]))
+        self.comm.add_layernorm(xd, bias, gamma, beta, eps, xd, hd)
 
     def _decode_layers_fused(self, B, H, Lc, out_ids):
         """One GPU: five launches per layer — residual + LN1 + QKV projection,

@@ -549,3 +549,21 @@ def allreduce_add_layernorm(regions, rank, region_bytes, rows_max, slot, x, bias
         _ptr(bias), _ptr(gamma), _ptr(beta), _ptr(s_out), _ptr(out), rows, d, float(eps)))
     return s_out, out
 
+
+def gemm_allreduce_add_layernorm(a, w, regions, rank, region_bytes, rows_max, slot, x, bias, gamma,
+                                 beta, s_out, out, eps=1e-5, stream=None):
+    """s_out = x + Σ_r bf16(a_r · w_rᵀ) + bias, out = LayerNorm(s_out): this rank's projection
+    tile and the cross-rank reduction in one launch (a [rows, K], w [d, K], both bf16)."""
+    _need(a, "a", torch.bfloat16, 2)
+    _need(w, "w", torch.bfloat16, 2)
+    _need(x, "x", torch.bfloat16, 2)
+    rows, d = x.shape
+    if a.shape[0] != rows or w.shape[0] != d or a.shape[1] != w.shape[1]:
+        raise ValueError(f"gemm_allreduce_add_layernorm: a {tuple(a.shape)} w {tuple(w.shape)} "
+                         f"x {tuple(x.shape)}")
+    arr = (ctypes.c_void_p * len(regions))(*regions)
+    check(_lib.load().nd_gemm_allreduce_add_layernorm(
+        _stream(stream), _ptr(a), _ptr(w), a.shape[1], arr, len(regions), rank, region_bytes,
+        rows_max, slot, _ptr(x), _ptr(bias), _ptr(gamma), _ptr(beta), _ptr(s_out), _ptr(out),
+        rows, d, float(eps)))
+    return s_out, out

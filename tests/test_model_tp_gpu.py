@@ -5,8 +5,10 @@ is rounded to bf16 before the all-reduce, one extra rounding per sub-layer)
 and the greedy tokens wherever the one-GPU top-2 margin exceeds 5e-2 — and
 its graph-captured decode must give the same tokens as its eager decode.
 The same holds for the tp=2 model whose decode reductions run over NVLink
-peer memory (nd_allreduce_add_layernorm) instead of NCCL.  Skipped with fewer
-than 2 GPUs.
+peer memory instead of NCCL, with the row-parallel projection fused into the
+exchange (nd_gemm_allreduce_add_layernorm); the same model with the
+projection as a separate launch before nd_allreduce_add_layernorm gives
+bit-identical logits.  Skipped with fewer than 2 GPUs.
 Each rank runs the same collectives in the same order; the process group has
 a 60 s timeout so a lost rank ends the others with an error.
 """
@@ -72,28 +74,31 @@ def _rank_main(rank, world, port, out_dir):
             np.save(os.path.join(out_dir, "logits.npy"), np.stack(full))
             np.save(os.path.join(out_dir, "tokens.npy"), tokens.cpu().numpy())
             np.save(os.path.join(out_dir, "graphed.npy"), graphed.cpu().numpy())
-        # decode reductions over NVLink peer memory
-        m2 = GPT(GPTConfig(**CFG), seed=21, device=dev, tp=world, rank=rank,
-                 group=dist.group.WORLD, weight_std=0.05, bias_std=0.02, nvlink_rows=8)
-        logits2, tokens2 = _run(m2, ids)
-        full2 = []
-        for lg in logits2:
-            parts = [torch.empty_like(lg) for _ in range(world)]
-            dist.all_gather(parts, lg)
-            full2.append(torch.cat(parts, dim=1).cpu().numpy())
-        graphed2 = m2.generate(ids, STEPS, graph_chunk=2).clone()
-        again2 = m2.generate(ids, STEPS, graph_chunk=2).clone()
-        torch.cuda.synchronize()
+        # decode reductions over NVLink peer memory: the projection fused with
+        # the exchange (default), and the projection as its own launch
         from neurodsl_b200 import ops
-        err = ops.device_error()
-        m2.close()
-        if rank == 0:
-            np.save(os.path.join(out_dir, "logits_nv.npy"), np.stack(full2))
-            np.save(os.path.join(out_dir, "tokens_nv.npy"), tokens2.cpu().numpy())
-            np.save(os.path.join(out_dir, "graphed_nv.npy"),
-                    np.stack([graphed2.cpu().numpy(), again2.cpu().numpy()]))
-            np.save(os.path.join(out_dir, "err_nv.npy"), np.array([err]))
-        dist.barrier()
+        for tag, fused in (("nv", True), ("nvsep", False)):
+            m2 = GPT(GPTConfig(**CFG), seed=21, device=dev, tp=world, rank=rank,
+                     group=dist.group.WORLD, weight_std=0.05, bias_std=0.02, nvlink_rows=8,
+                     fused_projection=fused)
+            logits2, tokens2 = _run(m2, ids)
+            full2 = []
+            for lg in logits2:
+                parts = [torch.empty_like(lg) for _ in range(world)]
+                dist.all_gather(parts, lg)
+                full2.append(torch.cat(parts, dim=1).cpu().numpy())
+            graphed2 = m2.generate(ids, STEPS, graph_chunk=2).clone()
+            again2 = m2.generate(ids, STEPS, graph_chunk=2).clone()
+            torch.cuda.synchronize()
+            err = ops.device_error()
+            m2.close()
+            if rank == 0:
+                np.save(os.path.join(out_dir, f"logits_{tag}.npy"), np.stack(full2))
+                np.save(os.path.join(out_dir, f"tokens_{tag}.npy"), tokens2.cpu().numpy())
+                np.save(os.path.join(out_dir, f"graphed_{tag}.npy"),
+                        np.stack([graphed2.cpu().numpy(), again2.cpu().numpy()]))
+                np.save(os.path.join(out_dir, f"err_{tag}.npy"), np.array([err]))
+            dist.barrier()
     finally:
         dist.destroy_process_group()
 
@@ -135,3 +140,8 @@ def test_tp2_matches_single_gpu(tmp_path):
         if (tokens_nv[:, :k] == ref_tokens[:, :k]).all():
             assert close(logits_nv[k], ref_logits[k]), k
             np.testing.assert_array_equal(tokens_nv[clear, k], ref_tokens[clear, k])
+    # the fused projection + exchange gives the bits of the separate launches
+    assert int(np.load(tmp_path / "err_nvsep.npy")[0]) == 0
+    np.testing.assert_array_equal(np.load(tmp_path / "logits_nvsep.npy"), logits_nv)
+    np.testing.assert_array_equal(np.load(tmp_path / "tokens_nvsep.npy"), tokens_nv)
+    np.testing.assert_array_equal(np.load(tmp_path / "graphed_nvsep.npy")[0], tokens_nv)
