@@ -667,30 +667,115 @@ def run_ours(args):
     return 0
 
 
+# entry points of neurodsl_b200.ops that a decode step calls
+_STEP_OPS = ("embed", "layernorm", "add_layernorm", "linear", "ln_linear", "kv_decode_attn_qkv",
+             "allreduce_add_layernorm", "gemm_allreduce_add_layernorm", "argmax")
+
+
+def _op_times_of_step(model, t, dev):
+    """Per-operation device times of decode step t: every call of the ops in
+    _STEP_OPS (and the LM head's all-gathers) is bracketed by CUDA events.
+    A sleep kernel holds the stream while the host enqueues the step, so the
+    launches and events run back to back without host gaps; the events are
+    then the only addition to the step.  Returns {op: [calls, us]}, the
+    step's event-to-event time and the sum over ops."""
+    import collections
+
+    import torch
+    import torch.distributed as dist
+
+    from neurodsl_b200 import ops
+    rec = []
+
+    def wrap(name, fn):
+        def timed(*a, **k):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(*a, **k)
+            e1.record()
+            rec.append((name, e0, e1))
+            return r
+        return timed
+
+    saved = {n: getattr(ops, n) for n in _STEP_OPS}
+    saved_ag = dist.all_gather_into_tensor
+    try:
+        for n, fn in saved.items():
+            setattr(ops, n, wrap(n, fn))
+        dist.all_gather_into_tensor = wrap("all_gather (LM head max, index)", saved_ag)
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000)   # ~10 ms at 2 GHz: the host enqueues the step meanwhile
+        s0.record()
+        model.decode_step(t)
+        s1.record()
+    finally:
+        for n, fn in saved.items():
+            setattr(ops, n, fn)
+        dist.all_gather_into_tensor = saved_ag
+    torch.cuda.synchronize(dev)
+    agg = collections.OrderedDict()
+    for name, e0, e1 in rec:
+        a = agg.setdefault(name, [0, 0.0])
+        a[0] += 1
+        a[1] += e0.elapsed_time(e1) * 1e3
+    return agg, s0.elapsed_time(s1) * 1e3
+
+
 def run_decoder_only(args):
     """A short eager run of one decoder (prefill, then `--decoder-steps`
     greedy decode steps, one launch per kernel, no CUDA graphs) for ncu
-    captures of the decode-step kernels; prints one line of step times."""
+    captures of the decode-step kernels; prints one line of step times.
+    Under torchrun the decoder is tensor-parallel over all ranks (decode
+    reductions over NVLink).  With --op-times the last step is timed per
+    operation (CUDA events, programmatic dependent launch off) and the table
+    of rank 0 and the per-op maximum over ranks is printed too."""
+    import datetime
+
     import torch
+    import torch.distributed as dist
 
     from neurodsl_b200.model import GPT, GPT2_SMALL, GPT_24L_1024
     cfg, B, S = {"gpt2_small": (GPT2_SMALL, 16, 512),
                  "gpt_24l_1024": (GPT_24L_1024, 32, 2048)}[args.decoder_only]
-    torch.cuda.set_device(0)
-    model = GPT(cfg, seed=0)
-    gen = torch.Generator(device="cuda").manual_seed(99)
-    ids = torch.randint(0, cfg.vocab, (B, S), device="cuda", dtype=torch.int32, generator=gen)
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+        group = dist.group.WORLD
+    model = GPT(cfg, seed=0, device=dev, tp=world, rank=rank, group=group,
+                nvlink_rows=B if world > 1 else 0, pdl=not args.op_times)
+    gen = torch.Generator(device=dev).manual_seed(99)
+    ids = torch.randint(0, cfg.vocab, (B, S), device=dev, dtype=torch.int32, generator=gen)
     n = max(2, args.decoder_steps)
     model.prefill(ids, n + 1)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(n + 1)]
     ev[0].record()
-    for t in range(n):
+    for t in range(n - 1 if args.op_times else n):
         model.decode_step(t)
         ev[t + 1].record()
     torch.cuda.synchronize()
-    us = [ev[t].elapsed_time(ev[t + 1]) * 1e3 for t in range(n)]
-    print(json.dumps({"decoder": args.decoder_only, "batch": B, "prompt": S,
-                      "eager_decode_step_us": us}), flush=True)
+    steps = n - 1 if args.op_times else n
+    us = [ev[t].elapsed_time(ev[t + 1]) * 1e3 for t in range(steps)]
+    out = {"decoder": args.decoder_only, "batch": B, "prompt": S, "tp": world,
+           "eager_decode_step_us": us}
+    if args.op_times:
+        barrier()
+        agg, step_us = _op_times_of_step(model, n - 1, dev)
+        names = list(agg)
+        worst = {nm: round(max_over_ranks(agg[nm][1], dev), 1) for nm in names}
+        out["op_times_step"] = {"pdl": False, "step_us": round(step_us, 1),
+                                "step_us_max_over_ranks": round(max_over_ranks(step_us, dev), 1),
+                                "sum_of_ops_us": round(sum(v[1] for v in agg.values()), 1),
+                                "ops": {nm: {"calls": agg[nm][0], "us": round(agg[nm][1], 1),
+                                             "us_max_over_ranks": worst[nm]} for nm in names}}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    model.close()
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -713,8 +798,12 @@ def run_comm_bench(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
-    rows, d, n = 32, 1024, 500
+    # one process without torchrun: a one-rank group (the tp = 1 kernels)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    rows, d, n = 32, 1024, args.comm_iters
     x = torch.randn(rows, d, device=dev).bfloat16()
     h = torch.empty_like(x)
     bias = torch.zeros(d, device=dev)
@@ -802,6 +891,10 @@ def main():
     ap.add_argument("--decoder-only", choices=["gpt2_small", "gpt_24l_1024"],
                     help="only a short eager run of this decoder (for kernel profiles)")
     ap.add_argument("--decoder-steps", type=int, default=4)
+    ap.add_argument("--op-times", action="store_true",
+                    help="with --decoder-only: per-operation times of one decode step")
+    ap.add_argument("--comm-iters", type=int, default=500,
+                    help="timed calls per variant of --comm-bench")
     ap.add_argument("--comm-bench", action="store_true",
                     help="only the tensor-parallel reduction microbenchmark (torchrun)")
     args = ap.parse_args()

@@ -28,6 +28,8 @@
  *   nd_kv_decode_attn_qkv  nd_kv_decode_attn reading a fused QKV projection row
  *   nd_kv_append        no reference counterpart (cache append for decode)
  *   nd_set_pdl          no reference counterpart (launch mode of the decode steps)
+ *   nd_set_sm_limit     no reference counterpart (SM share of the persistent
+ *                       kernels, for compute overlapped with a collective)
  *   nd_gemm_bias_act    :linear src/dispatch.jl:363-384, :fused_matmul_add
  *                       :281-296, :matmul trans_b :213-243, residual :add
  *                       :386-417, fused_linear_gelu notebook/compiler.ipynb
@@ -186,6 +188,16 @@ int nd_kv_decode_attn_qkv(void *stream, const void *qkv, int64_t qkv_ld, void *k
  * graph keep the setting they were captured with.
  */
 int nd_set_pdl(int enable, int *previous);
+
+/*
+ * Upper bound on the SMs the persistent kernels (nd_gemm_bias_act and its
+ * fused forms with more than 32 rows, the nd_flash_attn_fwd family) occupy,
+ * for launches from the calling host thread; 0 (the default) = all SMs.
+ * *previous (if not NULL) receives the earlier setting.  The SMs left free
+ * run kernels of other streams alongside, e.g. a collective that overlaps a
+ * tensor-parallel prefill's compute.  Results do not depend on it.
+ */
+int nd_set_sm_limit(int sms, int *previous);
 
 /*
  * Allocation-free KV-cache decode attention.  No counterpart in the

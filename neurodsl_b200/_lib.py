@@ -55,6 +55,7 @@ SIGNATURES = {
     "nd_kv_decode_attn_qkv": (_i, [_vp, _vp, ctypes.c_int64, _vp, _vp, _vp, _i, _vp, _i, _i, _i,
                                    _i, _i, _f, _vp, _sz]),
     "nd_set_pdl": (_i, [_i, ctypes.POINTER(_i)]),
+    "nd_set_sm_limit": (_i, [_i, ctypes.POINTER(_i)]),
     "nd_kv_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_qkv_cache": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i]),

@@ -53,9 +53,12 @@ int* device_error_word() {
 }
 namespace {
 thread_local bool t_pdl = false;
+thread_local int t_sm_limit = 0;
 }  // namespace
 bool pdl_enabled() { return t_pdl; }
 void set_pdl_enabled(bool on) { t_pdl = on; }
+int sm_limit() { return t_sm_limit; }
+void set_sm_limit(int n) { t_sm_limit = n; }
 }  // namespace nd
 
 namespace {
@@ -401,6 +404,13 @@ __attribute__((visibility("default"))) int nd_kv_decode_attn_qkv(
 __attribute__((visibility("default"))) int nd_set_pdl(int enable, int* previous) {
   if (previous != nullptr) *previous = nd::pdl_enabled() ? 1 : 0;
   nd::set_pdl_enabled(enable != 0);
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_set_sm_limit(int sms, int* previous) {
+  if (sms < 0) return fail(ND_ERR_INVALID_ARG, "nd_set_sm_limit: sms = %d must be >= 0", sms);
+  if (previous != nullptr) *previous = nd::sm_limit();
+  nd::set_sm_limit(sms);
   return ok();
 }
 

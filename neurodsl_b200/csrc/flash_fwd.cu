@@ -44,6 +44,7 @@
 #include <stdint.h>
 
 #include "flash_fwd.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "tma.h"
 
@@ -751,6 +752,7 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUten
   e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
+  sms = limited_sms(sms);
   const int n_items = ceil_div(Sq, kRowsPerCta) * BH;
   dim3 grid(n_items < sms ? n_items : sms);
   kern<<<grid, kThreads, kSmemBytes, stream>>>(tq, tk, tv, to, lay, lse, mx, BH, Sq, Sk, scale_log2,

@@ -15,8 +15,11 @@
 // TMEM accumulators alternate between tiles, so the epilogue of one tile
 // overlaps the main loop of the next.  The epilogue keeps each row in
 // registers: bias, activation and residual are applied two columns per
-// instruction (f32x2) and the row segment leaves in 16-byte stores; the
-// activation is a template parameter, so there are no per-element branches.
+// instruction (f32x2); for bf16 outputs each warp then passes its 32 rows x 32
+// columns through a small shared-memory staging buffer (80-byte pitch), so
+// that every global store instruction writes whole 64-byte row segments
+// rather than half sectors.  The activation is a template parameter, so
+// there are no per-element branches.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -1014,6 +1017,7 @@ cudaError_t launch_gemm(cudaStream_t stream, const __nv_bfloat16* A, const __nv_
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
+  sms = limited_sms(sms);
   // Tile width: fewest waves of tiles over the SMs, a wave of 128- or 64-wide
   // tiles counting half or a quarter of a 256-wide one, with a penalty for
   // the narrower tiles (each A tile is reused over fewer columns); ties keep

@@ -28,6 +28,18 @@ namespace nd {
 bool pdl_enabled();
 void set_pdl_enabled(bool on);
 
+// Upper bound on the SMs a persistent kernel (the large-M GEMM, prefill
+// attention) occupies, for launches from the calling host thread; 0 = all.
+// Leaves SMs free for kernels on other streams, e.g. a collective that
+// overlaps the compute.
+int sm_limit();
+void set_sm_limit(int n);
+// The device's SM count under the calling thread's limit.
+inline int limited_sms(int sms) {
+  const int lim = sm_limit();
+  return lim > 0 && lim < sms ? lim : sms;
+}
+
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -82,7 +82,8 @@ class GPT:
     """Weights of one rank plus the buffers of one (batch, length) shape."""
 
     def __init__(self, cfg: GPTConfig, seed=0, device=None, tp=1, rank=0, group=None,
-                 weight_std=0.02, bias_std=0.0, nvlink_rows=0, pdl=True, fused_projection=True):
+                 weight_std=0.02, bias_std=0.0, nvlink_rows=0, pdl=True, fused_projection=True,
+                 prefill_groups=2, overlap_reserve_sms=16):
         if cfg.d_head != 64:
             raise ValueError("head_dim must be 64")
         self.cfg = cfg
@@ -92,6 +93,13 @@ class GPT:
         # NVLink decode reductions compute the row-parallel projection in the
         # same launch where the shapes allow it
         self.fused_projection = fused_projection
+        # tensor-parallel prefill: the batch runs as `prefill_groups` groups of
+        # sequences on as many streams, so one group's all-reduce overlaps the
+        # others' compute; the persistent kernels leave overlap_reserve_sms
+        # SMs to the collective
+        self.prefill_groups = prefill_groups
+        self.overlap_reserve_sms = overlap_reserve_sms
+        self._side_streams = []
         self.tp, self.rank, self.group = tp, rank, group
         self.device = torch.device(device or "cuda")
         dev = self.device
@@ -223,30 +231,95 @@ class GPT:
         B, S = ids.shape
         self._alloc(B, S, max(steps, 1))
         cfg, b = self.cfg, self.buf
-        H, dl = self.n_head_local, self.d_local
         x, h = b["x"], b["h"]
         ops.embed(ids.reshape(-1), self.wte, self.wpe, b["pos_prefill"], out=x)
         ops.layernorm(x, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=h,
                       stats=False)
-        parts = b["qkv"].view(B, S, 3, H, 64).permute(2, 0, 3, 1, 4)   # [3][B][H][S][64]
-        o4 = b["attn"].view(B, S, H, 64).permute(0, 2, 1, 3)
-        for i, L in enumerate(self.layers):
-            ops.linear_qkv_cache(h, L["w_qkv"], L["b_qkv"], b["qkv"], self.k_cache[i],
-                                 self.v_cache[i], B, S)
-            ops.flash_attn_fwd(parts[0], parts[1], parts[2], causal=True, out=o4)
-            ops.linear(b["attn"], L["w_o"], out=b["part"])
-            self._all_reduce(b["part"])
-            ops.add_layernorm(x, b["part"], L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=x, out=h)
-            ops.linear(h, L["w_1"], L["b_1"], act=cfg.act, out=b["u"])
-            ops.linear(b["u"], L["w_2"], out=b["part"])
-            self._all_reduce(b["part"])
-            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
-            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
-            ops.add_layernorm(x, b["part"], L["b_2"], g_, b_, cfg.eps, s_out=x, out=h)
+        G = self.prefill_groups if self.tp > 1 else 1
+        if G > 1 and B % G == 0:
+            self._prefill_layers_overlapped(B, S, G)
+        else:
+            for i in range(cfg.n_layer):
+                for sub in self._prefill_sublayers(i, self._prefill_group(0, B, S)):
+                    sub()
         b["last"].copy_(h.view(B, S, -1)[:, -1])
         self._next_token(b["last"], b["ids"][1])
         b["ids"][0].copy_(ids[:, -1])
         return b["logits"]
+
+    def _prefill_group(self, b0, b1, S):
+        """Views of the prefill buffers and caches for sequences [b0, b1)."""
+        b, H = self.buf, self.n_head_local
+        n = b1 - b0
+        r0, r1 = b0 * S, b1 * S
+        qkv = b["qkv"][r0:r1]
+        return {"n": n, "S": S, "x": b["x"][r0:r1], "h": b["h"][r0:r1], "qkv": qkv,
+                "attn": b["attn"][r0:r1], "part": b["part"][r0:r1], "u": b["u"][r0:r1],
+                "parts": qkv.view(n, S, 3, H, 64).permute(2, 0, 3, 1, 4),   # [3][n][H][S][64]
+                "o4": b["attn"][r0:r1].view(n, S, H, 64).permute(0, 2, 1, 3),
+                "b0": b0, "b1": b1}
+
+    def _prefill_sublayers(self, i, g):
+        """Layer i of the prefill over one group of sequences as two launch
+        sequences, each ending in its tensor-parallel all-reduce: attention
+        (QKV projection filling the caches, causal attention, output
+        projection) and the MLP (residual + LN2, up, down), the residual + next
+        LayerNorm opening the following one."""
+        cfg, L = self.cfg, self.layers[i]
+        x, h, part = g["x"], g["h"], g["part"]
+        nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+        g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
+
+        def attention():
+            ops.linear_qkv_cache(h, L["w_qkv"], L["b_qkv"], g["qkv"],
+                                 self.k_cache[i][g["b0"]:g["b1"]],
+                                 self.v_cache[i][g["b0"]:g["b1"]], g["n"], g["S"])
+            p = g["parts"]
+            ops.flash_attn_fwd(p[0], p[1], p[2], causal=True, out=g["o4"])
+            ops.linear(g["attn"], L["w_o"], out=part)
+            self._all_reduce(part)
+
+        def mlp():
+            ops.add_layernorm(x, part, L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=x, out=h)
+            ops.linear(h, L["w_1"], L["b_1"], act=cfg.act, out=g["u"])
+            ops.linear(g["u"], L["w_2"], out=part)
+            self._all_reduce(part)
+
+        def close():
+            ops.add_layernorm(x, part, L["b_2"], g_, b_, cfg.eps, s_out=x, out=h)
+
+        return attention, mlp, close
+
+    def _prefill_layers_overlapped(self, B, S, G):
+        """Tensor-parallel prefill with the all-reduces overlapped: the batch
+        is split into G groups of sequences (independent through every
+        layer), group k's launches go to stream k, and the launch sequences
+        are issued round-robin, so while one group's all-reduce runs (on the
+        process group's stream, after that group's projection) the next
+        group's GEMMs and attention run beside it.  The persistent kernels are
+        capped to leave overlap_reserve_sms SMs to the collective's CTAs.  The
+        groups share no data and every kernel computes a row from that row's
+        inputs, so at tp = 2 the results are the one-stream prefill's bits; with
+        more ranks the collective may add the smaller messages' partial sums
+        in another order."""
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        while len(self._side_streams) < G - 1:
+            self._side_streams.append(torch.cuda.Stream(dev))
+        streams = [main] + self._side_streams[:G - 1]
+        for s in streams[1:]:
+            s.wait_stream(main)
+        groups = [self._prefill_group(k * B // G, (k + 1) * B // G, S) for k in range(G)]
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        with ops.sm_limit(max(1, sms - self.overlap_reserve_sms)):
+            for i in range(self.cfg.n_layer):
+                seqs = [self._prefill_sublayers(i, g) for g in groups]
+                for part in range(3):
+                    for k, s in enumerate(streams):
+                        with torch.cuda.stream(s):
+                            seqs[k][part]()
+        for s in streams[1:]:
+            main.wait_stream(s)
 
     # -------------------------------------------------------------- decode
     def decode_step(self, t):

@@ -182,6 +182,30 @@ class pdl:
         return False
 
 
+def set_sm_limit(sms):
+    """Cap the SMs this thread's persistent GEMM / prefill-attention launches
+    occupy (nd_set_sm_limit; 0 = all); returns the previous setting."""
+    prev = ctypes.c_int(0)
+    check(_lib.load().nd_set_sm_limit(int(sms), ctypes.byref(prev)))
+    return prev.value
+
+
+class sm_limit:
+    """Context manager: launches inside leave all but `sms` SMs to other
+    streams' kernels (0 = no cap), restoring the previous cap on exit."""
+
+    def __init__(self, sms):
+        self.sms = sms
+
+    def __enter__(self):
+        self.prev = set_sm_limit(self.sms)
+        return self
+
+    def __exit__(self, *exc):
+        set_sm_limit(self.prev)
+        return False
+
+
 def kv_append(k_new, v_new, k_cache, v_cache, pos, stream=None):
     _need(k_new, "k_new", torch.bfloat16, 3)
     _need(v_new, "v_new", torch.bfloat16, 3)

@@ -3,7 +3,10 @@ same seed must reproduce the one-GPU model — LM-head logits within relative
 L2 1e-2 and max-abs 5e-2 (logits spread ~0.8 here; each rank's partial sum
 is rounded to bf16 before the all-reduce, one extra rounding per sub-layer)
 and the greedy tokens wherever the one-GPU top-2 margin exceeds 5e-2 — and
-its graph-captured decode must give the same tokens as its eager decode.
+its graph-captured decode must give the same tokens as its eager decode.  Its
+prefill with the batch split into two sequence groups on two streams (each
+group's all-reduces overlapping the other's compute) gives the one-stream
+prefill's bits.
 The same holds for the tp=2 model whose decode reductions run over NVLink
 peer memory instead of NCCL, with the row-parallel projection fused into the
 exchange (nd_gemm_allreduce_add_layernorm); the same model with the
@@ -60,6 +63,18 @@ def _rank_main(rank, world, port, out_dir):
     try:
         m = GPT(GPTConfig(**CFG), seed=21, device=dev, tp=world, rank=rank,
                 group=dist.group.WORLD, weight_std=0.05, bias_std=0.02)
+        # the prefill with its two sequence groups on two streams (all-reduces
+        # overlapped with the other group's compute) against one stream, on
+        # prompts long enough that a group's GEMMs keep the many-row kernel
+        long_ids = torch.from_numpy(
+            np.random.default_rng(4).integers(0, CFG["vocab"], (B, 40)).astype(np.int32)).to(dev)
+        m.prefill_groups = 1
+        one_stream = m.prefill(long_ids, STEPS).clone()
+        caches = [c[:, :, :40].clone() for c in m.k_cache + m.v_cache]
+        m.prefill_groups = 2
+        assert torch.equal(m.prefill(long_ids, STEPS), one_stream)
+        for c, ref in zip(m.k_cache + m.v_cache, caches):
+            assert torch.equal(c[:, :, :40], ref)
         ids = torch.from_numpy(_prompt()).to(dev)
         logits, tokens = _run(m, ids)
         full = []
