@@ -331,6 +331,28 @@ def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, pari
     p_ms = max_over_ranks(min(tp_ms), dev)
     d_ms = max_over_ranks(min(td_ms), dev)
     tokens = model.tokens()[:, :4].cpu().tolist()
+    # tensor-parallel models prefill with the prompts sharded over the ranks;
+    # the Megatron prefill (sharded weights, two all-reduces per layer,
+    # overlapped in two sequence groups) is timed beside it
+    p_ms_tp = None
+    if tp > 1 and model.prefill_mode == "dp" and B % tp == 0:
+        model.prefill_mode = "tp"
+        model._prefill_graph, model._prefill_key = None, None
+        t_tp = []
+        for _ in range(reps):
+            barrier()
+            torch.cuda.synchronize()
+            ev[0].record()
+            if graphs:
+                model.prefill_graphed(ids, steps)
+            else:
+                model.prefill(ids, steps)
+            ev[1].record()
+            torch.cuda.synchronize()
+            t_tp.append(ev[0].elapsed_time(ev[1]))
+        p_ms_tp = max_over_ranks(min(t_tp), dev)
+        model.prefill_mode = "dp"
+        model._prefill_graph, model._prefill_key = None, None
     par = None
     if parity and tp > 1:
         if gi == 0:
@@ -356,8 +378,10 @@ def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, pari
                     f"F={cfg.d_ff} vocab {cfg.vocab}, batch {B} per model, prompt {S}, "
                     f"{steps} greedy tokens",
         "parallelism": layout,
-        "reduction": ("prefill: NCCL all-reduce; decode: one-shot NVLink peer reduction fused "
-                      "with residual + LayerNorm") if tp > 1 else None,
+        "reduction": ("prefill: prompts sharded over the ranks, keys/values to their heads' "
+                      "ranks by one NCCL all-to-all per layer; decode: row-parallel projection "
+                      "fused with the NVLink peer exchange, residual and LayerNorm")
+                     if tp > 1 else None,
         "scaling": "strong" if (tp > 1 and dp == 1) else "weak",
         "prefill": {"value": dp * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
                     "launch": "one CUDA graph" if graphs else "eager launches",
@@ -373,6 +397,11 @@ def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, pari
                                 "bytes": "bf16 weights + K/V read per step"}},
         "first_tokens": tokens[0],
     }
+    if p_ms_tp is not None:
+        line["prefill_tensor_parallel"] = {
+            "value": dp * B * S / (p_ms_tp * 1e-3), "unit": "tokens/s", "ms": p_ms_tp,
+            "how": "Megatron shards, NCCL all-reduce after the output and down projections, "
+                   "two sequence groups on two streams"}
     if par is not None or (parity and tp > 1):
         line["tp_parity"] = par
     return line

@@ -28,6 +28,8 @@
  *   nd_kv_decode_attn_qkv  nd_kv_decode_attn reading a fused QKV projection row
  *   nd_kv_append        no reference counterpart (cache append for decode)
  *   nd_set_pdl          no reference counterpart (launch mode of the decode steps)
+ *   nd_gemm_qkv_cache_peers  no reference counterpart (prompt-sharded prefill
+ *                       of a tensor-parallel model: K/V into the owners' caches)
  *   nd_set_sm_limit     no reference counterpart (SM share of the persistent
  *                       kernels, for compute overlapped with a collective)
  *   nd_gemm_bias_act    :linear src/dispatch.jl:363-384, :fused_matmul_add
@@ -254,6 +256,26 @@ int nd_gemm_qkv_cache(void *stream, const void *A, const void *W, const float *b
                       int pos0);
 
 /*
+ * nd_gemm_qkv_cache over all tp·H heads of a model whose decode caches are
+ * sharded by heads over tp ranks (no reference counterpart: the prefill of a
+ * tensor-parallel model with the prompts sharded over the ranks).  This
+ * rank's B prompts (sequences b0 .. b0+B-1 of the batch) are projected with
+ * the full weights (W [3·tp·H·64][K], Y [M][3·tp·H·64]); the K and V columns
+ * of head h are written straight into the caches of rank q = h / H as head
+ * h - q·H, sequence b0 + b: k_caches[q], v_caches[q] [b0+B..][H][L_max][64]
+ * bf16 are the ranks' caches mapped into this process (this rank's own
+ * included; e.g. nd_comm_alloc regions), written with plain stores over
+ * NVLink from the GEMM's epilogue.  The caller orders the ranks: no rank
+ * reads a cache while another writes it, and a rank reads its caches only
+ * after every writer's launch has finished (e.g. a collective on each
+ * rank's stream before and after).  More than 32 rows (M = B·S), 16-byte
+ * aligned bias; tp <= 8.
+ */
+int nd_gemm_qkv_cache_peers(void *stream, const void *A, const void *W, const float *bias,
+                            void *Y, int M, int K, void *const *k_caches, void *const *v_caches,
+                            int tp, int B, int b0, int S, int H, int L_max, int pos0);
+
+/*
  * Few-row linear layer with the residual add and LayerNorm in its prologue
  * (the decode-step form of residual :add + :layernorm + :linear):
  *   s = bf16(x + (p + p_bias));  Y = act(LayerNorm(s) · Wᵀ + bias)
@@ -338,6 +360,16 @@ int nd_gather_rows(void *stream, const void *table, int dtype, long long ld_tabl
  */
 int nd_copy_2d(void *stream, const void *src, long long ld_src, void *dst, long long ld_dst,
                int rows, int cols, int elem_bytes);
+
+/*
+ * nd_copy_2d over `batch` (<= 65535) such views, the b-th at src + b·bs_src
+ * and dst + b·bs_dst elements: dst[b][r][c] = src[b][r][c].  No reference
+ * counterpart: packs each rank's key/value columns of a data-parallel
+ * prefill for the all-to-all into the head-sharded decode caches.
+ */
+int nd_copy_2d_batched(void *stream, const void *src, long long ld_src, long long bs_src,
+                       void *dst, long long ld_dst, long long bs_dst, int batch, int rows,
+                       int cols, int elem_bytes);
 
 /*
  * Token embedding with learned positions: y[t] = wte[ids[t]] + wpe[pos[t]].

@@ -59,6 +59,8 @@ SIGNATURES = {
     "nd_kv_append": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_bias_act": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _vp, _i, _i, _i, _i, _i]),
     "nd_gemm_qkv_cache": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i, _i]),
+    "nd_gemm_qkv_cache_peers": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, ctypes.POINTER(_vp),
+                                     ctypes.POINTER(_vp), _i, _i, _i, _i, _i, _i, _i]),
     "nd_ln_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i]),
     "nd_gelu": (_i, [_vp, _vp, _vp, ctypes.c_int64, _i]),
     "nd_scale_mask": (_i, [_vp, _vp, _vp, _i, _i, _i]),
@@ -70,6 +72,8 @@ SIGNATURES = {
     "nd_gather_rows": (_i, [_vp, _vp, _i, ctypes.c_longlong, _i, _vp, _i, _i, _i, _i, _vp,
                             ctypes.c_longlong]),
     "nd_copy_2d": (_i, [_vp, _vp, ctypes.c_longlong, _vp, ctypes.c_longlong, _i, _i, _i]),
+    "nd_copy_2d_batched": (_i, [_vp, _vp, ctypes.c_longlong, ctypes.c_longlong, _vp,
+                                ctypes.c_longlong, ctypes.c_longlong, _i, _i, _i, _i]),
     "nd_embed": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i]),
     "nd_argmax": (_i, [_vp, _vp, _i, ctypes.c_int64, _i, _i, _vp, _vp]),
     "nd_kv_store": (_i, [_vp, _vp, ctypes.c_int64, _i, _i, _vp, _vp, _i, _i, _i, _i, _i, _i]),

@@ -570,6 +570,54 @@ __attribute__((visibility("default"))) int nd_gemm_qkv_cache(
   return ok();
 }
 
+// The QKV projection of a prompt-sharded prefill: the K/V columns of every
+// head go straight to the cache of the rank that owns the head.
+__attribute__((visibility("default"))) int nd_gemm_qkv_cache_peers(
+    void* stream, const void* A, const void* W, const float* bias, void* Y, int M, int K,
+    void* const* k_caches, void* const* v_caches, int tp, int B, int b0, int S, int H,
+    int L_max, int pos0) {
+  const char* fn = "nd_gemm_qkv_cache_peers";
+  if (M < 0 || K < 0 || B < 0 || b0 < 0 || S < 0 || H < 0 || pos0 < 0)
+    return fail(ND_ERR_INVALID_ARG, "%s: negative size", fn);
+  if (tp < 1 || tp > nd::kKvMaxPeers) return fail(ND_ERR_INVALID_ARG, "%s: tp %d (1..%d)", fn, tp, nd::kKvMaxPeers);
+  if (static_cast<long long>(B) * S != M)
+    return fail(ND_ERR_SHAPE, "%s: M = %d rows but B*S = %lld", fn, M, static_cast<long long>(B) * S);
+  if (pos0 + S > L_max)
+    return fail(ND_ERR_SHAPE, "%s: positions [%d, %d) exceed L_max %d", fn, pos0, pos0 + S, L_max);
+  if (M == 0 || H == 0) return ok();
+  if (M <= 32) return fail(ND_ERR_UNSUPPORTED, "%s: %d rows (the cache-writing epilogue needs more than 32)", fn, M);
+  if (K == 0 || K % 8) return fail(ND_ERR_SHAPE, "%s: K = %d must be a positive multiple of 8", fn, K);
+  if (!A || !W || !Y || !k_caches || !v_caches) return fail(ND_ERR_INVALID_ARG, "%s: null pointer", fn);
+  if (!aligned16(A) || !aligned16(W) || !aligned16(Y) || !aligned16(bias))
+    return fail(ND_ERR_ALIGNMENT, "%s: A/W/Y/bias must be 16-byte aligned", fn);
+  if (static_cast<long long>(b0 + B) * H > 65535) return fail(ND_ERR_SHAPE, "%s: (b0+B)*H exceeds 65535", fn);
+  nd::KvOut kv;
+  for (int q = 0; q < tp; ++q) {
+    if (!k_caches[q] || !v_caches[q] || !aligned16(k_caches[q]) || !aligned16(v_caches[q]))
+      return fail(ND_ERR_INVALID_ARG, "%s: cache of rank %d is NULL or unaligned", fn, q);
+    kv.k_peer[q] = static_cast<__nv_bfloat16*>(k_caches[q]);
+    kv.v_peer[q] = static_cast<__nv_bfloat16*>(v_caches[q]);
+  }
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  const int dl = tp * H * 64, N = 3 * dl;
+  kv.k = kv.k_peer[0];
+  kv.v = kv.v_peer[0];
+  kv.S = S;
+  kv.H = H;
+  kv.L_max = L_max;
+  kv.pos0 = pos0;
+  kv.dl = dl;
+  kv.n_peers = tp;
+  kv.b0 = b0;
+  const char* msg = nullptr;
+  cudaError_t e = nd::launch_gemm(static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(A),
+                                  static_cast<const __nv_bfloat16*>(W), bias, nullptr, false, Y,
+                                  false, M, N, K, ND_ACT_NONE, &msg, kv);
+  if (e != cudaSuccess) return cuda_fail(e, fn, msg);
+  return ok();
+}
+
 // Few-row linear layer with the residual add and LayerNorm in its prologue.
 __attribute__((visibility("default"))) int nd_ln_gemm(void* stream, const void* x, const void* p,
                                                       const float* p_bias, const float* gamma,
@@ -771,6 +819,30 @@ __attribute__((visibility("default"))) int nd_copy_2d(void* stream, const void* 
   cudaError_t e = nd::launch_copy_2d(static_cast<cudaStream_t>(stream), src, ld_src, dst, ld_dst,
                                      rows, cols, elem_bytes);
   if (e != cudaSuccess) return cuda_fail(e, "nd_copy_2d");
+  return ok();
+}
+
+__attribute__((visibility("default"))) int nd_copy_2d_batched(
+    void* stream, const void* src, long long ld_src, long long bs_src, void* dst, long long ld_dst,
+    long long bs_dst, int batch, int rows, int cols, int elem_bytes) {
+  const char* fn = "nd_copy_2d_batched";
+  if (rows < 0 || cols < 0 || batch < 0) return fail(ND_ERR_INVALID_ARG, "%s: negative size", fn);
+  if (batch > 65535) return fail(ND_ERR_SHAPE, "%s: batch %d above 65535", fn, batch);
+  if (elem_bytes != 2 && elem_bytes != 4)
+    return fail(ND_ERR_UNSUPPORTED, "%s: element size %d (2 or 4)", fn, elem_bytes);
+  if (ld_src < cols || ld_dst < cols)
+    return fail(ND_ERR_SHAPE, "%s: row strides (%lld, %lld) below cols = %d", fn, ld_src, ld_dst, cols);
+  if (batch > 1 && (bs_src < 0 || bs_dst < 0))
+    return fail(ND_ERR_SHAPE, "%s: negative batch stride", fn);
+  if (rows == 0 || cols == 0 || batch == 0) return ok();
+  if (!src || !dst) return fail(ND_ERR_INVALID_ARG, "%s: null pointer", fn);
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % elem_bytes)
+    return fail(ND_ERR_ALIGNMENT, "%s: pointers not aligned to the element size", fn);
+  int rc = check_current_device(nullptr);
+  if (rc) return rc;
+  cudaError_t e = nd::launch_copy_2d(static_cast<cudaStream_t>(stream), src, ld_src, dst, ld_dst,
+                                     rows, cols, elem_bytes, batch, bs_src, bs_dst);
+  if (e != cudaSuccess) return cuda_fail(e, fn);
   return ok();
 }
 

@@ -131,11 +131,15 @@ __global__ void __launch_bounds__(128)
   for (int c = threadIdx.x; c < d; c += blockDim.x) dst[c] = ok ? src[c] : T(0);
 }
 
-// dst[r][c] = src[r][c] in units of U (16, 4 or 2 bytes), row strides in units.
+// dst[b][r][c] = src[b][r][c] in units of U (16, 4 or 2 bytes), row and batch
+// strides in units; batch b = blockIdx.y.
 template <typename U>
-__global__ void copy_2d_kernel(const U* __restrict__ src, long long ld_src, U* __restrict__ dst,
-                               long long ld_dst, int rows, long long units) {
+__global__ void copy_2d_kernel(const U* __restrict__ src, long long ld_src, long long bs_src,
+                               U* __restrict__ dst, long long ld_dst, long long bs_dst, int rows,
+                               long long units) {
   const long long n = static_cast<long long>(rows) * units;
+  src += blockIdx.y * bs_src;
+  dst += blockIdx.y * bs_dst;
   for (long long k = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; k < n;
        k += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long r = k / units, c = k - r * units;
@@ -194,26 +198,35 @@ cudaError_t launch_gather_rows(cudaStream_t stream, const void* table, int elem_
 }
 
 cudaError_t launch_copy_2d(cudaStream_t stream, const void* src, long long ld_src, void* dst,
-                           long long ld_dst, int rows, int cols, int elem_bytes) {
+                           long long ld_dst, int rows, int cols, int elem_bytes, int batch,
+                           long long bs_src, long long bs_dst) {
   const long long row_bytes = static_cast<long long>(cols) * elem_bytes;
-  if (rows == 0 || row_bytes == 0) return cudaSuccess;
+  if (rows == 0 || row_bytes == 0 || batch == 0) return cudaSuccess;
   const long long sb = ld_src * elem_bytes, db = ld_dst * elem_bytes;
+  const long long bsb = bs_src * elem_bytes, bdb = bs_dst * elem_bytes;
   const uintptr_t align = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) |
                           static_cast<uintptr_t>(sb) | static_cast<uintptr_t>(db) |
+                          static_cast<uintptr_t>(bsb) | static_cast<uintptr_t>(bdb) |
                           static_cast<uintptr_t>(row_bytes);
-  // the widest unit that divides both addresses, both strides and a row
+  // the widest unit that divides both addresses, all strides and a row
   const int unit = (align % 16 == 0) ? 16 : (align % 4 == 0) ? 4 : 2;
   const long long units = row_bytes / unit;
-  const int grid = grid_for(static_cast<long long>(rows) * units, 256);
+  int gx = grid_for(static_cast<long long>(rows) * units, 256);
+  const int cap = (148 * 32 + batch - 1) / batch;  // about the same CTAs in total
+  if (gx > cap) gx = cap;
+  const dim3 grid(gx, batch);
   if (unit == 16)
-    copy_2d_kernel<uint4><<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src), sb / 16,
-                                                   static_cast<uint4*>(dst), db / 16, rows, units);
+    copy_2d_kernel<uint4><<<grid, 256, 0, stream>>>(static_cast<const uint4*>(src), sb / 16, bsb / 16,
+                                                   static_cast<uint4*>(dst), db / 16, bdb / 16, rows,
+                                                   units);
   else if (unit == 4)
     copy_2d_kernel<uint32_t><<<grid, 256, 0, stream>>>(static_cast<const uint32_t*>(src), sb / 4,
-                                                      static_cast<uint32_t*>(dst), db / 4, rows, units);
+                                                      bsb / 4, static_cast<uint32_t*>(dst), db / 4,
+                                                      bdb / 4, rows, units);
   else
     copy_2d_kernel<uint16_t><<<grid, 256, 0, stream>>>(static_cast<const uint16_t*>(src), sb / 2,
-                                                      static_cast<uint16_t*>(dst), db / 2, rows, units);
+                                                      bsb / 2, static_cast<uint16_t*>(dst), db / 2,
+                                                      bdb / 2, rows, units);
   return cudaGetLastError();
 }
 

@@ -25,10 +25,11 @@ cudaError_t launch_gather_rows(cudaStream_t stream, const void* table, int elem_
                                long long ld_table, int vocab, const void* idx, int idx_kind,
                                int base, int n, int d, void* out, long long ld_out, int* err_word);
 
-// dst[r][c] = src[r][c], rows x cols elements of elem_bytes (2 or 4), row
-// strides in elements.
+// dst[b][r][c] = src[b][r][c], batch x rows x cols elements of elem_bytes (2
+// or 4), row strides and batch strides in elements (batch <= 65535).
 cudaError_t launch_copy_2d(cudaStream_t stream, const void* src, long long ld_src, void* dst,
-                           long long ld_dst, int rows, int cols, int elem_bytes);
+                           long long ld_dst, int rows, int cols, int elem_bytes, int batch = 1,
+                           long long bs_src = 0, long long bs_dst = 0);
 
 // Row softmax of [rows][cols] fp32 (rows of -Inf give zeros).
 cudaError_t launch_softmax(cudaStream_t stream, const float* x, float* y, int rows, int cols);

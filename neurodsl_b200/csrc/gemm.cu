@@ -299,10 +299,22 @@ __device__ __forceinline__ void store_chunk_staged(const uint32_t (&r)[32], uint
         const int is_v = c >= kv.dl ? 1 : 0;
         const int hc = c - is_v * kv.dl;
         const int b = m / kv.S, s = m - b * kv.S;
+        int head = hc >> 6, seq = b;
+        __nv_bfloat16* base = is_v ? kv.v : kv.k;
+        if (kv.n_peers > 0) {
+          // the owning rank's cache (a select over the unrolled peer list,
+          // so the pointer array stays in the parameter space)
+          const int q = head / kv.H;
+          head -= q * kv.H;
+          seq += kv.b0;
+#pragma unroll
+          for (int j = 0; j < kKvMaxPeers; ++j)
+            if (j == q) base = is_v ? kv.v_peer[j] : kv.k_peer[j];
+        }
         const size_t idx =
-            (static_cast<size_t>(b * kv.H + (hc >> 6)) * kv.L_max + kv.pos0 + s) * 64 + (hc & 63) +
+            (static_cast<size_t>(seq * kv.H + head) * kv.L_max + kv.pos0 + s) * 64 + (hc & 63) +
             piece * 8;
-        *reinterpret_cast<uint4*>((is_v ? kv.v : kv.k) + idx) = v;
+        *reinterpret_cast<uint4*>(base + idx) = v;
       }
     }
   }

@@ -14,10 +14,19 @@ namespace nd {
 // the bf16 staged epilogue of the tensor-core path only: the caller checks
 // that the launch takes it (bf16 Y, no residual, 16-byte aligned Y and bias,
 // N % 8 == 0, dl % 64 == 0, more than 32 rows).
+// With n_peers > 0 the heads are split over n_peers ranks of H heads each:
+// head h goes to rank q = h / H, whose caches (k_peer[q], v_peer[q], peer
+// memory mapped into this process; this rank's own among them) hold it as
+// head h - q·H at sequence b0 + b; dl is then n_peers·H·64 and k, v only mark
+// the cache-writing launch.
+constexpr int kKvMaxPeers = 8;
 struct KvOut {
   __nv_bfloat16* k = nullptr;
   __nv_bfloat16* v = nullptr;
   int S = 0, H = 0, L_max = 0, pos0 = 0, dl = 0;
+  int n_peers = 0, b0 = 0;
+  __nv_bfloat16* k_peer[kKvMaxPeers] = {};
+  __nv_bfloat16* v_peer[kKvMaxPeers] = {};
 };
 
 // Y[M][N] = act(A[M][K] · W[N][K]ᵀ + bias[N]) + residual[M][N]

@@ -83,7 +83,7 @@ class GPT:
 
     def __init__(self, cfg: GPTConfig, seed=0, device=None, tp=1, rank=0, group=None,
                  weight_std=0.02, bias_std=0.0, nvlink_rows=0, pdl=True, fused_projection=True,
-                 prefill_groups=2, overlap_reserve_sms=16):
+                 prefill_groups=2, overlap_reserve_sms=16, prefill_mode="dp"):
         if cfg.d_head != 64:
             raise ValueError("head_dim must be 64")
         self.cfg = cfg
@@ -100,6 +100,13 @@ class GPT:
         self.prefill_groups = prefill_groups
         self.overlap_reserve_sms = overlap_reserve_sms
         self._side_streams = []
+        # tensor-parallel models prefill with the prompts sharded by default: each
+        # rank runs whole layers (full weights) for B/tp prompts and sends the
+        # keys/values of the other ranks' heads to them ("dp"); "tp" prefills
+        # with the sharded weights and all-reduces
+        if prefill_mode not in ("dp", "tp"):
+            raise ValueError(f"prefill_mode {prefill_mode!r} (dp or tp)")
+        self.prefill_mode = prefill_mode
         self.tp, self.rank, self.group = tp, rank, group
         self.device = torch.device(device or "cuda")
         dev = self.device
@@ -123,6 +130,7 @@ class GPT:
         self.wte = randn(V, d).to(bf)
         self.wpe = randn(cfg.n_pos, d).to(bf)
         self.layers = []
+        self.full_layers = []          # full bf16 weights of each layer (tp > 1)
         cols = slice(h0 * 64, h1 * 64)
         for _ in range(cfg.n_layer):
             ln1_g = 1 + randn(d, std=0.1) if bias_std else torch.ones(d, device=dev)
@@ -149,6 +157,10 @@ class GPT:
                 "w_1": w_1[f0:f1].to(bf).contiguous(), "b_1": b_1[f0:f1].contiguous(),
                 "w_2": w_2[:, f0:f1].to(bf).contiguous(), "b_2": b_2,
             })
+            if tp > 1:
+                self.full_layers.append({"w_qkv": w_qkv.to(bf), "b_qkv": b_qkv,
+                                         "w_o": w_o.to(bf), "w_1": w_1.to(bf), "b_1": b_1,
+                                         "w_2": w_2.to(bf)})
         self.lnf_g = torch.ones(d, device=dev)
         self.lnf_b = torch.zeros(d, device=dev)
         self.w_head = self.wte[self.v0:self.v1]           # tied LM head, local vocab rows
@@ -195,13 +207,63 @@ class GPT:
         ws = ops.kv_decode_workspace_size(B, self.n_head_local, L_max)
         # decode scratch owned here (zero-filled once, left ready by every call)
         self.buf["ws"] = torch.zeros(max(ws, 16), device=dev, dtype=torch.uint8)
-        self.k_cache = [torch.zeros(B, self.n_head_local, L_max, 64, device=dev, dtype=bf)
-                        for _ in range(cfg.n_layer)]
-        self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
+        self._alloc_caches(B, L_max)
         if self.tp > 1:
             self.buf["gval"] = torch.empty(self.tp, B, device=dev, dtype=torch.float32)
             self.buf["gidx"] = torch.empty(self.tp, B, device=dev, dtype=torch.int32)
         self._shape = (B, S, steps)
+
+    def _alloc_caches(self, B, L_max):
+        """Decode caches [B][H_local][L_max][64] per layer.  Tensor-parallel
+        models keep all of a rank's caches in one region shared with the other
+        ranks (CUDA IPC), so a prompt-sharded prefill writes each head's keys
+        and values straight into its owner's cache; every rank maps the
+        others' regions."""
+        cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+        shape = (B, self.n_head_local, L_max, 64)
+        self._free_cache_region()
+        if self.tp == 1:
+            self.k_cache = [torch.zeros(shape, device=dev, dtype=bf) for _ in range(cfg.n_layer)]
+            self.v_cache = [torch.zeros_like(c) for c in self.k_cache]
+            return
+        import torch.distributed as dist
+
+        from .comm import _DeviceArray
+        n = B * self.n_head_local * L_max * 64          # elements per cache
+        nbytes = 2 * cfg.n_layer * n * 2
+        ptr, handle = ops.comm_alloc(nbytes)            # zero-filled
+        handles = [None] * self.tp
+        dist.all_gather_object(handles, handle, group=self.group)
+        bases = [ptr if q == self.rank else ops.comm_open(handles[q]) for q in range(self.tp)]
+        self._cache_region = (ptr, bases)
+        region = torch.as_tensor(_DeviceArray(ptr, (2 * cfg.n_layer * n,), "<i2"),
+                                 device=dev).view(bf)
+        self.k_cache = [region[(2 * i) * n:(2 * i + 1) * n].view(shape) for i in range(cfg.n_layer)]
+        self.v_cache = [region[(2 * i + 1) * n:(2 * i + 2) * n].view(shape)
+                        for i in range(cfg.n_layer)]
+        # every rank's cache of layer i, as this process sees it
+        self._peer_k = [[base + 2 * (2 * i) * n for base in bases] for i in range(cfg.n_layer)]
+        self._peer_v = [[base + 2 * (2 * i + 1) * n for base in bases] for i in range(cfg.n_layer)]
+        self._cache_sync = torch.zeros(1, device=dev)
+
+    def _free_cache_region(self):
+        """Unmap the peers' cache regions and free this rank's once no rank
+        uses them (collective over the model's group)."""
+        region = getattr(self, "_cache_region", None)
+        if region is None:
+            return
+        import torch.distributed as dist
+        ptr, bases = region
+        self.k_cache = self.v_cache = []
+        self._peer_k = self._peer_v = None
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)       # no rank writes or reads any cache any more
+        for q, base in enumerate(bases):
+            if q != self.rank:
+                ops.comm_close(base)
+        dist.barrier(group=self.group)       # every mapping of this region is closed
+        ops.comm_free(ptr)
+        self._cache_region = None
 
     def _all_reduce(self, t):
         if self.tp > 1:
@@ -231,21 +293,126 @@ class GPT:
         B, S = ids.shape
         self._alloc(B, S, max(steps, 1))
         cfg, b = self.cfg, self.buf
-        x, h = b["x"], b["h"]
-        ops.embed(ids.reshape(-1), self.wte, self.wpe, b["pos_prefill"], out=x)
-        ops.layernorm(x, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=h,
-                      stats=False)
-        G = self.prefill_groups if self.tp > 1 else 1
-        if G > 1 and B % G == 0:
-            self._prefill_layers_overlapped(B, S, G)
+        if self.tp > 1 and self.prefill_mode == "dp" and B % self.tp == 0:
+            self._prefill_sharded_prompts(ids, B, S)
         else:
-            for i in range(cfg.n_layer):
-                for sub in self._prefill_sublayers(i, self._prefill_group(0, B, S)):
-                    sub()
-        b["last"].copy_(h.view(B, S, -1)[:, -1])
+            x, h = b["x"], b["h"]
+            ops.embed(ids.reshape(-1), self.wte, self.wpe, b["pos_prefill"], out=x)
+            ops.layernorm(x, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps,
+                          out=h, stats=False)
+            G = self.prefill_groups if self.tp > 1 else 1
+            if G > 1 and B % G == 0:
+                self._prefill_layers_overlapped(B, S, G)
+            else:
+                for i in range(cfg.n_layer):
+                    for sub in self._prefill_sublayers(i, self._prefill_group(0, B, S)):
+                        sub()
+            b["last"].copy_(h.view(B, S, -1)[:, -1])
         self._next_token(b["last"], b["ids"][1])
         b["ids"][0].copy_(ids[:, -1])
         return b["logits"]
+
+    def _shard_buffers(self, B, S):
+        """Buffers of the prompt-sharded prefill for this rank's B/tp prompts."""
+        key = (B, S)
+        if getattr(self, "_shard_key", None) != key:
+            cfg, dev, bf = self.cfg, self.device, torch.bfloat16
+            d, F, tp, dl = cfg.d_model, cfg.d_ff, self.tp, self.d_local
+            T = B // tp * S
+            self._shard = {
+                "x": torch.empty(T, d, device=dev, dtype=bf), "h": torch.empty(T, d, device=dev, dtype=bf),
+                "qkv": torch.empty(T, 3 * d, device=dev, dtype=bf),
+                "attn": torch.empty(T, d, device=dev, dtype=bf),
+                "part": torch.empty(T, d, device=dev, dtype=bf),
+                "u": torch.empty(T, F, device=dev, dtype=bf),
+                "last": torch.empty(B // tp, d, device=dev, dtype=bf),
+                # keys and values of this rank's tokens for rank q: send[q][t][k | v][dl]
+                "send": torch.empty(tp, T, 2, dl, device=dev, dtype=bf),
+                # every rank's tokens (global token order) for this rank's heads
+                "recv": torch.empty(B * S, 2 * dl, device=dev, dtype=bf),
+            }
+            self._shard_key = key
+        return self._shard
+
+    def _prefill_sharded_prompts(self, ids, B, S):
+        """Prefill of a tensor-parallel model with the prompts sharded over the
+        ranks: rank r runs every layer with the full weights for prompts
+        [r·B/tp, (r+1)·B/tp) — the one-GPU prefill of those prompts, with no
+        reduction — and after each layer's QKV projection sends the keys and
+        values of rank q's heads to rank q (one all-to-all, on a side stream
+        so it overlaps the rest of the layer), which writes them into its
+        head-sharded decode caches — or, for more than 32 rows, the QKV
+        projection's epilogue stores them straight into the owners' caches
+        over NVLink (nd_gemm_qkv_cache_peers), with no copy, collective or
+        extra launch.  The last positions' hidden states are all-gathered for
+        the vocabulary-sharded LM head.  The caches and the
+        LM head's input are those of the one-GPU model bit for bit; the
+        communication is the keys and values once, instead of two all-reduces
+        of the activations per layer."""
+        cfg, b = self.cfg, self.buf
+        tp, r, dl, H, d = self.tp, self.rank, self.d_local, cfg.n_head, cfg.d_model
+        Bl = B // tp
+        T = Bl * S
+        sp = self._shard_buffers(B, S)
+        x, h, qkv, attn = (sp[k] for k in ("x", "h", "qkv", "attn"))
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        if not self._side_streams:
+            self._side_streams.append(torch.cuda.Stream(dev))
+        side = self._side_streams[0]
+        side.wait_stream(main)               # the side stream joins this prefill (or its capture)
+        ops.embed(ids[r * Bl:(r + 1) * Bl].reshape(-1), self.wte, self.wpe,
+                  b["pos_prefill"][:T], out=x)
+        ops.layernorm(x, self.layers[0]["ln1_g"], self.layers[0]["ln1_b"], eps=cfg.eps, out=h,
+                      stats=False)
+        parts = qkv.view(Bl, S, 3, H, 64).permute(2, 0, 3, 1, 4)   # [3][Bl][H][S][64]
+        o4 = attn.view(Bl, S, H, 64).permute(0, 2, 1, 3)
+        # the K (then V) columns of rank q's heads: [tp][T][dl] views of qkv
+        cols = [qkv[:, (1 + kv) * d:(2 + kv) * d].view(T, tp, dl).permute(1, 0, 2) for kv in (0, 1)]
+        # no rank still reads its caches (an earlier decode) when the others
+        # start writing into them
+        torch.distributed.all_reduce(self._cache_sync, group=self.group)
+        # the all-to-all form (few rows) leaves SMs to the collective; the
+        # direct form needs none (its transfers are the GEMM's own stores)
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        reserve = self.overlap_reserve_sms if T <= 32 else 0
+        with ops.sm_limit(max(1, sms - reserve) if reserve > 0 else 0):
+            self._sharded_layers(cfg, sp, cols, parts, o4, side, main, B, S, dl)
+        sp["last"].copy_(h.view(Bl, S, -1)[:, -1])
+        torch.distributed.all_gather_into_tensor(b["last"], sp["last"], group=self.group)
+        main.wait_stream(side)
+
+    def _sharded_layers(self, cfg, sp, cols, parts, o4, side, main, B, S, dl):
+        """The layers of the prompt-sharded prefill (see _prefill_sharded_prompts)."""
+        x, h, qkv, attn, part, u = (sp[k] for k in ("x", "h", "qkv", "attn", "part", "u"))
+        Bl = B // self.tp
+        L_max = self.k_cache[0].shape[2]
+        # more than 32 rows: the projection's epilogue writes every head's keys
+        # and values into its owner's cache over NVLink; else an all-to-all
+        direct = Bl * S > 32
+        for i, (L, FL) in enumerate(zip(self.layers, self.full_layers)):
+            if direct:
+                ops.linear_qkv_cache_peers(h, FL["w_qkv"], FL["b_qkv"], qkv, self._peer_k[i],
+                                           self._peer_v[i], self.n_head_local, L_max, Bl,
+                                           self.rank * Bl, S)
+            else:
+                ops.linear(h, FL["w_qkv"], FL["b_qkv"], out=qkv)
+                main.wait_stream(side)           # the previous layer's all-to-all has read send
+                for kv in (0, 1):
+                    ops.copy_2d_batched(cols[kv], sp["send"][:, :, kv, :])
+                side.wait_stream(main)
+                with torch.cuda.stream(side):
+                    torch.distributed.all_to_all_single(sp["recv"].view(-1), sp["send"].view(-1),
+                                                        group=self.group)
+                    ops.kv_store(sp["recv"], 0, dl, self.k_cache[i], self.v_cache[i], B, S)
+            ops.flash_attn_fwd(parts[0], parts[1], parts[2], causal=True, out=o4)
+            ops.linear(attn, FL["w_o"], out=part)
+            ops.add_layernorm(x, part, L["b_o"], L["ln2_g"], L["ln2_b"], cfg.eps, s_out=x, out=h)
+            ops.linear(h, FL["w_1"], FL["b_1"], act=cfg.act, out=u)
+            ops.linear(u, FL["w_2"], out=part)
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            g_, b_ = (nxt["ln1_g"], nxt["ln1_b"]) if nxt else (self.lnf_g, self.lnf_b)
+            ops.add_layernorm(x, part, L["b_2"], g_, b_, cfg.eps, s_out=x, out=h)
 
     def _prefill_group(self, b0, b1, S):
         """Views of the prefill buffers and caches for sequences [b0, b1)."""
@@ -476,6 +643,8 @@ class GPT:
         """Release graphs and the NVLink reduction regions (collective when
         tensor-parallel: every rank calls it before the group is destroyed)."""
         self.release_graphs()
+        self._free_cache_region()
+        self._shape = None
         if self.comm is not None:
             self.comm.close()
             self.comm = None

@@ -270,6 +270,28 @@ def linear_qkv_cache(A, W, bias, out, k_cache, v_cache, B, S, pos0=0, stream=Non
     return out
 
 
+def linear_qkv_cache_peers(A, W, bias, out, k_caches, v_caches, H, L_max, B, b0, S, pos0=0,
+                           stream=None):
+    """The full-head QKV projection of this rank's B prompts (sequences b0..)
+    writing the K/V columns of head h into the cache of rank h // H
+    (nd_gemm_qkv_cache_peers); k_caches / v_caches: every rank's cache base
+    pointer (ints, [..][H][L_max][64] bf16), this rank's own included."""
+    _need(A, "A", torch.bfloat16, 2)
+    _need(W, "W", torch.bfloat16, 2)
+    _need(out, "out", torch.bfloat16, 2)
+    _need(bias, "bias", torch.float32, 1)
+    tp = len(k_caches)
+    M, K = A.shape
+    if W.shape != (3 * tp * H * 64, K) or tuple(out.shape) != (M, 3 * tp * H * 64) or M != B * S:
+        raise ValueError("QKV projection / cache shape mismatch")
+    kc = (ctypes.c_void_p * tp)(*k_caches)
+    vc = (ctypes.c_void_p * tp)(*v_caches)
+    check(_lib.load().nd_gemm_qkv_cache_peers(_stream(stream), _ptr(A), _ptr(W), _ptr(bias),
+                                              _ptr(out), M, K, kc, vc, tp, int(B), int(b0),
+                                              int(S), int(H), int(L_max), int(pos0)))
+    return out
+
+
 def ln_linear(x, W, p=None, p_bias=None, gamma=None, beta=None, eps=1e-5, s_out=None, bias=None,
               act="none", out=None, out_dtype=torch.bfloat16, stream=None):
     """Y = act(LayerNorm(x + p + p_bias)·Wᵀ + bias) for at most 32 rows, with
@@ -457,6 +479,21 @@ def copy_2d(src, dst, stream=None):
     ld = lambda t: t.stride(0) if rows > 1 else cols
     check(_lib.load().nd_copy_2d(_stream(stream), _ptr(src), ld(src), _ptr(dst), ld(dst), rows,
                                  cols, src.element_size()))
+    return dst
+
+
+def copy_2d_batched(src, dst, stream=None):
+    """dst[b, :, :] = src[b, :, :] for 3-D views whose rows are contiguous
+    (nd_copy_2d_batched: any batch and row strides)."""
+    for name, t in (("src", src), ("dst", dst)):
+        if not t.is_cuda or t.dim() != 3 or (t.shape[2] > 1 and t.stride(2) != 1):
+            raise ValueError(f"{name} must be a 3-D CUDA view with contiguous rows")
+    if tuple(src.shape) != tuple(dst.shape) or src.dtype != dst.dtype:
+        raise ValueError("src and dst differ in shape or dtype")
+    batch, rows, cols = src.shape
+    check(_lib.load().nd_copy_2d_batched(_stream(stream), _ptr(src), src.stride(1), src.stride(0),
+                                         _ptr(dst), dst.stride(1), dst.stride(0), batch, rows,
+                                         cols, src.element_size()))
     return dst
 
 

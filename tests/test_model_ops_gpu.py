@@ -146,3 +146,54 @@ def test_qkv_projection_fills_the_caches(B, S, H, K, pos0, bias_off):
     torch.cuda.synchronize()
     assert torch.equal(y, y_ref)
     assert torch.equal(kc, kc_ref) and torch.equal(vc, vc_ref)
+
+
+@pytest.mark.parametrize("tp,Bl,rank,S,Hl,K", [(2, 2, 1, 40, 2, 128), (4, 1, 2, 50, 3, 192),
+                                                (8, 3, 0, 17, 1, 64)])
+def test_qkv_projection_into_the_owners_caches(tp, Bl, rank, S, Hl, K):
+    """nd_gemm_qkv_cache_peers (the prompt-sharded prefill of a tensor-parallel
+    model) on one GPU, the tp ranks' caches being separate local buffers: the
+    projection is nd_gemm_bias_act's, and head h's keys/values land in cache
+    h // Hl as head h % Hl of sequences rank·Bl .. — the full-head
+    nd_gemm_qkv_cache rows, bit for bit; nothing else of any cache changes."""
+    ops = _ops()
+    gen = torch.Generator(device="cuda").manual_seed(tp * 100 + S)
+    bf = torch.bfloat16
+    H = tp * Hl
+    B, M, N, L_max = tp * Bl, Bl * S, 3 * H * 64, S + 4
+    A = torch.randn(M, K, device="cuda", generator=gen).to(bf)
+    W = (0.05 * torch.randn(N, K, device="cuda", generator=gen)).to(bf)
+    bias = torch.randn(N, device="cuda", generator=gen)
+    # the full-head caches of this rank's prompts, as one GPU fills them
+    kf = torch.zeros(Bl, H, L_max, 64, device="cuda", dtype=bf)
+    vf = torch.zeros_like(kf)
+    y_ref = torch.empty(M, N, device="cuda", dtype=bf)
+    ops.linear_qkv_cache(A, W, bias, y_ref, kf, vf, Bl, S)
+    kc0 = [torch.randn(B, Hl, L_max, 64, device="cuda", generator=gen).to(bf) for _ in range(tp)]
+    vc0 = [torch.randn(B, Hl, L_max, 64, device="cuda", generator=gen).to(bf) for _ in range(tp)]
+    kc, vc = [c.clone() for c in kc0], [c.clone() for c in vc0]
+    y = torch.empty_like(y_ref)
+    ops.linear_qkv_cache_peers(A, W, bias, y, [c.data_ptr() for c in kc], [c.data_ptr() for c in vc],
+                               Hl, L_max, Bl, rank * Bl, S)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    b0 = rank * Bl
+    for q in range(tp):
+        for got, ref, base in ((kc[q], kf, kc0[q]), (vc[q], vf, vc0[q])):
+            want = base.clone()
+            want[b0:b0 + Bl, :, :S] = ref[:, q * Hl:(q + 1) * Hl, :S]
+            assert torch.equal(got, want), q
+
+
+def test_qkv_projection_into_the_owners_caches_rejects():
+    ops = _ops()
+    from neurodsl_b200._lib import NeuroDSLError
+    bf = torch.bfloat16
+    A = torch.zeros(16, 64, device="cuda", dtype=bf)     # 16 rows: the epilogue path needs > 32
+    W = torch.zeros(3 * 2 * 64, 64, device="cuda", dtype=bf)
+    bias = torch.zeros(3 * 2 * 64, device="cuda")
+    y = torch.empty(16, 3 * 2 * 64, device="cuda", dtype=bf)
+    c = [torch.zeros(2, 1, 20, 64, device="cuda", dtype=bf) for _ in range(2)]
+    ptrs = [t.data_ptr() for t in c]
+    with pytest.raises(NeuroDSLError):
+        ops.linear_qkv_cache_peers(A, W, bias, y, ptrs, ptrs, 1, 20, 1, 0, 16)

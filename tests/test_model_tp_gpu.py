@@ -4,9 +4,11 @@ L2 1e-2 and max-abs 5e-2 (logits spread ~0.8 here; each rank's partial sum
 is rounded to bf16 before the all-reduce, one extra rounding per sub-layer)
 and the greedy tokens wherever the one-GPU top-2 margin exceeds 5e-2 — and
 its graph-captured decode must give the same tokens as its eager decode.  Its
-prefill with the batch split into two sequence groups on two streams (each
-group's all-reduces overlapping the other's compute) gives the one-stream
-prefill's bits.
+tensor-parallel prefill with the batch split into two sequence groups on two
+streams (each group's all-reduces overlapping the other's compute) gives the
+one-stream prefill's bits, and its default prefill with the prompts sharded
+over the ranks (whole layers per rank, keys/values sent to their heads' ranks)
+gives the one-GPU model's prefill logits and caches bit for bit.
 The same holds for the tp=2 model whose decode reductions run over NVLink
 peer memory instead of NCCL, with the row-parallel projection fused into the
 exchange (nd_gemm_allreduce_add_layernorm); the same model with the
@@ -44,6 +46,13 @@ def _prompt():
     return np.random.default_rng(9).integers(0, CFG["vocab"], (B, S)).astype(np.int32)
 
 
+LONG = 40   # prompts long enough that every GEMM of a one-prompt shard keeps the many-row kernel
+
+
+def _long_prompt():
+    return np.random.default_rng(4).integers(0, CFG["vocab"], (B, LONG)).astype(np.int32)
+
+
 def _run(model, ids):
     logits = [model.prefill(ids, STEPS).clone()]
     for t in range(STEPS - 1):
@@ -66,15 +75,26 @@ def _rank_main(rank, world, port, out_dir):
         # the prefill with its two sequence groups on two streams (all-reduces
         # overlapped with the other group's compute) against one stream, on
         # prompts long enough that a group's GEMMs keep the many-row kernel
-        long_ids = torch.from_numpy(
-            np.random.default_rng(4).integers(0, CFG["vocab"], (B, 40)).astype(np.int32)).to(dev)
+        long_ids = torch.from_numpy(_long_prompt()).to(dev)
+        m.prefill_mode = "tp"
         m.prefill_groups = 1
         one_stream = m.prefill(long_ids, STEPS).clone()
-        caches = [c[:, :, :40].clone() for c in m.k_cache + m.v_cache]
+        caches = [c[:, :, :LONG].clone() for c in m.k_cache + m.v_cache]
         m.prefill_groups = 2
         assert torch.equal(m.prefill(long_ids, STEPS), one_stream)
         for c, ref in zip(m.k_cache + m.v_cache, caches):
-            assert torch.equal(c[:, :, :40], ref)
+            assert torch.equal(c[:, :, :LONG], ref)
+        # the prompt-sharded prefill (the default): each rank runs whole layers
+        # for its prompts, keys/values go to their heads' ranks by all-to-all
+        m.prefill_mode = "dp"
+        sharded = m.prefill(long_ids, STEPS)
+        parts = [torch.empty_like(sharded) for _ in range(world)]
+        dist.all_gather(parts, sharded)
+        np.save(os.path.join(out_dir, f"sharded_caches_{rank}.npy"),
+                np.stack([c[:, :, :LONG].float().cpu().numpy() for c in m.k_cache + m.v_cache]))
+        if rank == 0:
+            np.save(os.path.join(out_dir, "sharded_logits.npy"),
+                    torch.cat(parts, dim=1).cpu().numpy())
         ids = torch.from_numpy(_prompt()).to(dev)
         logits, tokens = _run(m, ids)
         full = []
@@ -125,6 +145,16 @@ def test_tp2_matches_single_gpu(tmp_path):
     mp.start_processes(_rank_main, args=(2, _port(), str(tmp_path)), nprocs=2, join=True,
                        start_method="spawn")
     ref = GPT(GPTConfig(**CFG), seed=21, device="cuda:0", weight_std=0.05, bias_std=0.02)
+    # the prompt-sharded prefill computes the one-GPU prefill: same logits and
+    # caches (each rank's heads), bit for bit
+    ref_long = ref.prefill(torch.from_numpy(_long_prompt()).cuda(), STEPS).cpu().numpy()
+    np.testing.assert_array_equal(np.load(tmp_path / "sharded_logits.npy"), ref_long)
+    hl = CFG["n_head"] // 2
+    for r in range(2):
+        got = np.load(tmp_path / f"sharded_caches_{r}.npy")
+        want = np.stack([c[:, r * hl:(r + 1) * hl, :LONG].float().cpu().numpy()
+                         for c in ref.k_cache + ref.v_cache])
+        np.testing.assert_array_equal(got, want)
     ref_logits, ref_tokens = _run(ref, torch.from_numpy(_prompt()).cuda())
     ref_logits = np.stack([x.cpu().numpy() for x in ref_logits])
     ref_tokens = ref_tokens.cpu().numpy()
