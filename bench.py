@@ -664,7 +664,8 @@ def run_ours(args):
                 "value": dec_tokens, "unit": "tokens/s", "ms_per_pass": dec_ms,
                 "us_per_token_step": dec_ms * 1e3 / DEC_T,
                 "gpu_launches": dec_reps * DEC_T,
-                "launch": "128 steps captured in one CUDA graph, replayed",
+                "launch": f"{DEC_T} steps captured in one CUDA graph, replayed; one "
+                          f"kv_decode_kernel launch per step, {dec_reps} timed passes",
                 "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": peaks["hbm_gbs"],
                              "unit": "GB/s", "frac": dec_gbs / peaks["hbm_gbs"],
                              "traffic": dec_traffic,
