@@ -279,13 +279,16 @@ def tp_parity(model, cfg, ids, group, tp, dev, steps=16):
     return out
 
 
-def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, parity):
+def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, parity,
+               split_batch=False):
     """Prefill and greedy decode of a GPT-style decoder built from the library
     (neurodsl_b200.model).  The world is split into world/tp groups of tp
-    consecutive ranks; each group runs one tensor-parallel model (Megatron
-    shards; NCCL all-reduces for prefill, the NVLink peer reduction for
-    decode) on its own batch.  tp == world: one model over all GPUs (strong
-    scaling); tp == 1: one replica per GPU (weak scaling)."""
+    consecutive ranks; each group runs one tensor-parallel model (prompt-
+    sharded prefill writing the keys/values into the owning ranks' caches;
+    decode with the row-parallel projection fused with the NVLink exchange)
+    on its own batch.  tp == world: one model over all GPUs (strong scaling);
+    tp == 1: one replica per GPU (weak scaling), or with split_batch one
+    global batch of B·world prompts split over the replicas (strong)."""
     import torch
     import torch.distributed as dist
 
@@ -367,7 +370,9 @@ def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, pari
     dec_bytes = decode_weight_bytes(cfg) * n_dec + kv   # one model, all its ranks together
     p_tflops = dp * fl / (p_ms * 1e-3) / 1e12
     d_gbs = dp * dec_bytes / (d_ms * 1e-3) / 1e9
-    if tp == 1:
+    if tp == 1 and split_batch:
+        layout = f"dp{world} replicas, global batch {B * world} split over them"
+    elif tp == 1:
         layout = f"dp{world} replicas"
     elif dp == 1:
         layout = f"tp{tp}"
@@ -382,7 +387,7 @@ def model_line(name, cfg, B, S, steps, tp, groups, dev, peaks, reps, chunk, pari
                       "ranks by one NCCL all-to-all per layer; decode: row-parallel projection "
                       "fused with the NVLink peer exchange, residual and LayerNorm")
                      if tp > 1 else None,
-        "scaling": "strong" if (tp > 1 and dp == 1) else "weak",
+        "scaling": "strong" if ((tp > 1 and dp == 1) or split_batch) else "weak",
         "prefill": {"value": dp * B * S / (p_ms * 1e-3), "unit": "tokens/s", "ms": p_ms,
                     "launch": "one CUDA graph" if graphs else "eager launches",
                     "roofline": {"bound": "tensor", "achieved": p_tflops / world,
@@ -637,6 +642,12 @@ def run_ours(args):
                                                  min(world, 4), groups, dev, peaks, 2, 32, True)
         models["gpt_24l_1024"] = model_line("24-layer", GPT_24L_1024, 32, 2048, 512, world, groups,
                                             dev, peaks, 2, 64, True)
+        if world > 1 and 32 % world == 0:
+            # the same 32 prompts as replicas of the whole model, 32/N per GPU
+            # (no collective on the data path): the data-parallel counterpart
+            models["gpt_24l_1024_dp"] = model_line("24-layer", GPT_24L_1024, 32 // world, 2048,
+                                                   512, 1, groups, dev, peaks, 2, 64, False,
+                                                   split_batch=True)
     traffic = load_traffic("flash_fwd_causal_b8_h16_s2048_d64")
     dec_traffic = load_traffic("kv_decode_b64_h12_l1024_d64")
     if rank == 0:
