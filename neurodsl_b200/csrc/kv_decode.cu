@@ -245,16 +245,38 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (s_ticket != static_cast<unsigned int>(nchunks - 1)) return;
 
-  // Last CTA of this head: merge every chunk's partial.
+  // Last CTA of this head: merge every chunk's partial.  The global max
+  // first (thread t reads chunk t's max; a block reduction), then each output
+  // dim sums its chunks in order, eight chunks' loads in flight at a time, so
+  // the partials' L2 reads overlap instead of taking one round trip per chunk.
   const ChunkPartial* all = partials + static_cast<size_t>(bh) * nchunks;
-  float gm = -INFINITY;
-  for (int c = 0; c < nchunks; ++c) gm = fmaxf(gm, __ldcg(&all[c].m));
+  float tm = -INFINITY;
+  for (int c = threadIdx.x; c < nchunks; c += kThreads) tm = fmaxf(tm, __ldcg(&all[c].m));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, o));
+  __shared__ float s_gm[kThreads / 32];
+  if (lane == 0) s_gm[warp] = tm;
+  __syncthreads();
+  float gm = s_gm[0];
+#pragma unroll
+  for (int w = 1; w < kThreads / 32; ++w) gm = fmaxf(gm, s_gm[w]);
   float gl = 0.f, gacc = 0.f;
-  for (int c = 0; c < nchunks; ++c) {
-    const float mc = __ldcg(&all[c].m);
-    const float f = (mc == -INFINITY) ? 0.f : exp2f(mc - gm);
-    gl += __ldcg(&all[c].l) * f;
-    if (dim < kD) gacc += __ldcg(&all[c].acc[dim]) * f;
+  for (int c0 = 0; c0 < nchunks; c0 += 8) {
+    float mc[8], lc[8], ac[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int c = c0 + u;
+      const bool in = c < nchunks;
+      mc[u] = in ? __ldcg(&all[c].m) : -INFINITY;
+      lc[u] = in ? __ldcg(&all[c].l) : 0.f;
+      ac[u] = (in && dim < kD) ? __ldcg(&all[c].acc[dim]) : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float f = (mc[u] == -INFINITY) ? 0.f : exp2f(mc[u] - gm);
+      gl += lc[u] * f;
+      gacc += ac[u] * f;
+    }
   }
   if (dim < kD) store_out<kOutF32>(out, static_cast<size_t>(bh) * kD + dim, gacc / gl);
   if (dim == 0) {
