@@ -13,6 +13,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/neurodsl_b200.h"
@@ -59,6 +60,18 @@ bool pdl_enabled() { return t_pdl; }
 void set_pdl_enabled(bool on) { t_pdl = on; }
 int sm_limit() { return t_sm_limit; }
 void set_sm_limit(int n) { t_sm_limit = n; }
+int current_sm_count() {
+  static std::atomic<int> counts[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = counts[dev].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      return 148;
+    counts[dev].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
 }  // namespace nd
 
 namespace {

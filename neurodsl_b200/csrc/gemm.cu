@@ -668,7 +668,7 @@ template <int kMB, bool kOutF32, int kAct>
 cudaError_t launch_skinny_act(cudaStream_t stream, const __nv_bfloat16* A, const __nv_bfloat16* W,
                               const float* bias, const void* residual, bool residual_f32, void* Y,
                               int M, int N, int K) {
-  const int ks = skinny_ksplit(N, K);
+  const int ks = skinny_ksplit(N, K, current_sm_count());
   const dim3 grid(((N + 7) / 8) * ks);
   if (residual != nullptr)
     return launch_ex(skinny_gemm_kernel<kMB, kOutF32, kAct, true>, grid, dim3(kSkinnyWarps * 32), 0,

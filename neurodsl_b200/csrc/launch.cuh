@@ -34,6 +34,8 @@ void set_pdl_enabled(bool on);
 // overlaps the compute.
 int sm_limit();
 void set_sm_limit(int n);
+// The current device's SM count (cached per device).
+int current_sm_count();
 // The device's SM count under the calling thread's limit.
 inline int limited_sms(int sms) {
   const int lim = sm_limit();

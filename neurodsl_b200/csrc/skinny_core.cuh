@@ -19,8 +19,14 @@
 
 namespace nd {
 
+// Tuning switch (compile-time): k chunks of 32 per warp whose loads are
+// issued together; the split-K policy below sizes clusters so that one such
+// batch covers a warp's share of K.
+#ifndef ND_SKINNY_BATCH
+#define ND_SKINNY_BATCH 4
+#endif
 constexpr int kSkinnyWarps = 8;
-constexpr int kSkinnyBatch = 4;  // k chunks whose loads are issued together
+constexpr int kSkinnyBatch = ND_SKINNY_BATCH;  // k chunks whose loads are issued together
 constexpr int kSkinnyMaxSplit = 8;
 
 __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1,
@@ -38,15 +44,19 @@ __device__ __forceinline__ uint4 ldg16_or_zero(const __nv_bfloat16* p, bool ok) 
 }
 
 // K split across a cluster: enough CTAs that each warp's share of K is one
-// batch of loads, at most kSkinnyMaxSplit, and only while the grid has fewer
-// CTAs than two per SM (a larger grid already keeps every SM's loads busy).
-inline int skinny_ksplit(int N, int K) {
+// batch of loads, at most kSkinnyMaxSplit, and no more than two CTAs per SM
+// in total — two are resident per SM at the kernel's register use, and a
+// second wave of CTAs costs more than a second batch of loads per warp (the
+// 32-row 1024 x 4096 projection: 9.9 us in two waves of 512 CTAs, 6.9 us in
+// one wave of 256).  The skinny GEMM and the fused tensor-parallel projection
+// share the rule, so they split K alike and give the same bits.
+inline int skinny_ksplit(int N, int K, int sms) {
   const int n_chunks = K / 32;
   const int nblk = (N + 7) / 8;
   int ks = (n_chunks + kSkinnyWarps * kSkinnyBatch - 1) / (kSkinnyWarps * kSkinnyBatch);
   if (ks > kSkinnyMaxSplit) ks = kSkinnyMaxSplit;
+  if (nblk * ks > 2 * sms) ks = (2 * sms) / nblk;
   if (ks < 1) ks = 1;
-  if (nblk >= 2 * 148) ks = 1;
   return ks;
 }
 

@@ -392,7 +392,7 @@ cudaError_t launch_fused_one(cudaStream_t stream, const __nv_bfloat16* A,
                              const float* bias, const float* gamma, const float* beta,
                              __nv_bfloat16* s_out, __nv_bfloat16* y, float eps, int* err_word) {
   auto kern = gemm_allreduce_ln_kernel<kMB, kMaxVec, kTP>;
-  const int ks = skinny_ksplit(d, K);
+  const int ks = skinny_ksplit(d, K, current_sm_count());
   const int grid = (d / 8) * ks;
   return launch_ex(kern, dim3(grid), dim3(kSkinnyWarps * 32), 0, stream, ks, true, A, W, M, d, K,
                    regs, static_cast<char*>(regs.r[rank]), rank, recv_off, block, x, bias, gamma,
