@@ -197,3 +197,51 @@ def test_qkv_projection_into_the_owners_caches_rejects():
     ptrs = [t.data_ptr() for t in c]
     with pytest.raises(NeuroDSLError):
         ops.linear_qkv_cache_peers(A, W, bias, y, ptrs, ptrs, 1, 20, 1, 0, 16)
+
+
+def test_copy_2d_batched_matches_views():
+    """nd_copy_2d_batched over strided 3-D views (the key/value packing of the
+    prompt-sharded prefill: column blocks of a projection into per-rank
+    chunks), element sizes 2 and 4, and a 2-byte-aligned case."""
+    ops = _ops()
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    qkv = torch.randn(40, 3 * 256, device="cuda", generator=gen).bfloat16()
+    src = qkv[:, 256:512].view(40, 4, 64).permute(1, 0, 2)       # [4][40][64], strides (64, 768, 1)
+    dst = torch.zeros(4, 40, 2, 64, device="cuda", dtype=torch.bfloat16)[:, :, 1, :]
+    ops.copy_2d_batched(src, dst)
+    f = torch.randn(3, 17, 33, device="cuda", generator=gen)[:, :, 1:30]   # fp32, odd strides
+    g = torch.zeros(3, 20, 40, device="cuda")[:, 2:19, 5:34]
+    ops.copy_2d_batched(f, g)
+    h = torch.randn(5, 7, 13, device="cuda", generator=gen).bfloat16()[:, :, 1:12]  # 2-byte aligned
+    k = torch.zeros(5, 7, 11, device="cuda", dtype=torch.bfloat16)
+    ops.copy_2d_batched(h, k)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src) and torch.equal(g, f) and torch.equal(k, h)
+    from neurodsl_b200._lib import NeuroDSLError
+    with pytest.raises(NeuroDSLError):        # more than 65535 views
+        ops.copy_2d_batched(torch.zeros(70000, 1, 8, device="cuda"),
+                            torch.zeros(70000, 1, 8, device="cuda"))
+
+
+def test_sm_limit_leaves_results_unchanged():
+    """nd_set_sm_limit caps the persistent GEMM and prefill-attention grids
+    (the SMs left over run a collective beside them); the outputs keep their
+    bits, and a negative cap is refused."""
+    ops = _ops()
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    A = torch.randn(4096, 1024, device="cuda", generator=gen).bfloat16()
+    W = (0.03 * torch.randn(3072, 1024, device="cuda", generator=gen)).bfloat16()
+    b = torch.randn(3072, device="cuda", generator=gen)
+    q, k, v = (torch.randn(2, 4, 700, 64, device="cuda", generator=gen).bfloat16() for _ in range(3))
+    y0 = ops.linear(A, W, b, act="tanh")
+    o0 = ops.flash_attn_fwd(q, k, v, causal=True)[0].clone()
+    for cap in (100, 37, 1):
+        with ops.sm_limit(cap):
+            y = ops.linear(A, W, b, act="tanh")
+            o = ops.flash_attn_fwd(q, k, v, causal=True)[0]
+        torch.cuda.synchronize()
+        assert torch.equal(y, y0) and torch.equal(o, o0), cap
+    assert ops.set_sm_limit(0) == 0
+    from neurodsl_b200._lib import NeuroDSLError
+    with pytest.raises(NeuroDSLError):
+        ops.set_sm_limit(-1)
