@@ -89,27 +89,71 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// 8 bf16 of one sender at value offset v of a receive block: four words,
-// polled until all carry `seq` (bounded by the deadline t0 + timeout; on
-// expiry *ok is cleared and whatever was read is returned).
-__device__ __forceinline__ uint4 poll_words(const char* block_base, size_t v, uint32_t seq,
-                                            uint64_t t0, int* ok) {
-  const char* src = block_base + v * 4;
-  uint64_t w0, w1, w2, w3;
+// Vectors per polling round: kG vectors x kTP senders x four 8-byte words
+// stay within 32 words (64 registers), 16 for the widest rows (whose
+// vectors already hold most of the registers).
+template <int kMaxVec, int kTP>
+__host__ __device__ constexpr int poll_group() {
+  return ((kMaxVec >= 8 ? 4 : 8) / kTP) < 1 ? 1
+         : (((kMaxVec >= 8 ? 4 : 8) / kTP) > kMaxVec ? kMaxVec : ((kMaxVec >= 8 ? 4 : 8) / kTP));
+}
+
+// One row's sum over the senders for the kG vectors starting at i0: every
+// sender's words of those vectors are loaded in one round (all loads in
+// flight together, not one sender and vector after another), re-read until
+// all carry `seq` (bounded by the deadline t0 + timeout; on expiry *ok is
+// cleared and whatever was read is used), then added in rank order into v.
+// `skip` (or -1) is a sender whose values the caller adds itself (the
+// reduction kernel's own partial); its slot in the order is left to it.
+template <int kMaxVec, int kTP, int kG>
+__device__ __forceinline__ void poll_sum(const char* recv, size_t block, size_t off, int lane,
+                                         int nvec, int i0, int skip, uint32_t seq, uint64_t t0,
+                                         int* ok, float (&v)[kMaxVec][8], const uint4* own_vals) {
+  uint64_t w[kG][kTP][4];
   uint32_t it = 0;
   for (;;) {
-    ld_words_sys(src, w0, w1);
-    ld_words_sys(src + 16, w2, w3);
-    if (static_cast<uint32_t>(w0 >> 32) == seq && static_cast<uint32_t>(w1 >> 32) == seq &&
-        static_cast<uint32_t>(w2 >> 32) == seq && static_cast<uint32_t>(w3 >> 32) == seq)
-      break;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const int c = lane + (i0 + g) * 32;
+#pragma unroll
+      for (int p = 0; p < kTP; ++p) {
+        if (c < nvec && p != skip) {
+          const char* src = recv + p * block + (off + c * 8) * 4;
+          ld_words_sys(src, w[g][p][0], w[g][p][1]);
+          ld_words_sys(src + 16, w[g][p][2], w[g][p][3]);
+        }
+      }
+    }
+    bool all = true;
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      const int c = lane + (i0 + g) * 32;
+#pragma unroll
+      for (int p = 0; p < kTP; ++p)
+        if (c < nvec && p != skip)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) all &= static_cast<uint32_t>(w[g][p][k] >> 32) == seq;
+    }
+    if (all) break;
     if ((++it & 63u) == 0 && globaltimer() - t0 > ND_WAIT_TIMEOUT_NS) {
       *ok = 0;
       break;
     }
   }
-  return make_uint4(static_cast<uint32_t>(w0), static_cast<uint32_t>(w1),
-                    static_cast<uint32_t>(w2), static_cast<uint32_t>(w3));
+#pragma unroll
+  for (int g = 0; g < kG; ++g) {
+    const int i = i0 + g, c = lane + i * 32;
+    if (c >= nvec) continue;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+#pragma unroll
+    for (int p = 0; p < kTP; ++p) {
+      const uint4 u = p == skip ? own_vals[g]
+                                : make_uint4(static_cast<uint32_t>(w[g][p][0]), static_cast<uint32_t>(w[g][p][1]),
+                                             static_cast<uint32_t>(w[g][p][2]), static_cast<uint32_t>(w[g][p][3]));
+      bf16x8_add(u, v[i]);
+    }
+  }
 }
 
 // s = x + Σ_p pv[p] + bias in rank order, rounded to bf16 and stored to
@@ -228,26 +272,34 @@ __global__ void __launch_bounds__(256)
   int ok = 1;
   const uint64_t t0 = kTP > 1 ? globaltimer() : 0;
 
-  // 3. sum in rank order from local memory, residual, bias, LayerNorm
+  // 3. sum in rank order from local memory (2. the peers' words of this
+  //    call, polled a group of vectors at a time), residual, bias, LayerNorm
+  constexpr int kG = poll_group<kMaxVec, kTP>();
   for (int row = row0; row < rows; row += row_step) {
     const size_t off = static_cast<size_t>(row) * d;
     float v[kMaxVec][8];
+    uint4 xr[kMaxVec];
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = lane + i * 32;
+      if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
+    }
+#pragma unroll
+    for (int i0 = 0; i0 < kMaxVec; i0 += kG) {
+      uint4 own_vals[kG];
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        const int c = lane + (i0 + g) * 32;
+        own_vals[g] = c < nvec ? ld_cg16(mine_p + (off + c * 8) * 2) : make_uint4(0, 0, 0, 0);
+      }
+      poll_sum<kMaxVec, kTP, kG>(own + recv_off, block, off, lane, nvec, i0, rank, seq, t0, &ok,
+                                 v, own_vals);
+    }
 #pragma unroll
     for (int i = 0; i < kMaxVec; ++i) {
       const int c = lane + i * 32;
       if (c < nvec) {
-        uint4 pv[kTP];
-#pragma unroll
-        for (int p = 0; p < kTP; ++p)
-          pv[p] = p == rank ? ld_cg16(mine_p + (off + c * 8) * 2)
-                            // 2. the peer's words of this call
-                            : poll_words(own + recv_off + p * block, off + c * 8, seq, t0, &ok);
-        const uint4 xr = reinterpret_cast<const uint4*>(x + off)[c];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
-#pragma unroll
-        for (int p = 0; p < kTP; ++p) bf16x8_add(pv[p], v[i]);
-        bf16x8_add(xr, v[i]);
+        bf16x8_add(xr[i], v[i]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] += bs[i][e];
       }
@@ -333,20 +385,23 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32, 2)
   const uint64_t t0 = globaltimer();
   const size_t off = static_cast<size_t>(row) * d;
   float v[kMaxVec][8];
+  uint4 xr[kMaxVec];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = lane + i * 32;
+    if (c < nvec) xr[i] = reinterpret_cast<const uint4*>(x + off)[c];
+  }
+  // every rank's words of this row, a group of vectors per polling round
+  constexpr int kG = poll_group<kMaxVec, kTP>();
+#pragma unroll
+  for (int i0 = 0; i0 < kMaxVec; i0 += kG)
+    poll_sum<kMaxVec, kTP, kG>(own + recv_off, block, off, lane, nvec, i0, -1, seq, t0, &ok, v,
+                               nullptr);
 #pragma unroll
   for (int i = 0; i < kMaxVec; ++i) {
     const int c = lane + i * 32;
     if (c < nvec) {
-      uint4 pv[kTP];
-#pragma unroll
-      for (int p = 0; p < kTP; ++p)
-        pv[p] = poll_words(own + recv_off + p * block, off + c * 8, seq, t0, &ok);
-      const uint4 xr = reinterpret_cast<const uint4*>(x + off)[c];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
-#pragma unroll
-      for (int p = 0; p < kTP; ++p) bf16x8_add(pv[p], v[i]);
-      bf16x8_add(xr, v[i]);
+      bf16x8_add(xr[i], v[i]);
 #pragma unroll
       for (int e = 0; e < 8; ++e) v[i][e] += bias ? __ldg(bias + c * 8 + e) : 0.f;
     }
