@@ -23,19 +23,24 @@ in libneurodsl_b200.so:
   greedy token          nd_argmax on the LM-head logits
 
 Tensor parallelism (Megatron layout): rank r of `tp` holds heads
-[r·H/tp, (r+1)·H/tp) with their Q/K/V rows and output-projection columns,
-MLP columns [r·F/tp, (r+1)·F/tp) of the up projection and the matching
-columns of the down projection, and vocabulary rows [r·V/tp, ...) of the LM
-head.  The output and down projections produce partial sums that are
-all-reduced before the fused residual + LayerNorm — with NCCL, or for decode
-batches of up to `nvlink_rows` rows by one kernel that computes this rank's
-projection tile, pushes it to every rank over NVLink and applies the
-residual and LayerNorm to the sum (neurodsl_b200.comm,
-nd_gemm_allreduce_add_layernorm; nd_allreduce_add_layernorm after a separate
-projection where the fused kernel does not take the shapes); the LM head gives a
-local (max, index) per row that is all-gathered and reduced to the global
-first maximum.  Weights are generated from one seed on every rank and sliced,
-so any `tp` computes the same model.
+[r·H/tp, (r+1)·H/tp) with their Q/K/V rows, output-projection columns and
+decode caches, MLP columns [r·F/tp, (r+1)·F/tp) of the up projection and the
+matching columns of the down projection, and vocabulary rows [r·V/tp, ...)
+of the LM head.  In decode the output and down projections produce partial
+sums that are reduced before the fused residual + LayerNorm — for batches of
+up to `nvlink_rows` rows by one kernel that computes this rank's projection
+tile, pushes it to every rank over NVLink and applies the residual and
+LayerNorm to the sum (neurodsl_b200.comm, nd_gemm_allreduce_add_layernorm;
+nd_allreduce_add_layernorm after a separate projection where the fused
+kernel does not take the shapes), else with NCCL.  The prefill shards the
+prompts instead (prefill_mode "dp", the default when the batch divides by
+tp): each rank runs whole layers with the full weights for its prompts and
+its QKV projection's epilogue writes every head's keys and values into the
+owning rank's cache over NVLink (nd_gemm_qkv_cache_peers); prefill_mode "tp"
+is the Megatron prefill with NCCL all-reduces, overlapped with compute in
+stream groups.  The LM head gives a local (max, index) per row that is
+all-gathered and reduced to the global first maximum.  Weights are generated
+from one seed on every rank and sliced, so any `tp` computes the same model.
 
 Decode steps run with programmatic dependent launch (nd_set_pdl): each
 kernel's weight loads, and the decode attention's cache reads, overlap the
