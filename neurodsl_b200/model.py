@@ -553,25 +553,41 @@ class GPT:
         """One GPU: five launches per layer — residual + LN1 + QKV projection,
         attention, output projection, residual + LN2 + up projection, down
         projection (nd_ln_gemm folds each residual add and LayerNorm into the
-        linear layer after it) — then residual + final LN + LM head, argmax.
+        linear layer after it; above 16 rows the two go as separate launches)
+        — then residual + final LN + LM head, argmax.
         The residual stream alternates between two buffers: each fused launch
         reads one and writes the updated stream to the other, since all its
         CTAs read the old stream while one writes the new."""
         cfg, b = self.cfg, self.buf
         xa, xb = b["xd"], b["xd2"]
         p = pb = None
+
+        def ln_linear(x, W, p, p_bias, gamma, beta, s_out, bias, out, act="none"):
+            # Above 16 rows the residual + LayerNorm goes first in its own
+            # launch (a warp per row) and the projection reads it: every CTA
+            # of the fused form repeats the LayerNorm of all rows, which at 32
+            # rows costs more than the extra launch (24-layer QKV projection:
+            # 11.0 vs 12.5 us).  Same bits either way.
+            if x.shape[0] <= 16:
+                ops.ln_linear(x, W, p=p, p_bias=p_bias, gamma=gamma, beta=beta, eps=cfg.eps,
+                              s_out=s_out, bias=bias, act=act, out=out)
+            elif p is None:
+                ops.layernorm(x, gamma, beta, eps=cfg.eps, out=b["hd"], stats=False)
+                ops.linear(b["hd"], W, bias, act=act, out=out)
+            else:
+                ops.add_layernorm(x, p, p_bias, gamma, beta, cfg.eps, s_out=s_out, out=b["hd"])
+                ops.linear(b["hd"], W, bias, act=act, out=out)
+
         for i, L in enumerate(self.layers):
-            ops.ln_linear(xa, L["w_qkv"], p=p, p_bias=pb, gamma=L["ln1_g"], beta=L["ln1_b"],
-                          eps=cfg.eps, s_out=None if p is None else xb, bias=L["b_qkv"],
-                          out=b["qkvd"])
+            ln_linear(xa, L["w_qkv"], p, pb, L["ln1_g"], L["ln1_b"], None if p is None else xb,
+                      L["b_qkv"], b["qkvd"])
             if p is not None:
                 xa, xb = xb, xa
             ops.kv_decode_attn_qkv(b["qkvd"], self.k_cache[i], self.v_cache[i], Lc,
                                    out=b["ad"].view(B, H, 64), workspace=b["ws"])
             ops.linear(b["ad"], L["w_o"], out=b["pd"])
-            ops.ln_linear(xa, L["w_1"], p=b["pd"], p_bias=L["b_o"], gamma=L["ln2_g"],
-                          beta=L["ln2_b"], eps=cfg.eps, s_out=xb, bias=L["b_1"], act=cfg.act,
-                          out=b["ud"])
+            ln_linear(xa, L["w_1"], b["pd"], L["b_o"], L["ln2_g"], L["ln2_b"], xb, L["b_1"],
+                      b["ud"], act=cfg.act)
             xa, xb = xb, xa
             ops.linear(b["ud"], L["w_2"], out=b["pd"])
             p, pb = b["pd"], L["b_2"]
