@@ -242,38 +242,49 @@ def _gather_vocab(logits, V, tp, group):
 def tp_parity(model, cfg, ids, group, tp, dev, steps=16):
     """Tensor-parallel decoder against the one-GPU model of the same seed on
     the same prompts: logits of the last prompt position (max-abs and
-    relative L2 over the full vocabulary) and the first `steps` greedy tokens
-    of every row.  Collective over the model's group; the one-GPU model runs
+    relative L2 over the full vocabulary), the first `steps` greedy tokens of
+    every row, and — so that a differing token can be told from a near tie —
+    the largest logit difference over the steps before the first differing
+    token and the one-GPU model's top-2 margin of each row where the tokens
+    first differ.  Collective over the model's group; the one-GPU model runs
     on the group's first rank, which returns the result (others None)."""
     import torch
     import torch.distributed as dist
 
     from neurodsl_b200.model import GPT
     model.release_graphs()
-    lg = model.prefill(ids, steps).clone()
+    lgs = [_gather_vocab(model.prefill(ids, steps), cfg.vocab, tp, group)]
     for t in range(steps - 1):
-        model.decode_step(t)
+        lgs.append(_gather_vocab(model.decode_step(t), cfg.vocab, tp, group))
     toks = model.tokens().clone()
-    full = _gather_vocab(lg, cfg.vocab, tp, group)
     out = None
     if dist.get_rank(group) == 0:
         ref = GPT(cfg, seed=0, device=dev)
-        rl = ref.prefill(ids, steps).clone()
+        rls = [ref.prefill(ids, steps).clone()]
         for t in range(steps - 1):
-            ref.decode_step(t)
+            rls.append(ref.decode_step(t).clone())
         rt = ref.tokens().clone()
         torch.cuda.synchronize()
-        diff = (full - rl).abs()
+        full, rl = lgs[0], rls[0]
         eq = (toks == rt)
         first = None
+        margins = []
+        dev_before = 0.0
         if not bool(eq.all()):
             bad = (~eq).nonzero()
             first = int(bad[:, 1].min())
+            for r in bad[bad[:, 1] == first][:, 0].tolist():
+                top2 = torch.topk(rls[first][r], 2).values
+                margins.append(float(top2[0] - top2[1]))
+        for k in range(first if first is not None else steps):
+            dev_before = max(dev_before, float((lgs[k] - rls[k]).abs().max()))
         out = {"reference": "one-GPU model, same seed and prompts",
-               "logits_max_abs": float(diff.max()),
+               "logits_max_abs": float((full - rl).abs().max()),
                "logits_rel_l2": float((full - rl).norm() / rl.norm()),
                "tokens_equal": bool(eq.all()), "tokens_checked": int(eq.numel()),
-               "first_differing_step": first}
+               "first_differing_step": first,
+               "decode_logits_max_abs_before_first_difference": dev_before,
+               "one_gpu_top2_margin_where_first_different": margins}
         del ref
         torch.cuda.empty_cache()
     return out
